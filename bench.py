@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Benchmark of the VQ2 decode hot path on B200 (one JSON line on stdout, rank 0).
+
+Workload (BASELINE config 2 at M = 1, 2 bpw): one decode step of a 24-layer, hidden-2048
+decoder whose linears are VQ-compressed -- per layer q/k/v/o 2048x2048, gate/up 2048->6144,
+down 6144->2048 -- plus lm_head 2048->151936, chained through the public PackedLinear API
+(q/k/v share one rotation of h, o consumes v in place of attention, gate/up share the
+rotation of o, down consumes silu(gate)*up). 169 GEMVs and 97 RHTs per step; ~405 MB of
+compressed weights per step, more than 3x the 126 MB L2, so no L2 flush is needed.
+
+Metric: compressed bytes (indices + fp16 scales + fp16 x + fp16 y per GEMV) per second.
+`value`: the step captured in a CUDA graph, inputs resident in HBM. `e2e`: the same step
+through the public API with the token's hidden state copied from pinned host memory and the
+logits copied back every step. `roofline`: GEMV kernels alone (a graph of the 169 GEMVs on
+pre-rotated inputs), against the measured HBM copy bandwidth.
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own replica of the step
+(the dense decode path does not shard; "replicas only"); value = all ranks' bytes / max time.
+
+--impl reference: the reference's CPU path (gather + einsum GEMV of
+scratch/test_cpu_vq_gemv.py, restated in oracle/cpu_path.py) on the host cores, each step a
+bounded sample (one layer's 7 GEMVs + 1/24 of lm_head's rows).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+HIDDEN, INTER, VOCAB = 2048, 6144, 151936
+METRIC = "VQ GEMV HBM GB/s (compressed bytes)"
+UNIT = "GB/s"
+WORKLOAD = ("config2 decode step: 24 layers x (q,k,v,o 2048x2048; gate,up 2048->6144; down 6144->2048) "
+            "+ lm_head 2048->151936; 2 bpw; M=1")
+
+
+def gemv_bytes(out, n, M=1, bpw3=False):
+    """Algorithmic bytes of one GEMV: indices, fp16 scales, fp16 input rows, fp16 output rows."""
+    return out * (n // 8) * (3 if bpw3 else 2) + 2 * out + 2 * M * n + 2 * M * out
+
+
+def shapes(layers):
+    s = []
+    for _ in range(layers):
+        s += [("q", HIDDEN, HIDDEN), ("k", HIDDEN, HIDDEN), ("v", HIDDEN, HIDDEN), ("o", HIDDEN, HIDDEN),
+              ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]
+    s.append(("lm_head", VOCAB, HIDDEN))
+    return s
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        # nvidia-smi numbering can differ from CUDA's (CUDA_VISIBLE_DEVICES); select by UUID
+        try:
+            u = str(torch.cuda.get_device_properties(device).uuid)
+            self.index = u if u.startswith("GPU-") else f"GPU-{u}"
+        except (AttributeError, RuntimeError):
+            self.index = str(device.index)
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(self.rows[0][2]),
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------- our arm
+class DecodeStack:
+    """The 24-layer dense decode chain over PackedLinear modules (public API)."""
+
+    def __init__(self, layers, device, seed=0):
+        from compressai_b200 import runtime, synth
+        g = torch.Generator(device=device).manual_seed(seed)
+        cbn = synth.random_codebooks(1)
+        self.cbs = {k: torch.from_numpy(v).to(device) for k, v in cbn.items()}
+        tags = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "mlp_in",
+                "up": "mlp_in", "down": "mlp_down", "lm_head": "lm_head"}
+        self.mods = []
+        for name, out, n in shapes(layers):
+            idx = torch.randint(-32768, 32768, (out, n // 8), generator=g, device=device, dtype=torch.int16)
+            scale = (0.02 * torch.exp(0.1 * torch.randn(out, generator=g, device=device))).half()
+            self.mods.append((name, runtime.PackedLinear((out, n), (16,), tags[name], [idx], scale, self.cbs, device)))
+        self.layers = layers
+
+    def __call__(self, h):
+        mods = self.mods
+        for li in range(self.layers):
+            q, k, v, o, gate, up, down = (m for _, m in mods[7 * li: 7 * li + 7])
+            q(h), k(h)
+            a = o(v(h))
+            act = torch.nn.functional.silu(gate(a)) * up(a)
+            h = down(act)
+        return mods[-1][1](h)
+
+    def launches_per_step(self):
+        return 7 * self.layers + 1 + 4 * self.layers + 1   # GEMVs + RHTs
+
+
+def time_graph(graph, steps, stream):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
+def max_over_ranks(t, dist):
+    if dist is None:
+        return t
+    v = torch.tensor([t], dtype=torch.float64, device="cuda")
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return float(v.item())
+
+
+def barrier(dist):
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def cpu_gemv_sample(stack, min_seconds, layer_from=0, lm_rows=None):
+    """Time the reference CPU GEMV path on host copies of one layer (+ lm_head rows)."""
+    from oracle import cpu_path
+    cb = stack.cbs["16"].float().cpu()
+    xs = {}
+    work = []
+    li = layer_from % stack.layers
+    for name, m in stack.mods[7 * li: 7 * li + 7]:
+        work.append((m.idx0.cpu(), m.scale.float().cpu(), m.n))
+    if lm_rows is not None:
+        m = stack.mods[-1][1]
+        r0, r1 = lm_rows
+        work.append((m.idx0[r0:r1].cpu(), m.scale[r0:r1].float().cpu(), m.n))
+    for _, _, n in work:
+        xs[n] = torch.randn(n)
+    nbytes = sum(gemv_bytes(i.shape[0], n) for i, _, n in work)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for i, s, n in work:
+            cpu_path.vq_gemv_cpu_streaming(xs[n], i, cb, s)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return nbytes * reps, el, reps
+
+
+def run_ours(args, dist, rank, world):
+    from compressai_b200 import kernels
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    stack = DecodeStack(args.layers, dev, seed=1234)
+    sh = shapes(args.layers)
+    step_bytes = sum(gemv_bytes(o, n) for _, o, n in sh)
+    stream = torch.cuda.Stream(dev)
+    h_static = torch.randn(1, HIDDEN, device=dev).half()
+    # warm-up eagerly (first-call setup), then capture the step
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            stack(h_static)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        logits_static = stack(h_static)
+    for _ in range(args.warmup):
+        g.replay()
+    barrier(dist)
+    with ClockSampler(dev) as clk:
+        t = time_graph(g, args.steps, stream)
+        barrier(dist)
+        t = max_over_ranks(t, dist)
+
+        # e2e: pinned host input -> device, replay, logits -> pinned host, every step
+        h_host = torch.randn(args.steps + args.warmup, 1, HIDDEN).half().pin_memory()
+        out_host = torch.empty(VOCAB, dtype=torch.float16).pin_memory()
+        for i in range(args.warmup):
+            with torch.cuda.stream(stream):
+                h_static.copy_(h_host[i], non_blocking=True)
+                g.replay()
+                out_host.copy_(logits_static.view(-1), non_blocking=True)
+            stream.synchronize()
+        barrier(dist)
+        t0 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                h_static.copy_(h_host[args.warmup + i], non_blocking=True)
+                g.replay()
+                out_host.copy_(logits_static.view(-1), non_blocking=True)
+            stream.synchronize()
+        ev1.record(stream)
+        ev1.synchronize()
+        t_e2e = max(ev0.elapsed_time(ev1) / 1e3, 0.0)
+        t_e2e_wall = time.perf_counter() - t0
+        barrier(dist)
+        t_e2e = max_over_ranks(max(t_e2e, t_e2e_wall), dist)
+
+        # roofline: GEMV kernels alone on pre-rotated inputs
+        xr = {n: torch.randn(1, n, device=dev) for n in (HIDDEN, INTER)}
+        ys = [torch.empty(1, m.out, device=dev, dtype=torch.float16) for _, m in stack.mods]
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for (_, m), y in zip(stack.mods, ys):
+                kernels.vq_gemv(xr[m.n], m.idx0, stack.cbs["16"], m.scale, y=y, out_dtype=torch.float16)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gg, stream=stream):
+            for (_, m), y in zip(stack.mods, ys):
+                kernels.vq_gemv(xr[m.n], m.idx0, stack.cbs["16"], m.scale, y=y, out_dtype=torch.float16)
+        for _ in range(args.warmup):
+            gg.replay()
+        barrier(dist)
+        t_gemv = max_over_ranks(time_graph(gg, args.steps, stream), dist)
+    clocks = clk.summary()
+
+    peaks = load_peaks()
+    n_gemv = len(sh)
+    per_launch_s = t_gemv / (args.steps * n_gemv)
+    achieved = step_bytes / n_gemv / per_launch_s / 1e9
+    res = {
+        "metric": METRIC, "value": round(world * step_bytes * args.steps / t / 1e9, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (fp16 in/out, int16 indices)",
+        "data": "synthetic: seeded uniform 16-bit indices, fp16 scales ~0.02, N(0,1) fp16 codebook and input",
+        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1, "bpw": 2, "layers": args.layers,
+                   "step_weight_bytes": step_bytes, "l2": "inputs larger than L2 (no flush)",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": round(world * step_bytes * args.steps / t_e2e / 1e9, 2), "unit": UNIT,
+                "h2d_bytes_per_step": HIDDEN * 2, "d2h_bytes_per_step": VOCAB * 2,
+                "ms_per_step": round(t_e2e / args.steps * 1e3, 4)},
+        "roofline": {"bound": "hbm", "kernel": "vq_gemv_kernel", "achieved": round(achieved, 1),
+                     "peak": peaks[0], "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
+                     "peak_source": peaks[1], "traffic": None,
+                     "avg_launch_us": round(per_launch_s * 1e6, 3), "launches_per_step": n_gemv},
+        "gpu_launches": stack.launches_per_step() * args.steps * 2 + n_gemv * args.steps,
+        "clocks": clocks,
+    }
+    return res, stack
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def run_reference(args, rank, world):
+    """Reference CPU path on the host cores; rank 0 only."""
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count())
+    dev = "cuda" if torch.cuda.is_available() else None
+    if dev is None:
+        raise SystemExit("bench.py needs a CUDA device to build the workload")
+    stack = DecodeStack(args.layers, torch.device(dev), seed=1234)
+    rows_per = (VOCAB + args.layers - 1) // args.layers
+    total_b, total_t = 0, 0.0
+    for s in range(args.warmup + args.steps):
+        r0 = (s % args.layers) * rows_per
+        b, t, _ = cpu_gemv_sample(stack, 0.0, layer_from=s, lm_rows=(r0, min(VOCAB, r0 + rows_per)))
+        if s >= args.warmup:
+            total_b += b
+            total_t += t
+    v = round(total_b / total_t / 1e9, 3)
+    return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "data": "synthetic (same seeded workload as our arm)",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": 1, "bpw": 2, "layers": args.layers,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": "per step: one layer's 7 GEMVs + 1/24 of lm_head rows, gather+einsum fp32 "
+                                       "(scratch/test_cpu_vq_gemv.py:53-70)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = tdist
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, rank, world)
+        else:
+            res, stack = run_ours(args, dist, rank, world)
+            if rank == 0 and world == 1:
+                torch.set_num_threads(os.cpu_count())
+                b, t, reps = cpu_gemv_sample(stack, args.cpu_seconds)
+                res["cpu_baseline"] = {"value": round(b / t / 1e9, 3), "unit": UNIT,
+                                       "cores": torch.get_num_threads(), "kind": "port",
+                                       "sample": f"layer 0's 7 GEMVs x{reps} ({t:.1f} s), gather+einsum fp32 "
+                                                 "(scratch/test_cpu_vq_gemv.py:53-70)"}
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

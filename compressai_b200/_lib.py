@@ -1,0 +1,116 @@
+"""ctypes binding of the C-ABI library ``lib/libvq2_b200.so`` (declared in include/vq2_b200.h).
+
+The library is loaded on first use. There is no fallback: if it is missing or fails to load,
+every compute entry point raises. Status codes from the C-ABI are mapped to Python
+exceptions: shape/dtype/alignment/argument errors -> ValueError, launch/timeout -> RuntimeError.
+"""
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("VQ2_B200_LIB", os.path.join(_HERE, "lib", "libvq2_b200.so"))
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "vq2_b200.h")
+
+VQ2_OK, VQ2_ERR_SHAPE, VQ2_ERR_DTYPE, VQ2_ERR_ALIGN, VQ2_ERR_LAUNCH, VQ2_ERR_TIMEOUT, VQ2_ERR_ARG = range(7)
+VQ2_F16, VQ2_BF16, VQ2_F32 = 0, 1, 2
+
+_DTYPE_CODE = {torch.float16: VQ2_F16, torch.bfloat16: VQ2_BF16, torch.float32: VQ2_F32}
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+
+# name -> argtypes (restype is int unless stated); must match include/vq2_b200.h
+SIGNATURES = {
+    "vq2_abi_version": [],
+    "vq2_status_string": [_i32],
+    "vq2_last_cuda_error": [],
+    "vq2_rht": [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _f32, _i32, _p, _i64, _p],
+    "vq2_swiglu_rht": [_p, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _i64, _p],
+    "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p],
+    "vq2_moe_gemv": [_p, _i32, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _f32, _p],
+    "vq2_moe_combine": [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p],
+}
+ABI_VERSION = 1
+
+_lib = None
+_lock = threading.Lock()
+
+
+class VQ2Error(RuntimeError):
+    pass
+
+
+def load():
+    """Load the library once (thread-safe) and bind every declared symbol."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise VQ2Error(f"compressai_b200 CUDA library not built: {LIB_PATH} is missing "
+                           "(run `python -m compressai_b200.build`); there is no CPU fallback")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_char_p if name == "vq2_status_string" else ctypes.c_int
+        if lib.vq2_abi_version() != ABI_VERSION:
+            raise VQ2Error(f"ABI version mismatch: library {lib.vq2_abi_version()}, python {ABI_VERSION}")
+        _lib = lib
+    return _lib
+
+
+def available():
+    """True when the CUDA library exists and loads (the reference's HAVE_TRITON role)."""
+    try:
+        load()
+        return True
+    except (OSError, VQ2Error):
+        return False
+
+
+def check(status, what):
+    if status == VQ2_OK:
+        return
+    lib = load()
+    msg = f"{what}: {lib.vq2_status_string(status).decode()} (status {status})"
+    if status in (VQ2_ERR_SHAPE, VQ2_ERR_DTYPE, VQ2_ERR_ALIGN, VQ2_ERR_ARG):
+        raise ValueError(msg)
+    if status == VQ2_ERR_LAUNCH:
+        msg += f", cudaError {lib.vq2_last_cuda_error()}"
+    raise VQ2Error(msg)
+
+
+def call(name, *args):
+    """Call a C-ABI entry point and raise on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
+
+
+def dtype_code(t):
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    """The product path is CUDA-only: CPU tensors are an error, not a fallback."""
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("compressai_b200 kernels take CUDA tensors only (no CPU fallback); "
+                             f"got a tensor on {t.device}")

@@ -1,0 +1,26 @@
+// C-ABI bookkeeping: version, status strings, last CUDA error.
+#include <atomic>
+
+#include "common.cuh"
+
+namespace vq2 {
+static std::atomic<int> g_last_cuda_error{0};
+void set_last_cuda_error(cudaError_t e) { g_last_cuda_error.store(static_cast<int>(e)); }
+}  // namespace vq2
+
+extern "C" int vq2_abi_version(void) { return 1; }
+
+extern "C" int vq2_last_cuda_error(void) { return vq2::g_last_cuda_error.load(); }
+
+extern "C" const char* vq2_status_string(int status) {
+  switch (status) {
+    case VQ2_OK: return "ok";
+    case VQ2_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case VQ2_ERR_DTYPE: return "unsupported dtype";
+    case VQ2_ERR_ALIGN: return "misaligned pointer or stride";
+    case VQ2_ERR_LAUNCH: return "CUDA launch/runtime error";
+    case VQ2_ERR_TIMEOUT: return "device-side wait timed out";
+    case VQ2_ERR_ARG: return "null pointer or bad argument";
+    default: return "unknown status";
+  }
+}

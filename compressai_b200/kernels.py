@@ -1,0 +1,158 @@
+"""Kernel entry points with the signatures of reference ``vq2/kernels.py``, backed by the sm_100a
+C-ABI library (no Triton, no CPU fallback).
+
+Reference-compatible functions (same argument order and meaning):
+  vq_gemv_16(xr, i0, cb0, scale, out, n, rs=1.0) -> y[out]               (kernels.py:224-230)
+  vq_gemv_16_8(xr, i0, i1, cb0, cb1, scale, out, n, rs=1.0) -> y[out]    (kernels.py:215-221)
+  vq_moe_parallel_gate_up(xr, topk_ids, gate_up_idx, cb16, gate_up_scale, y_out,
+                          OUT=1024, NG=256, rs=1.0)                      (kernels.py:246-254)
+  vq_moe_parallel_down(act_r, topk_ids, down_idx, cb16, down_scale, y_out,
+                       OUT=2048, NG=64, rs=1.0)                          (kernels.py:256-264)
+Differences: the output dtype is the codebook's dtype (the reference always returns bf16,
+because its codebooks are bf16); xr may be fp32/fp16/bf16; any number of leading rows of xr
+is accepted by the dense GEMVs (the reference's Triton path is batch-1 only).
+
+Extra entry points used by the runtime: ``vq_gemv`` (batched, any output dtype),
+``moe_gemv``, ``swiglu_rht`` and ``moe_combine``.
+"""
+import torch
+
+from . import _lib
+
+HAVE_TRITON = _lib.available()   # name kept for importers: "fused GPU kernels available"
+HAVE_CUDA_KERNELS = HAVE_TRITON
+FUSED_KERNELS_ENABLED = True
+
+
+def set_fused_kernels_enabled(enabled: bool):
+    """Kept for API compatibility (vq2/kernels.py:16-20); the CUDA kernels are always used."""
+    global FUSED_KERNELS_ENABLED
+    FUSED_KERNELS_ENABLED = bool(enabled)
+
+
+def _check_vals(*ts):
+    dt = ts[0].dtype
+    if dt not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"codebook/scale dtype must be float16 or bfloat16, got {dt}")
+    for t in ts[1:]:
+        if t is not None and t.dtype != dt:
+            raise ValueError(f"codebooks and scales must share one dtype ({dt} vs {t.dtype})")
+
+
+def _c(t):
+    return t if t is None or t.is_contiguous() else t.contiguous()
+
+
+def vq_gemv(xr, i0, cb0, scale, i1=None, cb1=None, rs=1.0, out_dtype=None, y=None):
+    """y[..., out] = rs * scale * sum_g (cb0[i0] (+cb1[i1])) . xr  for pre-rotated xr [..., n].
+
+    fp32 accumulation; ``out_dtype`` defaults to the codebook dtype."""
+    _lib.require_cuda(xr, i0, i1, cb0, cb1, scale)
+    if i0.dtype != torch.int16 or (i1 is not None and i1.dtype != torch.uint8):
+        raise ValueError("indices must be int16 (stage 1) and uint8 (residual)")
+    _check_vals(cb0, cb1, scale)
+    out, ng = i0.shape
+    n = ng * 8
+    if xr.shape[-1] != n:
+        raise ValueError(f"xr last dim {xr.shape[-1]} != n={n}")
+    x2 = xr.reshape(-1, n)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    out_dtype = out_dtype or cb0.dtype
+    if y is None:
+        y = torch.empty(*xr.shape[:-1], out, dtype=out_dtype, device=xr.device)
+    elif y.dtype != out_dtype or not y.is_contiguous():
+        raise ValueError("y must be contiguous with dtype out_dtype")
+    i0, i1, cb0, cb1, scale = _c(i0), _c(i1), _c(cb0), _c(cb1), _c(scale)
+    _lib.call("vq2_gemv", _lib.ptr(x2), _lib.dtype_code(x2), M, x2.stride(0), _lib.ptr(i0), _lib.ptr(i1),
+              _lib.ptr(cb0), _lib.ptr(cb1), _lib.ptr(scale), _lib.dtype_code(cb0), _lib.ptr(y),
+              _lib.dtype_code(y), out, out, n, float(rs), _lib.stream_ptr(xr.device))
+    return y
+
+
+def vq_gemv_16_8(xr, i0, i1, cb0, cb1, scale, out, n, rs=1.0):
+    """3 bpw GEMV (stage-16 + residual-8 codebooks) -- vq2/kernels.py:215-221."""
+    if i0.shape != (out, n // 8):
+        raise ValueError(f"i0 shape {tuple(i0.shape)} != ({out}, {n // 8})")
+    return vq_gemv(xr.reshape(-1, n), i0, cb0, scale, i1=i1, cb1=cb1, rs=rs).reshape(*xr.shape[:-1], out)
+
+
+def vq_gemv_16(xr, i0, cb0, scale, out, n, rs=1.0):
+    """2 bpw GEMV -- vq2/kernels.py:224-230."""
+    if i0.shape != (out, n // 8):
+        raise ValueError(f"i0 shape {tuple(i0.shape)} != ({out}, {n // 8})")
+    return vq_gemv(xr.reshape(-1, n), i0, cb0, scale, rs=rs).reshape(*xr.shape[:-1], out)
+
+
+def _ids32(ids):
+    ids = ids.reshape(-1)
+    if ids.dtype != torch.int32:
+        ids = ids.to(torch.int32)
+    return ids.contiguous()
+
+
+def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.0):
+    """Expert-indexed GEMV: y[k] = rs * scale[e_k] * sum cb16[idx[e_k]] . x[k // x_k_div]."""
+    _lib.require_cuda(x, ids, pool_idx, cb16, pool_scale, y)
+    if pool_idx.dtype != torch.int16 or pool_idx.dim() != 3:
+        raise ValueError("pool_idx must be int16 [E, OUT, NG]")
+    _check_vals(cb16, pool_scale)
+    E, OUT, NG = pool_idx.shape
+    ids = _ids32(ids)
+    K = ids.numel()
+    if y.shape[0] < K or y.numel() < K * OUT or not y.is_contiguous():
+        raise ValueError(f"y must be contiguous with at least [{K}, {OUT}] elements")
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    pool_idx, pool_scale = _c(pool_idx), _c(pool_scale)
+    if pool_scale.numel() != E * OUT:
+        raise ValueError("pool_scale must be [E, OUT]")
+    _lib.call("vq2_moe_gemv", _lib.ptr(x), _lib.dtype_code(x), int(x_k_stride), int(x_k_div), _lib.ptr(ids), K, E,
+              _lib.ptr(pool_idx), _lib.ptr(cb16), _lib.ptr(pool_scale), _lib.dtype_code(cb16), _lib.ptr(y),
+              _lib.dtype_code(y), OUT, NG, float(rs), _lib.stream_ptr(x.device))
+    return y
+
+
+def vq_moe_parallel_gate_up(xr, topk_ids, gate_up_idx, cb16, gate_up_scale, y_out, OUT=1024, NG=256, rs=1.0):
+    """Gate+up projections of the K active experts on one shared activation -- vq2/kernels.py:246-254."""
+    if gate_up_idx.shape[1:] != (OUT, NG):
+        raise ValueError("gate_up_idx must be [E, OUT, NG]")
+    moe_gemv(xr.reshape(-1), topk_ids, gate_up_idx, cb16, gate_up_scale, y_out, x_k_stride=0, rs=rs)
+
+
+def vq_moe_parallel_down(act_r, topk_ids, down_idx, cb16, down_scale, y_out, OUT=2048, NG=64, rs=1.0):
+    """Down projections, expert k on its own activation row act_r[k] -- vq2/kernels.py:256-264."""
+    if down_idx.shape[1:] != (OUT, NG):
+        raise ValueError("down_idx must be [E, OUT, NG]")
+    moe_gemv(act_r.contiguous(), topk_ids, down_idx, cb16, down_scale, y_out, x_k_stride=NG * 8, rs=rs)
+
+
+def swiglu_rht(gu, rot, out=None):
+    """act = silu(gu[:, :I]) * gu[:, I:], then rot.fwd(act), all fp32. gu: fp32 [M, 2I]."""
+    _lib.require_cuda(gu)
+    if gu.dtype != torch.float32 or gu.dim() != 2 or gu.shape[1] != 2 * rot.n or gu.stride(1) != 1:
+        raise ValueError("gu must be fp32 [M, 2n] with unit inner stride")
+    M = gu.shape[0]
+    if out is None:
+        out = torch.empty(M, rot.n, dtype=torch.float32, device=gu.device)
+    _lib.call("vq2_swiglu_rht", _lib.ptr(gu), gu.stride(0), M, rot.n, rot.hb, _lib.ptr(rot.perm),
+              _lib.ptr(rot.sign), float(rot.scale), _lib.ptr(out), out.stride(0), _lib.stream_ptr(gu.device))
+    return out
+
+
+def moe_combine(y, w, top_k, add=None, out=None, out_dtype=torch.float16):
+    """out[t] = sum_j w[t, j] * y[t*top_k + j] (+ add[t]); y fp32 [T*top_k, H], w fp32 [T, top_k]."""
+    _lib.require_cuda(y, w, add)
+    if y.dtype != torch.float32 or w.dtype != torch.float32 or (add is not None and add.dtype != torch.float32):
+        raise ValueError("moe_combine takes fp32 y, w and add")
+    T = w.shape[0]
+    H = y.shape[-1]
+    if y.numel() != T * top_k * H:
+        raise ValueError("y must be [T*top_k, H]")
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=y.device)
+    y, w, add = _c(y), _c(w), _c(add)   # keep references alive across the launch
+    _lib.call("vq2_moe_combine", _lib.ptr(y), _lib.ptr(w), T, top_k, H, _lib.ptr(add), _lib.ptr(out),
+              _lib.dtype_code(out), _lib.stream_ptr(y.device))
+    return out

@@ -1,0 +1,232 @@
+"""Compressed-weight decode runtime, mirroring reference ``vq2/runtime.py``.
+
+``PackedLinear`` is a drop-in ``nn.Linear`` whose weight stays VQ-compressed in HBM. Its
+forward rotates the input once with the fp32 RHT kernel (cached per input tensor, like
+the reference's ``FastRot``) and runs the codebook-decode GEMV kernel for any number of rows
+M (the reference's fused path is batch-1 only, vq2/runtime.py:92; larger M fall back to
+dequantize-then-matmul there, :105-110). Scales and codebooks stay in their container dtype
+(fp16); the output takes the input's dtype.
+"""
+import os
+
+import numpy as np
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import kernels
+from . import vq
+
+RS = vq.HB ** -0.5   # the unnormalised-rotation scale folded into legacy GEMV calls (vq2/runtime.py:66)
+
+
+def _as_index(a, bits):
+    """Stored indices -> int32 codebook rows (vq2/runtime.py:32-35)."""
+    a = a.to(torch.int32)
+    return a & 0xFFFF if bits > 8 else a
+
+
+class _RotCache:
+    """Last (input tensor, version) -> fp32 rotation, shared by all modules with the same Rot."""
+
+    def __init__(self):
+        self.x = None
+        self.ver = -1
+        self.y = None
+
+
+_CACHES = {}
+
+
+def rotate_cached(rot, x, unnormalised=False):
+    key = (id(rot), unnormalised)
+    c = _CACHES.get(key)
+    if c is None:
+        c = _CACHES[key] = _RotCache()
+    if c.x is x and c.ver == x._version:
+        return c.y
+    y = rot.fwd_f32(x, unnormalised=unnormalised)
+    c.x, c.ver, c.y = x, x._version, y
+    return y
+
+
+class FastRot:
+    """Decode rotation: permutation + signs + UNnormalised Hadamard; the hb^-0.5 goes into the
+    GEMV's rs. The result is reused while the same tensor (identity and version) comes back
+    (vq2/runtime.py:37-63). Returns fp32 (the reference returns bf16)."""
+    _ALL = {}
+
+    def __init__(self, rot, device):
+        self.rot = rot
+        self.perm = rot.perm
+        self.sign = rot.sign
+        self.nb = rot.nb
+
+    @classmethod
+    def get(cls, tag, n, device, rot):
+        k = (tag, n, str(device))
+        if k not in cls._ALL:
+            cls._ALL[k] = cls(rot, device)
+        return cls._ALL[k]
+
+    def __call__(self, x):
+        return rotate_cached(self.rot, x.reshape(-1), unnormalised=True)
+
+
+class PackedLinear(nn.Module):
+    """nn.Linear replacement over VQ indices (vq2/runtime.py:70-113).
+
+    shape=(out, n); cfg=(16,) (2 bpw) or (16, 8) (3 bpw); idx: list of index tensors per stage
+    ([out, n/8] int16, uint8); scale: [out]; cbs: dict {"16": [65536, 8], "16_8": [256, 8]}
+    in fp16 (or bf16) on the device, shared between modules."""
+
+    def __init__(self, shape, cfg, tag, idx, scale, cbs, device):
+        super().__init__()
+        self.out, self.n = shape
+        self.cfg, self.tag = tuple(cfg), tag
+        if self.cfg not in ((16,), (16, 8)):
+            raise ValueError(f"unsupported cfg {cfg}: the decode kernels take (16,) or (16, 8)")
+        self.keys = [vq.cfg_key(self.cfg, i) for i in range(len(self.cfg))]
+        cb_dtype = cbs[self.keys[0]].dtype
+        for i, a in enumerate(idx):
+            a = torch.as_tensor(a)
+            a = a.to(torch.int16) if i == 0 else a.to(torch.uint8)
+            self.register_buffer(f"idx{i}", a.to(device).contiguous(), persistent=False)
+        self.register_buffer("scale", torch.as_tensor(scale).to(device=device, dtype=cb_dtype).contiguous(),
+                             persistent=False)
+        self._cbs = [cbs]
+        self.rot = vq.get_rot(tag, self.n, device)
+
+    def weight_rows(self, r0, r1):
+        """Rotated-space rows [r0, r1) in the codebook dtype (vq2/runtime.py:82-89)."""
+        rec = None
+        for i, k in enumerate(self.keys):
+            ix = _as_index(getattr(self, f"idx{i}")[r0:r1], self.cfg[i])
+            g = F.embedding(ix, self._cbs[0][k])
+            rec = g if rec is None else rec + g
+        return rec.reshape(r1 - r0, self.n) * self.scale[r0:r1, None]
+
+    def forward(self, x):
+        xr = rotate_cached(self.rot, x)
+        cbs = self._cbs[0]
+        out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float16
+        if self.cfg == (16, 8):
+            return kernels.vq_gemv(xr, self.idx0, cbs[self.keys[0]], self.scale, i1=self.idx1,
+                                   cb1=cbs[self.keys[1]], out_dtype=out_dtype)
+        return kernels.vq_gemv(xr, self.idx0, cbs[self.keys[0]], self.scale, out_dtype=out_dtype)
+
+    def nbytes(self):
+        return sum(b.numel() * b.element_size() for b in self.buffers())
+
+
+class PackedEmbedding(nn.Module):
+    """Row lookup of a compressed embedding: gather the token rows, decode them in fp32 and
+    inverse-rotate (vq2/runtime.py:116-133)."""
+
+    def __init__(self, lin, cbs32):
+        super().__init__()
+        self.lin = lin
+        self._cb32 = [cbs32]
+
+    def forward(self, ids):
+        flat = ids.reshape(-1)
+        rec = None
+        for i, k in enumerate(self.lin.keys):
+            ix = _as_index(getattr(self.lin, f"idx{i}")[flat], self.lin.cfg[i])
+            g = F.embedding(ix, self._cb32[0][k])
+            rec = g if rec is None else rec + g
+        q = rec.reshape(flat.numel(), self.lin.n) * self.lin.scale[flat].float()[:, None]
+        w = self.lin.rot.inv_f32(q)
+        return w.to(torch.bfloat16).reshape(*ids.shape, self.lin.n)
+
+
+class PackedLMHead(nn.Module):
+    """lm_head tied to the embedding: shares its compressed indices (vq2/runtime.py:136-144)."""
+
+    def __init__(self, lin):
+        super().__init__()
+        self.lin = lin
+
+    def forward(self, x):
+        return self.lin(x)
+
+
+# --------------------------------------------------------------------------------------------
+# containers
+# --------------------------------------------------------------------------------------------
+def unpack_fixed(buf, bits, n):
+    """Fixed-width index unpacking, 16/8/4/12 bits (vq2/export.py:56-70)."""
+    buf = np.asarray(buf)
+    if bits == 16:
+        return buf.view(np.uint16)[:n].astype(np.int64)
+    if bits == 8:
+        return buf[:n].astype(np.int64)
+    if bits == 4:
+        b = buf.astype(np.uint32)
+        out = np.empty(len(b) * 2, dtype=np.int64)
+        out[0::2] = b & 15
+        out[1::2] = b >> 4
+        return out[:n]
+    if bits == 12:
+        b = buf.reshape(-1, 3).astype(np.uint32)
+        w = b[:, 0] | (b[:, 1] << 8) | (b[:, 2] << 16)
+        out = np.empty(len(w) * 2, dtype=np.int64)
+        out[0::2] = w & 4095
+        out[1::2] = w >> 12
+        return out[:n]
+    raise ValueError(bits)
+
+
+def decode_indices(C):
+    """Container dict -> {name: [index tensor per stage]} (vq2/runtime.py:155-182). Fixed-width
+    streams are unpacked here; ANS streams (coded with the third-party `constriction` package)
+    cannot be decoded without it and raise."""
+    idx = {nm: [None] * len(C["meta"][nm]["cfg"]) for nm in C["names"]}
+    for key, e in C["streams"].items():
+        bits = e["bits"]
+        n = int(sum(e["sizes"]))
+        if e["mode"] == "ans":
+            raise NotImplementedError("ANS-coded .vq2 streams need `constriction`, which is not installed; "
+                                      "convert to .vq2r (raw indices) first")
+        fx = e["fixed"].numpy() if isinstance(e["fixed"], torch.Tensor) else e["fixed"]
+        sym = unpack_fixed(fx, bits, n)
+        arr = sym.astype(np.uint8) if bits <= 8 else sym.astype(np.uint16).view(np.int16)
+        t_all = torch.from_numpy(np.ascontiguousarray(arr))
+        owners = [nm for nm in C["names"]
+                  if key in [vq.cfg_key(C["meta"][nm]["cfg"], i) for i in range(len(C["meta"][nm]["cfg"]))]]
+        off = 0
+        for nm, sz in zip(owners, e["sizes"]):
+            cfg_ = C["meta"][nm]["cfg"]
+            i = [vq.cfg_key(cfg_, j) for j in range(len(cfg_))].index(key)
+            idx[nm][i] = t_all[off:off + sz].view(C["meta"][nm]["shape"][0], -1).clone()
+            off += sz
+    return idx
+
+
+def read_container(path):
+    """Read a .vq2 (fixed-width streams) or .vq2r (raw indices) dict (vq2/runtime.py:185-193)."""
+    C = torch.load(path, weights_only=False)
+    if C.get("format") == "vq2r":
+        return C
+    idx = decode_indices(C)
+    scales = {nm: (s if isinstance(s, torch.Tensor) else torch.from_numpy(s)) for nm, s in C["scales"].items()}
+    return dict(format="vq2r", names=C["names"], meta=C["meta"], idx=idx, scales=scales,
+                codebooks=C["codebooks"], codebooks_embed=C.get("codebooks_embed", C["codebooks"]),
+                dense=C.get("dense", {}))
+
+
+def convert_to_runtime(src, dst):
+    """Decode once and save raw indices (vq2/runtime.py:196-200)."""
+    torch.save(read_container(src), dst)
+    return os.path.getsize(dst)
+
+
+def build_packed_linears(C, device, cb_dtype=torch.float16):
+    """{name: PackedLinear} for every quantized matrix of a container dict (the module
+    construction loop of vq2/runtime.py:231-241, without the HF model around it)."""
+    cbs = {k: v.to(device=device, dtype=cb_dtype).contiguous() for k, v in C["codebooks"].items()}
+    mods = {}
+    for nm in C["names"]:
+        m = C["meta"][nm]
+        mods[nm] = PackedLinear(m["shape"], m["cfg"], m["tag"], C["idx"][nm], C["scales"][nm], cbs, device)
+    return mods

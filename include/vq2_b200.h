@@ -1,0 +1,131 @@
+/*
+ * vq2_b200.h -- C-ABI of the B200-native (sm_100a) VQ2 decode hot path.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no framework types. Every
+ * entry point:
+ *   - takes DEVICE pointers (except where stated) and enqueues its work on `stream`
+ *     (NULL = legacy default stream); it never synchronizes and never allocates;
+ *   - returns a status code (VQ2_OK = 0); on VQ2_ERR_LAUNCH the CUDA error code is kept
+ *     for vq2_last_cuda_error();
+ *   - is safe to capture in a CUDA graph.
+ *
+ * Index tensors hold the reference container layout: 16-bit stage indices are int16 holding
+ * uint16 bits (masked with 0xFFFF, reference vq2/kernels.py:47,72), the optional residual
+ * stage is uint8, both row-major [out, n/8]; one index selects an 8-dim codebook row.
+ * Codebooks are [K, 8] and scales [out], both in the "value" dtype (fp16 or bf16).
+ *
+ * Reference citations are paths inside Unoalss/CompressAI.
+ */
+#ifndef VQ2_B200_H
+#define VQ2_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VQ2_API __attribute__((visibility("default")))
+#else
+#define VQ2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define VQ2_OK 0
+#define VQ2_ERR_SHAPE 1    /* unsupported or inconsistent dimensions */
+#define VQ2_ERR_DTYPE 2    /* unsupported dtype code */
+#define VQ2_ERR_ALIGN 3    /* a pointer or stride breaks the required alignment */
+#define VQ2_ERR_LAUNCH 4   /* CUDA launch/runtime error (see vq2_last_cuda_error) */
+#define VQ2_ERR_TIMEOUT 5  /* a bounded device-side wait gave up */
+#define VQ2_ERR_ARG 6      /* null pointer or out-of-range argument */
+
+/* dtype codes */
+#define VQ2_F16 0
+#define VQ2_BF16 1
+#define VQ2_F32 2
+
+/* ABI version of this header (bumped on any signature change). */
+VQ2_API int vq2_abi_version(void);
+/* Static description of a status code. */
+VQ2_API const char* vq2_status_string(int status);
+/* cudaError_t of the most recent VQ2_ERR_LAUNCH (0 if none). */
+VQ2_API int vq2_last_cuda_error(void);
+
+/*
+ * Randomized Hadamard transform, forward (inverse = 0):
+ *   xr[m, b*hb + j] = out_scale * sum_i H[j, i] * x[m, perm[b*hb + i]] * sign[b*hb + i]
+ * and inverse (inverse = 1), the transpose map:
+ *   xr[m, perm[b*hb + j]] = out_scale * sign[b*hb + j] * sum_i H[j, i] * x[m, b*hb + i]
+ * for every row m < M and block b < n/hb, H the Sylvester Hadamard matrix of order hb.
+ * out_scale = hb^-0.5 gives Rot.fwd / Rot.inv; out_scale = 1 gives FastRot's unnormalised
+ * variant. x: [M, n] (x_dtype, row stride x_row_stride elements); perm: int32 [n], a
+ * permutation of 0..n-1; sign: int8 [n] of +-1; xr: fp32 [M, n] (row stride xr_row_stride),
+ * must not alias x. hb a power of two in [64, 2048].
+ * Replaces: Rot.fwd / Rot._orig_fwd / Rot.inv (vq2/vq.py:66-87) and FastRot.__call__
+ * (vq2/runtime.py:57-63).
+ */
+VQ2_API int vq2_rht(const void* x, int x_dtype, int64_t x_row_stride, int64_t M, int64_t n,
+                    int64_t hb, const int32_t* perm, const int8_t* sign, float out_scale,
+                    int inverse, float* xr, int64_t xr_row_stride, void* stream);
+
+/*
+ * SwiGLU activation fused with the forward RHT of its result:
+ *   act[m, j] = silu(gu[m, j]) * gu[m, I + j]      (j < I, fp32 math)
+ *   xr[m, :]  = RHT_forward(act[m, :])              (as vq2_rht with inverse = 0)
+ * gu: fp32 [M, 2I] (row stride gu_row_stride); xr: fp32 [M, I]. I = n is the RHT length.
+ * Replaces: the torch ops `silu(gate.float()) * up.float()` and `rot_512.fwd(act)` of
+ * PagedMoEExpert.forward (vq2/paged_runtime.py:501-504).
+ */
+VQ2_API int vq2_swiglu_rht(const float* gu, int64_t gu_row_stride, int64_t M, int64_t n,
+                           int64_t hb, const int32_t* perm, const int8_t* sign, float out_scale,
+                           float* xr, int64_t xr_row_stride, void* stream);
+
+/*
+ * VQ GEMV on a pre-rotated activation (fp32 accumulation):
+ *   y[m, r] = rs * scale[r] * sum_g dot(cb0[idx0[r, g]] (+ cb1[idx1[r, g]]), xr[m, 8g:8g+8])
+ * xr: [M, n] in x_dtype (row stride x_row_stride); idx0: int16 [out, n/8]; idx1: uint8
+ * [out, n/8] or NULL (2 bpw); cb0: [65536, 8]; cb1: [256, 8] or NULL; scale: [out], all
+ * three in val_dtype (fp16/bf16); y: [M, out] in y_dtype (row stride y_row_stride).
+ * n % 64 == 0; idx0, cb0, cb1 16-byte aligned, idx1 8-byte aligned.
+ * Replaces: vq_gemv_16 / vq_gemv_16_8 (vq2/kernels.py:215-230) and the Triton kernels
+ * _vq_gemv_16 / _vq_gemv_16_8 (vq2/kernels.py:32-78), which handle M = 1 only.
+ */
+VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_stride,
+                     const int16_t* idx0, const uint8_t* idx1, const void* cb0, const void* cb1,
+                     const void* scale, int val_dtype, void* y, int y_dtype, int64_t y_row_stride,
+                     int64_t out, int64_t n, float rs, void* stream);
+
+/*
+ * Expert-indexed VQ GEMV over K problems (2 bpw):
+ *   y[k, r] = rs * scale[e_k, r] * sum_g dot(cb0[idx[e_k, r, g]], x_k[8g:8g+8])
+ *   e_k = e_ids[k],  x_k = x + (k / x_k_div) * x_k_stride
+ * x_k_stride = 0 shares one activation among all problems (gate_up of one token);
+ * x_k_div = top_k maps problem t*top_k + j to token t. e_ids: int32 [K] device (slots of a
+ * paged pool or ids of a resident pool; ids outside [0, num_experts) give zero rows).
+ * idx: int16 [num_experts, out, ng]; scale: [num_experts, out] in val_dtype; y: [K, out] in
+ * y_dtype. ng % 8 == 0; idx and cb0 16-byte aligned.
+ * Replaces: vq_moe_parallel_gate_up / vq_moe_parallel_down (vq2/kernels.py:246-264) and
+ * _parallel_moe_gate_up_kernel / _parallel_moe_down_kernel (vq2/kernels.py:117-176).
+ */
+VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int64_t x_k_stride, int64_t x_k_div,
+                         const int32_t* e_ids, int64_t K, int64_t num_experts, const int16_t* idx,
+                         const void* cb0, const void* scale, int val_dtype, void* y, int y_dtype,
+                         int64_t out, int64_t ng, float rs, void* stream);
+
+/*
+ * Routing-weighted combine of per-(token, expert) rows:
+ *   out[t, :] = sum_{j < top_k} w[t, j] * y[t * top_k + j, :]  (+ add[t, :] if add != NULL)
+ * in fixed j order, fp32 math. y: fp32 [T*top_k, H]; w: fp32 [T, top_k]; add: fp32 [T, H]
+ * or NULL; out: [T, H] in out_dtype.
+ * Replaces: `(y_down * topk_w[:, None]).sum(0)` of PagedMoEExpert.forward
+ * (vq2/paged_runtime.py:510) and the shared-expert add of Qwen3_5MoeSparseMoeBlock.
+ */
+VQ2_API int vq2_moe_combine(const float* y, const float* w, int64_t T, int64_t top_k,
+                            int64_t H, const float* add, void* out, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VQ2_B200_H */

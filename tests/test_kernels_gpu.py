@@ -1,0 +1,204 @@
+"""CUDA kernels vs the CPU oracle (oracle/vq2_oracle.py), through the C-ABI.
+
+Tolerances: fp32 RHT vs the fp64 oracle 1e-5 relative to max|ref|; GEMV outputs in fp16
+max|y - ref| / max|ref| <= 1e-3; bf16 outputs 4e-3 (bf16 rounding
+alone is 2^-9 of |y|).
+"""
+import numpy as np
+import pytest
+import torch
+
+from compressai_b200 import kernels, synth, vq
+from oracle import vq2_oracle as O
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL_F16 = 1e-3
+TOL_BF16 = 4e-3
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30)
+
+
+@pytest.fixture(scope="module")
+def cbs():
+    try:
+        d = golden("codebooks.npz")
+        return {"16": d["cb16"], "16_8": d["cb16_8"]}
+    except pytest.skip.Exception:
+        return synth.random_codebooks(1)
+
+
+def dev_cbs(cbs, dtype=torch.float16):
+    return {k: torch.from_numpy(v.astype(np.float32)).to(DEV, dtype).contiguous() for k, v in cbs.items()}
+
+
+# ------------------------------------------------------------------------------------------ RHT
+@pytest.mark.parametrize("tag,n", [("dense_q", 2048), ("moe_expert_512", 512), ("mlp_down", 6144),
+                                   ("small_1024", 1024), ("t64", 64), ("t128", 128), ("t256", 256)])
+@pytest.mark.parametrize("M", [1, 3, 17])
+def test_rht_forward_inverse(tag, n, M):
+    rot = vq.get_rot(tag, n, DEV)
+    perm, sign, hb = O.rot_params(tag, n)
+    assert np.array_equal(rot.perm_cpu.numpy(), perm)
+    x = torch.randn(M, n, generator=torch.Generator().manual_seed(n + M))
+    y = rot.fwd_f32(x.to(DEV)).cpu().numpy()
+    ref = O.rht_fwd(x.numpy(), perm, sign, hb)
+    assert rel_err(y, ref) < 1e-5
+    z = rot.inv_f32(torch.from_numpy(ref.astype(np.float32)).to(DEV)).cpu().numpy()
+    assert rel_err(z, x.numpy()) < 1e-5
+    # unnormalised (FastRot) variant
+    yu = rot.fwd_f32(x.to(DEV), unnormalised=True).cpu().numpy()
+    assert rel_err(yu, ref * hb ** 0.5) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_rht_input_dtypes(dtype):
+    rot = vq.get_rot("attn", 2048, DEV)
+    x = torch.randn(2, 2048, generator=torch.Generator().manual_seed(3)).to(dtype)
+    y = rot.fwd_f32(x.to(DEV)).cpu().numpy()
+    ref = O.rht_fwd(x.float().numpy(), *O.rot_params("attn", 2048))
+    assert rel_err(y, ref) < 1e-5
+
+
+def test_rht_matches_reference_golden():
+    d = golden("rot.npz")
+    for tag, n in [("dense_q", 2048), ("mlp_down", 6144), ("moe_expert_512", 512), ("small_1024", 1024)]:
+        key = f"{tag}_{n}"
+        rot = vq.get_rot(tag, n, DEV)
+        x = torch.from_numpy(d[f"x_{key}"]).to(DEV)
+        assert rel_err(rot.fwd_f32(x).cpu().numpy(), d[f"fwd_{key}"]) < 1e-5
+        assert rel_err(rot.inv_f32(x).cpu().numpy(), d[f"inv_{key}"]) < 1e-5
+
+
+def test_swiglu_rht():
+    rot = vq.get_rot("moe_expert_512", 512, DEV)
+    gu = torch.randn(9, 1024, generator=torch.Generator().manual_seed(4))
+    out = kernels.swiglu_rht(gu.to(DEV), rot).cpu().numpy()
+    g, u = gu[:, :512].double().numpy(), gu[:, 512:].double().numpy()
+    ref = O.rht_fwd(O.silu(g) * u, *O.rot_params("moe_expert_512", 512))
+    assert rel_err(out, ref) < 2e-5
+
+
+# ----------------------------------------------------------------------------------------- GEMV
+def run_packed(idx, scale, x, tag, cbs_dev, out_dtype=None):
+    """Rotate x (fp32 RHT) then GEMV, as PackedLinear.forward does."""
+    out, ng = idx[0].shape
+    n = ng * 8
+    rot = vq.get_rot(tag, n, DEV)
+    xr = rot.fwd_f32(torch.from_numpy(np.asarray(x)).to(DEV))
+    i0 = torch.from_numpy(np.ascontiguousarray(idx[0])).to(DEV)
+    i1 = torch.from_numpy(np.ascontiguousarray(idx[1])).to(DEV) if len(idx) > 1 else None
+    sc = torch.from_numpy(np.asarray(scale)).to(DEV, cbs_dev["16"].dtype)
+    y = kernels.vq_gemv(xr, i0, cbs_dev["16"], sc, i1=i1, cb1=cbs_dev["16_8"] if i1 is not None else None,
+                        out_dtype=out_dtype or torch.float16)
+    return y.float().cpu().numpy()
+
+
+def test_gemv_golden_cases(cbs):
+    d = golden("gemv.npz")
+    cbd = dev_cbs(cbs)
+    names = sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_meta")})
+    assert "cfg1" in names
+    for nm in names:
+        out, n, nst, M = d[f"{nm}_meta"]
+        idx = [d[f"{nm}_idx0"]] + ([d[f"{nm}_idx1"]] if nst > 1 else [])
+        y = run_packed(idx, d[f"{nm}_scale"], d[f"{nm}_x"], str(d[f"{nm}_tag"]), cbd)
+        err = rel_err(y, d[f"{nm}_y"])
+        assert err < TOL_F16, (nm, err)
+
+
+@pytest.mark.parametrize("out,n,bits,M", [
+    (2048, 2048, (16,), 1), (2048, 2048, (16, 8), 1), (6144, 2048, (16,), 4), (2048, 6144, (16,), 1),
+    (2048, 6144, (16, 8), 4), (1000, 2048, (16,), 16), (512, 2048, (16, 8), 64), (300, 512, (16,), 3),
+    (128, 256, (16,), 2), (2048, 2048, (16,), 64), (40, 4096, (16, 8), 9),
+])
+def test_gemv_random_vs_oracle(cbs, out, n, bits, M):
+    idx, scale = synth.random_matrix(out * 7 + n, out, n, bits)
+    x = np.random.default_rng(M).standard_normal((M, n)).astype(np.float16)
+    tag = f"rand_{n}"
+    y = run_packed(idx, scale, x, tag, dev_cbs(cbs))
+    perm, sign, hb = O.rot_params(tag, n)
+    ref = O.gemv_ref(x.astype(np.float64), idx, bits, cbs, scale, perm, sign, hb)
+    assert rel_err(y, ref) < TOL_F16
+
+
+@pytest.mark.parametrize("out_dtype,tol", [(torch.bfloat16, TOL_BF16), (torch.float32, 2e-5)])
+def test_gemv_output_dtypes(cbs, out_dtype, tol):
+    idx, scale = synth.random_matrix(5, 512, 2048)
+    x = np.random.default_rng(0).standard_normal((2, 2048)).astype(np.float32)
+    y = run_packed(idx, scale, x, "dense_q", dev_cbs(cbs), out_dtype=out_dtype)
+    ref = O.gemv_ref(x, idx, (16,), cbs, scale, *O.rot_params("dense_q", 2048))
+    assert rel_err(y, ref) < tol
+
+
+def test_legacy_signatures_bf16(cbs):
+    """vq_gemv_16 / vq_gemv_16_8 with the reference's bf16 codebooks/scales and rs = 2048^-0.5."""
+    idx, scale = synth.random_matrix(9, 1024, 2048, (16, 8))
+    cbd = dev_cbs(cbs, torch.bfloat16)
+    xr = torch.randn(2048, generator=torch.Generator().manual_seed(1)).to(DEV, torch.bfloat16)
+    i0 = torch.from_numpy(idx[0]).to(DEV)
+    i1 = torch.from_numpy(idx[1]).to(DEV)
+    sc = torch.from_numpy(scale).to(DEV, torch.bfloat16)
+    rs = 2048 ** -0.5
+    y2 = kernels.vq_gemv_16(xr, i0, cbd["16"], sc, 1024, 2048, rs)
+    y3 = kernels.vq_gemv_16_8(xr, i0, i1, cbd["16"], cbd["16_8"], sc, 1024, 2048, rs)
+    assert y2.dtype == torch.bfloat16 and y2.shape == (1024,)
+    cb16 = cbd["16"].float().cpu().numpy()
+    cb8 = cbd["16_8"].float().cpu().numpy()
+    scf = sc.float().cpu().numpy()
+    xf = xr.float().cpu().numpy()
+    assert rel_err(y2.float().cpu(), O.vq_gemv_legacy(xf, idx[0], cb16, scf, rs)) < TOL_BF16
+    assert rel_err(y3.float().cpu(), O.vq_gemv_legacy(xf, idx[0], cb16, scf, rs, idx[1], cb8)) < TOL_BF16
+
+
+# ------------------------------------------------------------------------------------ MoE GEMV
+def _pool(E, seed):
+    ex = [synth.synth_expert(seed, e) for e in range(E)]
+    return [np.stack([x[i] for x in ex]) for i in range(4)]
+
+
+def test_moe_legacy_gate_up_down(cbs):
+    E = 12
+    gu_i, gu_s, dn_i, dn_s = _pool(E, 3)
+    cbd = dev_cbs(cbs)
+    slots = np.array([3, 0, 11, 7, 7, 2, 9, 5], dtype=np.int32)
+    xr = torch.randn(2048, generator=torch.Generator().manual_seed(2)).to(DEV, torch.float16)
+    y_gu = torch.empty(8, 1024, device=DEV, dtype=torch.float16)
+    kernels.vq_moe_parallel_gate_up(xr, torch.from_numpy(slots).to(DEV), torch.from_numpy(gu_i).to(DEV), cbd["16"],
+                                    torch.from_numpy(gu_s).to(DEV), y_gu)
+    ref = O.moe_gate_up_ref(xr.float().cpu().numpy(), slots, gu_i, cbs["16"], gu_s)
+    assert rel_err(y_gu.float().cpu(), ref) < TOL_F16
+    act = torch.randn(8, 512, generator=torch.Generator().manual_seed(5)).to(DEV, torch.float16)
+    y_dn = torch.empty(8, 2048, device=DEV, dtype=torch.float16)
+    kernels.vq_moe_parallel_down(act, torch.from_numpy(slots).to(DEV), torch.from_numpy(dn_i).to(DEV), cbd["16"],
+                                 torch.from_numpy(dn_s).to(DEV), y_dn)
+    ref = O.moe_down_ref(act.float().cpu().numpy(), slots, dn_i, cbs["16"], dn_s)
+    assert rel_err(y_dn.float().cpu(), ref) < TOL_F16
+
+
+def test_moe_gemv_out_of_range_ids_give_zero_rows(cbs):
+    gu_i, gu_s, _, _ = _pool(4, 1)
+    cbd = dev_cbs(cbs)
+    ids = torch.tensor([1, -1, 4, 2], dtype=torch.int32, device=DEV)
+    x = torch.randn(2048, device=DEV)
+    y = torch.full((4, 1024), 7.0, device=DEV)
+    kernels.moe_gemv(x, ids, torch.from_numpy(gu_i).to(DEV), cbd["16"], torch.from_numpy(gu_s).to(DEV), y,
+                     x_k_stride=0)
+    y = y.cpu()
+    assert torch.all(y[1] == 0) and torch.all(y[2] == 0)
+    assert torch.any(y[0] != 0) and torch.any(y[3] != 0)
+
+
+def test_moe_combine():
+    T, K, H = 3, 8, 2048
+    y = torch.randn(T * K, H, device=DEV)
+    w = torch.rand(T, K, device=DEV)
+    add = torch.randn(T, H, device=DEV)
+    out = kernels.moe_combine(y, w, K, add=add, out_dtype=torch.float32)
+    ref = (y.view(T, K, H).double() * w.double()[:, :, None]).sum(1) + add.double()
+    assert rel_err(out.cpu(), ref.cpu()) < 1e-6
