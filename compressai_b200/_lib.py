@@ -16,6 +16,7 @@ HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "vq2_b200.h")
 
 VQ2_OK, VQ2_ERR_SHAPE, VQ2_ERR_DTYPE, VQ2_ERR_ALIGN, VQ2_ERR_LAUNCH, VQ2_ERR_TIMEOUT, VQ2_ERR_ARG = range(7)
 VQ2_F16, VQ2_BF16, VQ2_F32 = 0, 1, 2
+VQ2_ACT_ROTATED, VQ2_ACT_RHT, VQ2_ACT_SWIGLU_RHT = 0, 1, 2
 
 _DTYPE_CODE = {torch.float16: VQ2_F16, torch.bfloat16: VQ2_BF16, torch.float32: VQ2_F32}
 
@@ -31,9 +32,13 @@ SIGNATURES = {
     "vq2_last_cuda_error": [],
     "vq2_rht": [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _f32, _i32, _p, _i64, _p],
     "vq2_swiglu_rht": [_p, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _i64, _p],
+    "vq2_gemv_multi": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _i64, _p, _p, _p, _p, _p, _p, _i32, _p,
+                       _i32, _i64, _i64, _f32, _p],
     "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p],
-    "vq2_moe_gemv": [_p, _i32, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _f32, _p],
+    "vq2_moe_gemv": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _i64, _i64, _p, _p, _p, _i32, _p, _i32,
+                     _i64, _i64, _f32, _p],
     "vq2_moe_combine": [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p],
+    "vq2_gather_probe": [_p, _i64, _i64, _i64, _p, _p],
 }
 ABI_VERSION = 1
 
@@ -102,6 +107,14 @@ def dtype_code(t):
 
 def ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def ptr_array(ctype, values):
+    """Host array of pointers/sizes for the multi-matrix entry points."""
+    arr = (ctype * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = v
+    return arr
 
 
 def stream_ptr(device):

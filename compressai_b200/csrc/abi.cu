@@ -3,9 +3,33 @@
 
 #include "common.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace vq2 {
 static std::atomic<int> g_last_cuda_error{0};
 void set_last_cuda_error(cudaError_t e) { g_last_cuda_error.store(static_cast<int>(e)); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VQ2_PDL");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int v = cache[dev & 63].load();
+  if (v == 0) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (v <= 0) v = 148;
+    cache[dev & 63].store(v);
+  }
+  return v;
+}
 }  // namespace vq2
 
 extern "C" int vq2_abi_version(void) { return 1; }

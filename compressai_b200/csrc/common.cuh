@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "vq2_b200.h"
 
 namespace vq2 {
@@ -77,5 +79,40 @@ __device__ __forceinline__ uint4 ld_cb_u4(const void* p, uint64_t pol) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
   return v;
 }
+
+// ---- programmatic dependent launch (PDL) ------------------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the previous kernel
+// in the stream is still running. It must call pdl_wait() before reading anything that kernel
+// wrote (or writing anything it reads); work on constant inputs (weights) may come earlier.
+// pdl_trigger() lets the next kernel in the stream start its own pre-wait portion.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether launches carry the PDL attribute (environment VQ2_PDL=0 disables it).
+bool pdl_enabled();
+
+// Launch `kern` on `st` with the PDL attribute when enabled; returns a VQ2 status.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return VQ2_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
 
 }  // namespace vq2

@@ -2,16 +2,24 @@
 //
 //   y[m, r] = rs * scale[r] * sum_g dot(cb0[idx0[r, g]] (+ cb1[idx1[r, g]]), xr[m, 8g:8g+8])
 //
-// Work split: a warp owns RW x RPL rows; LPR lanes cover one row (RPL = 32 / LPR rows per
-// warp-load), each lane loading 8 consecutive int16 indices (16 B) of its row per chunk with
-// one streaming 128-bit load. Each index is decoded by a 16-byte gather of the fp16/bf16
-// codebook row (read-only path, L1-allocating, L2 evict-last) and dotted with the 8 matching
-// activations held in shared memory as fp32. The residual codebook (3 bpw) is staged in
-// shared memory. Lane partial sums are reduced with warp shuffles; lane 0 of each row writes
-// the scaled result in the value dtype.
+// Bound: every 2-byte index costs one random 16-byte codebook gather. On B200 the codebook
+// (1 MiB fp16) lives in L2 and random 16-byte L2 gathers sustain ~1.1 per clock per SM, so the
+// kernel is gather-throughput bound well below HBM bandwidth; the design keeps that pipe busy:
 //
-// The activation tile in shared memory is padded by 4 floats every 8 groups so that the 8
-// lanes of one 128-bit access phase, which read groups 8 apart, hit distinct bank groups.
+// * Work items are (problem k, M tile, block of rows); a persistent grid walks them with a
+//   grid stride. A warp owns RW x RPL rows of an item; LPR lanes cover one row, each lane
+//   loading 8 consecutive int16 indices (16 B) per chunk with one streaming 128-bit load.
+// * The next task's index vectors are prefetched into registers while the current task's
+//   gathers and FMAs run, so HBM latency overlaps the gather pipe.
+// * Codebook rows are gathered with 128-bit read-only loads (L2 evict-last policy); index
+//   streams use no-L1-allocate loads with an L2 evict-first policy so they do not push
+//   codebook lines out.
+// * For n = 2048 at M = 1 each lane's 64 activations stay in registers for the whole kernel;
+//   otherwise the fp32 activation tile sits in shared memory, padded by 4 floats every 8 groups
+//   so the 8 lanes of one 128-bit access phase (groups 8 apart) hit distinct bank groups.
+// * The residual codebook (3 bpw, 4 KB) is staged in shared memory.
+// * Programmatic dependent launch: weights are prefetched before griddepcontrol.wait, so a
+//   GEMV's first index loads overlap the tail of the kernel that produces its input.
 //
 // Semantics: reference vq2/kernels.py:32-78 (_vq_gemv_16_8/_vq_gemv_16, M = 1) and
 // :117-176 (_parallel_moe_*: expert-indexed, shared or per-expert activation).
@@ -21,29 +29,49 @@
 
 namespace vq2 {
 
+constexpr int kMaxProbs = 8;  // matrices sharing one activation in a multi-matrix launch
+
 struct GemvArgs {
-  const void* x;          // activations, x_dtype
+  const void* x;          // activations, x_dtype (mode SWIGLU_RHT: fp32 [gate | up] rows)
   int x_dtype;
+  int x_mode;             // VQ2_ACT_ROTATED / VQ2_ACT_RHT / VQ2_ACT_SWIGLU_RHT
   int64_t x_row_stride;   // elements between activation rows m
   int64_t x_k_stride;     // elements between activation groups of problems (0 = shared)
   int64_t x_k_div;        // problem k reads activation group k / x_k_div
+  const int32_t* perm;    // rotation (modes RHT, SWIGLU_RHT)
+  const int8_t* sign;
+  int hb;
+  float rot_scale;
   int M;                  // activation rows
+  // expert-indexed problems (nprob == 0): problem k uses expert e_ids[k] of one pool
   const int16_t* idx0;    // [E, out, ng]
   const uint8_t* idx1;    // [E, out, ng] or null
-  const void* cb0;        // [65536, 8] val
-  const void* cb1;        // [256, 8] val or null
   const void* scale;      // [E, out] val
-  void* y;                // y_dtype
-  int y_dtype;
-  int64_t y_row_stride;   // elements between output rows m
-  int64_t y_k_stride;     // elements between problems k
+  void* y;                // [K, M, out] y_dtype
   const int32_t* e_ids;   // [K] or null (problem k uses expert 0)
   int64_t num_experts;
   int64_t idx_e_stride;   // out * ng
   int64_t scale_e_stride; // out
-  int out;
+  int64_t y_k_stride;     // elements between problems k
+  // multi-matrix problems (nprob > 0): problem p has its own weights/outputs, one shared x
+  int nprob;
+  const int16_t* p_idx0[kMaxProbs];
+  const uint8_t* p_idx1[kMaxProbs];
+  const void* p_scale[kMaxProbs];
+  void* p_y[kMaxProbs];
+  int p_out[kMaxProbs];
+  int p_rb0[kMaxProbs + 1];  // first row block of each problem
+  // common
+  const void* cb0;        // [65536, 8] val
+  const void* cb1;        // [256, 8] val or null
+  int y_dtype;
+  int64_t y_row_stride;   // elements between output rows m
+  int out;                // rows (expert-indexed mode)
   int n;
   float rs;
+  int K;                  // problems (expert-indexed mode)
+  int mtiles;             // M tiles
+  int row_blocks;         // row blocks per (problem, M tile) (expert mode) / total (multi mode)
 };
 
 // Padded position of activation element (group g, lane t) in shared memory.
@@ -56,86 +84,259 @@ __device__ __forceinline__ void decode8(const uint4 w, float f[8]) {
   f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
 }
 
-template <int LPR, int RW, int MT, bool RES, typename TV>
-__global__ void __launch_bounds__(256) vq_gemv_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) float smem[];
-  const int n = a.n;
-  const int xl = xs_len(n);
-  float* xs = smem;                                            // [MT][xl]
-  uint4* cb1s = reinterpret_cast<uint4*>(smem + MT * xl);      // [256] when RES
+constexpr int kScratchFloats = 2048 + 64;  // one RHT transpose round: SEG x (hb + hb/32) floats
 
-  const int k = blockIdx.y;
-  const int m0 = blockIdx.z * MT;
-  const int mt = min(MT, a.M - m0);
-  int64_t e = 0;
-  bool valid = true;
-  if (a.e_ids) {
-    e = a.e_ids[k];
-    valid = (e >= 0 && e < a.num_experts);
-    if (!valid) e = 0;
-  }
+__device__ __forceinline__ float load_act(const void* x, int dt, int64_t off) {
+  if (dt == VQ2_F32) return static_cast<const float*>(x)[off];
+  if (dt == VQ2_F16) return __half2float(static_cast<const __half*>(x)[off]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[off]);
+}
 
-  // ---- activations -> fp32, padded layout ----
-  for (int i = threadIdx.x; i < MT * n; i += blockDim.x) {
-    const int mi = i / n, j = i - mi * n;
-    float v = 0.f;
-    if (mi < mt) {
-      const int64_t off = (int64_t)(m0 + mi) * a.x_row_stride + (int64_t)(k / a.x_k_div) * a.x_k_stride + j;
-      if (a.x_dtype == VQ2_F32) v = static_cast<const float*>(a.x)[off];
-      else if (a.x_dtype == VQ2_F16) v = __half2float(static_cast<const __half*>(a.x)[off]);
-      else v = __bfloat162float(static_cast<const __nv_bfloat16*>(a.x)[off]);
+__device__ __forceinline__ void fwht8(float v[8]) {
+#pragma unroll
+  for (int d = 1; d < 8; d <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if ((i & d) == 0) {
+        const float a = v[i], b = v[i + d];
+        v[i] = a + b;
+        v[i + d] = a - b;
+      }
     }
-    xs[mi * xl + xs_pos(j >> 3, j & 7)] = v;
   }
-  if (RES) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) cb1s[i] = static_cast<const uint4*>(a.cb1)[i];
-  }
-  __syncthreads();
+}
 
-  constexpr int RPL = 32 / LPR;
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+
+// Stage MT activation rows (starting at element offset xoff) into the padded fp32 tile xs.
+// Mode ROTATED copies; modes RHT / SWIGLU_RHT apply the forward randomized Hadamard transform
+// (perm gather, sign, blocked Sylvester Hadamard, rot_scale) with the whole CTA: a segment of
+// hb elements belongs to T = hb/8 threads (8 values each): 3 butterfly stages in registers,
+// one transpose through `scratch`, 3 more in registers, the rest with warp shuffles (the same
+// scheme as the standalone vq2_rht kernel). Must be called by all 256 threads.
+template <int MT>
+__device__ void stage_activations(const GemvArgs& a, int64_t xoff, int mcount, float* xs, int xl, float* scratch) {
+  const int n = a.n;
+  if (a.x_mode == VQ2_ACT_ROTATED) {
+    for (int i = threadIdx.x; i < MT * n; i += blockDim.x) {
+      const int mi = i / n, j = i - mi * n;
+      const float v = mi < mcount ? load_act(a.x, a.x_dtype, xoff + (int64_t)mi * a.x_row_stride + j) : 0.f;
+      xs[mi * xl + xs_pos(j >> 3, j & 7)] = v;
+    }
+    return;
+  }
+  const int hb = a.hb, T = hb >> 3, SEG = 256 / T, nb = n / hb;
+  const int s = threadIdx.x / T, t = threadIdx.x % T;
+  const int segs = MT * nb;
+  const bool swiglu = (a.x_mode == VQ2_ACT_SWIGLU_RHT);
+  float* sc = scratch + s * (hb + (hb >> 5));
+  for (int s0 = 0; s0 < segs; s0 += SEG) {
+    const int gs = s0 + s;
+    const int mi = gs / nb, b = gs - mi * nb;
+    const bool active = gs < segs && mi < mcount;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float val = 0.f;
+      if (active) {
+        const int j = b * hb + t + T * i;
+        const int64_t row = xoff + (int64_t)mi * a.x_row_stride;
+        const int p = a.perm[j];
+        if (swiglu) {
+          const float* g = static_cast<const float*>(a.x) + row;
+          val = silu_f(g[p]) * g[n + p];
+        } else {
+          val = load_act(a.x, a.x_dtype, row + p);
+        }
+        val *= static_cast<float>(a.sign[j]);
+      }
+      v[i] = val;
+    }
+    fwht8(v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = t + T * i;
+      sc[e + (e >> 5)] = v[i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = 8 * t + i;
+      v[i] = sc[e + (e >> 5)];
+    }
+    fwht8(v);
+    for (int td = 1; td <= (T >> 4); td <<= 1) {
+      const bool upper = (t & td) != 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float q = __shfl_xor_sync(0xffffffffu, v[i], td);
+        v[i] = upper ? (q - v[i]) : (v[i] + q);
+      }
+    }
+    if (gs < segs) {
+      const int g = (b * hb >> 3) + t;  // 8-element group index within the row
+      float* o = xs + mi * xl + xs_pos(g, 0);
+      const float r = a.rot_scale;
+      *reinterpret_cast<float4*>(o) = make_float4(v[0] * r, v[1] * r, v[2] * r, v[3] * r);
+      *reinterpret_cast<float4*>(o + 4) = make_float4(v[4] * r, v[5] * r, v[6] * r, v[7] * r);
+    }
+    __syncthreads();
+  }
+}
+
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
+__global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
+  static_assert(!XREG || (LPR == 32 && MT == 1), "register activations need one 256-group chunk, M tile 1");
+  constexpr int RPL = 32 / LPR;   // rows per warp-load
+  constexpr int RPW = RW * RPL;   // rows per warp per item
+  constexpr int RPC = 8 * RPW;    // rows per CTA per item
+  extern __shared__ __align__(16) float smem[];
+  const int n = a.n, ng = n >> 3, xl = xs_len(n);
+  float* xs = smem;                                            // [MT][xl] activation tile
+  float* scratch = smem + MT * xl;                             // RHT transpose scratch (2112 floats)
+  uint4* cb1s = reinterpret_cast<uint4*>(scratch + kScratchFloats);  // [256] when RES
+
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane / LPR, li = lane % LPR;
-  const int row0 = blockIdx.x * (8 * RW * RPL) + warp * (RW * RPL) + sub;
-  const int ng = n >> 3;
   const int chunks = ng / (8 * LPR);
-  const int16_t* idx0 = a.idx0 + e * a.idx_e_stride;
-  const uint8_t* idx1 = RES ? a.idx1 + e * a.idx_e_stride : nullptr;
+  const bool multi = a.nprob > 0;
+  const int64_t items = multi ? (int64_t)a.row_blocks * a.mtiles : (int64_t)a.row_blocks * a.K * a.mtiles;
   const uint4* cb0 = static_cast<const uint4*>(a.cb0);
   const uint64_t pol_s = policy_evict_first();
   const uint64_t pol_c = policy_evict_last();
+  const bool weights_known = (a.e_ids == nullptr);  // expert ids may come from the previous kernel
 
-  float acc[RW][MT];
-#pragma unroll
-  for (int rw = 0; rw < RW; ++rw)
-#pragma unroll
-    for (int mi = 0; mi < MT; ++mi) acc[rw][mi] = 0.f;
-
-  for (int c = 0; c < chunks; ++c) {
-    const int gl = c * LPR + li;   // this lane's 8-group block index
-    const int g0 = gl * 8;
-    uint4 iv[RW];
-    uint2 jv[RW];
+  // One work item = RPC rows of one problem for one M tile. Each CTA owns a contiguous range
+  // of items, so consecutive items mostly share their problem and activation tile.
+  struct Item { int rb, mt, k, out; int64_t e; const int16_t* i0; const uint8_t* i1; bool valid; };
+  auto decode = [&](int64_t it) -> Item {
+    Item w;
+    if (multi) {
+      w.mt = (int)(it / a.row_blocks);
+      const int rbg = (int)(it - (int64_t)w.mt * a.row_blocks);
+      int p = 0;
+#pragma unroll 1
+      while (p + 1 < a.nprob && rbg >= a.p_rb0[p + 1]) ++p;
+      w.k = p;
+      w.rb = rbg - a.p_rb0[p];
+      w.out = a.p_out[p];
+      w.e = 0;
+      w.i0 = a.p_idx0[p];
+      w.i1 = a.p_idx1[p];
+      w.valid = true;
+    } else {
+      w.rb = (int)(it % a.row_blocks);
+      const int64_t q = it / a.row_blocks;
+      w.mt = (int)(q % a.mtiles);
+      w.k = (int)(q / a.mtiles);
+      w.out = a.out;
+      int64_t e = 0;
+      w.valid = true;
+      if (a.e_ids) {
+        e = a.e_ids[w.k];
+        w.valid = (e >= 0 && e < a.num_experts);
+        if (!w.valid) e = 0;
+      }
+      w.e = e;
+      w.i0 = a.idx0 + e * a.idx_e_stride;
+      w.i1 = RES ? a.idx1 + e * a.idx_e_stride : nullptr;
+    }
+    return w;
+  };
+  auto load_idx = [&](const Item& w, int c, uint4 (&iv)[RW], uint2 (&jv)[RW]) {
+    const int g0 = (c * LPR + li) * 8;
 #pragma unroll
     for (int rw = 0; rw < RW; ++rw) {
-      const int r = row0 + rw * RPL;
-      if (valid && r < a.out) {
-        iv[rw] = ld_stream_u4(idx0 + (int64_t)r * ng + g0, pol_s);
-        if (RES) jv[rw] = ld_stream_u2(idx1 + (int64_t)r * ng + g0, pol_s);
+      const int r = w.rb * RPC + warp * RPW + rw * RPL + sub;
+      if (w.valid && r < w.out) {
+        iv[rw] = ld_stream_u4(w.i0 + (int64_t)r * ng + g0, pol_s);
+        if (RES) jv[rw] = ld_stream_u2(w.i1 + (int64_t)r * ng + g0, pol_s);
       } else {
         iv[rw] = make_uint4(0, 0, 0, 0);
         if (RES) jv[rw] = make_uint2(0, 0);
       }
     }
+  };
+
+  const int64_t per = (items + gridDim.x - 1) / gridDim.x;
+  int64_t item = (int64_t)blockIdx.x * per;
+  const int64_t item_end = min(items, item + per);
+  int chunk = 0;
+  uint4 iv[RW];
+  uint2 jv[RW];
+  Item cur;
+  if (weights_known && item < item_end) {  // constant weights: safe before the dependency wait
+    cur = decode(item);
+    load_idx(cur, 0, iv, jv);
+  }
+  pdl_wait();
+  if (!weights_known && item < item_end) {
+    cur = decode(item);
+    load_idx(cur, 0, iv, jv);
+  }
+  if (RES) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) cb1s[i] = static_cast<const uint4*>(a.cb1)[i];
+  }
+  pdl_trigger();
+
+  int64_t cur_xoff = -1;
+  float xreg[XREG ? 64 : 1];
+  float acc[RW][MT];
+
+  while (item < item_end) {
+    const int m0 = cur.mt * MT;
+    const int mcount = min(MT, a.M - m0);
+    const int64_t xoff = (int64_t)m0 * a.x_row_stride + (multi ? 0 : (int64_t)(cur.k / a.x_k_div) * a.x_k_stride);
+    if (xoff != cur_xoff) {  // uniform over the CTA
+      __syncthreads();
+      stage_activations<MT>(a, xoff, mcount, xs, xl, scratch);
+      __syncthreads();
+      if constexpr (XREG) {  // this lane's 8 groups -> registers (conflict-free: lanes 68 floats apart)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 lo = *reinterpret_cast<const float4*>(xs + xs_pos(li * 8 + j, 0));
+          const float4 hi = *reinterpret_cast<const float4*>(xs + xs_pos(li * 8 + j, 4));
+          xreg[j * 8 + 0] = lo.x; xreg[j * 8 + 1] = lo.y; xreg[j * 8 + 2] = lo.z; xreg[j * 8 + 3] = lo.w;
+          xreg[j * 8 + 4] = hi.x; xreg[j * 8 + 5] = hi.y; xreg[j * 8 + 6] = hi.z; xreg[j * 8 + 7] = hi.w;
+        }
+      }
+      cur_xoff = xoff;
+    }
+
+    // prefetch the next task's indices
+    int64_t nitem = item;
+    int nchunk = chunk + 1;
+    if (nchunk == chunks) { nchunk = 0; nitem = item + 1; }
+    uint4 nv[RW];
+    uint2 njv[RW];
+    Item nxt = cur;
+    if (nitem < item_end) {
+      if (nitem != item) nxt = decode(nitem);
+      load_idx(nxt, nchunk, nv, njv);
+    }
+
+    if (chunk == 0) {
+#pragma unroll
+      for (int rw = 0; rw < RW; ++rw)
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) acc[rw][mi] = 0.f;
+    }
+    const int g0 = (chunk * LPR + li) * 8;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float xv[MT][8];
-      const int p = xs_pos(g0 + j, 0);
+      if constexpr (XREG) {
 #pragma unroll
-      for (int mi = 0; mi < MT; ++mi) {
-        const float4 lo = *reinterpret_cast<const float4*>(xs + mi * xl + p);
-        const float4 hi = *reinterpret_cast<const float4*>(xs + mi * xl + p + 4);
-        xv[mi][0] = lo.x; xv[mi][1] = lo.y; xv[mi][2] = lo.z; xv[mi][3] = lo.w;
-        xv[mi][4] = hi.x; xv[mi][5] = hi.y; xv[mi][6] = hi.z; xv[mi][7] = hi.w;
+        for (int t = 0; t < 8; ++t) xv[0][t] = xreg[j * 8 + t];
+      } else {
+        const int p = xs_pos(g0 + j, 0);
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+          const float4 lo = *reinterpret_cast<const float4*>(xs + mi * xl + p);
+          const float4 hi = *reinterpret_cast<const float4*>(xs + mi * xl + p + 4);
+          xv[mi][0] = lo.x; xv[mi][1] = lo.y; xv[mi][2] = lo.z; xv[mi][3] = lo.w;
+          xv[mi][4] = hi.x; xv[mi][5] = hi.y; xv[mi][6] = hi.z; xv[mi][7] = hi.w;
+        }
       }
 #pragma unroll
       for (int rw = 0; rw < RW; ++rw) {
@@ -159,88 +360,132 @@ __global__ void __launch_bounds__(256) vq_gemv_kernel(const GemvArgs a) {
         }
       }
     }
-  }
 
+    if (chunk == chunks - 1) {
 #pragma unroll
-  for (int rw = 0; rw < RW; ++rw)
+      for (int rw = 0; rw < RW; ++rw)
 #pragma unroll
-    for (int mi = 0; mi < MT; ++mi)
+        for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
-      for (int off = LPR / 2; off > 0; off >>= 1) acc[rw][mi] += __shfl_xor_sync(0xffffffffu, acc[rw][mi], off);
-
-  if (li == 0) {
-    const TV* sc = static_cast<const TV*>(a.scale) + e * a.scale_e_stride;
-    const int64_t ybase = (int64_t)k * a.y_k_stride;
+          for (int off = LPR / 2; off > 0; off >>= 1) acc[rw][mi] += __shfl_xor_sync(0xffffffffu, acc[rw][mi], off);
+      if (li == 0) {
+        const TV* sc = multi ? static_cast<const TV*>(a.p_scale[cur.k])
+                             : static_cast<const TV*>(a.scale) + cur.e * a.scale_e_stride;
+        void* ybase = multi ? a.p_y[cur.k] : a.y;
+        const int64_t yk = multi ? 0 : (int64_t)cur.k * a.y_k_stride;
 #pragma unroll
-    for (int rw = 0; rw < RW; ++rw) {
-      const int r = row0 + rw * RPL;
-      if (r < a.out) {
-        const float s = valid ? to_f32<TV>(sc[r]) * a.rs : 0.f;
+        for (int rw = 0; rw < RW; ++rw) {
+          const int r = cur.rb * RPC + warp * RPW + rw * RPL + sub;
+          if (r < cur.out) {
+            const float s = cur.valid ? to_f32<TV>(sc[r]) * a.rs : 0.f;
 #pragma unroll
-        for (int mi = 0; mi < MT; ++mi) {
-          if (mi < mt) {
-            const int64_t o = ybase + (int64_t)(m0 + mi) * a.y_row_stride + r;
-            const float v = acc[rw][mi] * s;
-            if (a.y_dtype == VQ2_F16) static_cast<__half*>(a.y)[o] = __float2half_rn(v);
-            else if (a.y_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(v);
-            else static_cast<float*>(a.y)[o] = v;
+            for (int mi = 0; mi < MT; ++mi) {
+              if (mi < mcount) {
+                const int64_t o = yk + (int64_t)(m0 + mi) * a.y_row_stride + r;
+                const float v = acc[rw][mi] * s;
+                if (a.y_dtype == VQ2_F16) static_cast<__half*>(ybase)[o] = __float2half_rn(v);
+                else if (a.y_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(ybase)[o] = __float2bfloat16_rn(v);
+                else static_cast<float*>(ybase)[o] = v;
+              }
+            }
           }
         }
       }
+    }
+    item = nitem;
+    chunk = nchunk;
+    cur = nxt;
+#pragma unroll
+    for (int rw = 0; rw < RW; ++rw) {
+      iv[rw] = nv[rw];
+      if (RES) jv[rw] = njv[rw];
     }
   }
 }
 
 // ---- host dispatch ------------------------------------------------------------------------
-constexpr int kRW = 2;
 constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the SM's 256 KB stays L1
 
-template <int LPR, int MT, bool RES, typename TV>
-static int launch4(const GemvArgs& a, int K, cudaStream_t st) {
-  constexpr int rows_per_cta = 8 * kRW * (32 / LPR);
-  const int mtiles = (a.M + MT - 1) / MT;
-  if (K > 65535 || mtiles > 65535) return VQ2_ERR_SHAPE;  // grid.y / grid.z limits
-  const dim3 grid((a.out + rows_per_cta - 1) / rows_per_cta, K, mtiles);
-  const size_t smem = (size_t)MT * xs_len(a.n) * sizeof(float) + (RES ? 256 * sizeof(uint4) : 0);
-  auto kern = vq_gemv_kernel<LPR, kRW, MT, RES, TV>;
-  if (smem > 48 * 1024) {
-    // Opt in to the largest dynamic shared memory this kernel can use, once per device.
-    static std::atomic<uint64_t> done{0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = uint64_t(1) << (dev & 63);
-    if (!(done.load() & bit)) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxXsBytes + 4096);
-      if (e != cudaSuccess) { set_last_cuda_error(e); return VQ2_ERR_LAUNCH; }
-      done.fetch_or(bit);
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
+static int launch_cfg(GemvArgs a, cudaStream_t st) {
+  constexpr int RPC = 8 * RW * (32 / LPR);
+  a.mtiles = (a.M + MT - 1) / MT;
+  int64_t items;
+  if (a.nprob > 0) {
+    int rb = 0;
+    for (int p = 0; p < a.nprob; ++p) {
+      a.p_rb0[p] = rb;
+      rb += (a.p_out[p] + RPC - 1) / RPC;
     }
+    a.p_rb0[a.nprob] = rb;
+    a.row_blocks = rb;
+    items = (int64_t)rb * a.mtiles;
+  } else {
+    a.row_blocks = (a.out + RPC - 1) / RPC;
+    items = (int64_t)a.row_blocks * a.K * a.mtiles;
   }
-  kern<<<grid, 256, smem, st>>>(a);
-  return launch_status();
+  const size_t smem = ((size_t)MT * xs_len(a.n) + kScratchFloats) * sizeof(float) + (RES ? 256 * sizeof(uint4) : 0);
+  auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV>;
+  // Per-device one-time attributes: dynamic shared memory opt-in and, for the small-tile
+  // variants, a small shared-memory carveout so most of the SM's 256 KB serves as L1.
+  static std::atomic<uint64_t> done{0};
+  static std::atomic<int> blocks_per_sm{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kMaxXsBytes + kScratchFloats * 4 + 4096);
+    if (e == cudaSuccess && XREG) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 20);
+    if (e != cudaSuccess) { set_last_cuda_error(e); return VQ2_ERR_LAUNCH; }
+    int nb = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, smem);
+    blocks_per_sm.store(nb > 0 ? nb : 1);
+    done.fetch_or(bit);
+  }
+  const int64_t cap = (int64_t)sm_count() * blocks_per_sm.load();
+  const int64_t grid = items < cap ? items : cap;
+  if (grid <= 0) return VQ2_OK;
+  return launch_kernel(kern, dim3((unsigned)grid), dim3(256), smem, st, a);
+}
+
+template <int LPR, int RW, bool RES, typename TV>
+static int launch_mt(const GemvArgs& a, int mt, bool xreg, cudaStream_t st) {
+  if constexpr (LPR == 32) {
+    if (xreg && mt == 1) return launch_cfg<LPR, RW, 1, RES, true, TV>(a, st);
+  }
+  switch (mt) {
+    case 1: return launch_cfg<LPR, RW, 1, RES, false, TV>(a, st);
+    case 2: return launch_cfg<LPR, RW, 2, RES, false, TV>(a, st);
+    case 4: return launch_cfg<LPR, RW, 4, RES, false, TV>(a, st);
+    default: return launch_cfg<LPR, RW, 8, RES, false, TV>(a, st);
+  }
 }
 
 template <int LPR, bool RES, typename TV>
-static int launch3(const GemvArgs& a, int mt, int K, cudaStream_t st) {
-  switch (mt) {
-    case 1: return launch4<LPR, 1, RES, TV>(a, K, st);
-    case 2: return launch4<LPR, 2, RES, TV>(a, K, st);
-    case 4: return launch4<LPR, 4, RES, TV>(a, K, st);
-    default: return launch4<LPR, 8, RES, TV>(a, K, st);
+static int launch_rw(const GemvArgs& a, int64_t total_rows, int mt, bool xreg, cudaStream_t st) {
+  // Few rows (small matrices, MoE problems) or wide M tiles: one row per warp-load keeps many
+  // CTAs busy within the register budget; many rows at M tile 1: two rows per warp amortise
+  // activation reads over more gathers.
+  if (mt == 1 && total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / LPR)) {
+    if (xreg && LPR == 32) return launch_cfg<LPR, 2, 1, RES, LPR == 32, TV>(a, st);
+    return launch_cfg<LPR, 2, 1, RES, false, TV>(a, st);
   }
+  return launch_mt<LPR, 1, RES, TV>(a, mt, xreg, st);
 }
 
 template <bool RES, typename TV>
-static int launch2(const GemvArgs& a, int lpr, int mt, int K, cudaStream_t st) {
+static int launch_lpr(const GemvArgs& a, int64_t total_rows, int lpr, int mt, cudaStream_t st) {
+  const bool xreg = (a.n == 2048);
   switch (lpr) {
-    case 4: return launch3<4, RES, TV>(a, mt, K, st);
-    case 8: return launch3<8, RES, TV>(a, mt, K, st);
-    case 16: return launch3<16, RES, TV>(a, mt, K, st);
-    default: return launch3<32, RES, TV>(a, mt, K, st);
+    case 4: return launch_rw<4, RES, TV>(a, total_rows, mt, false, st);
+    case 8: return launch_rw<8, RES, TV>(a, total_rows, mt, false, st);
+    case 16: return launch_rw<16, RES, TV>(a, total_rows, mt, false, st);
+    default: return launch_rw<32, RES, TV>(a, total_rows, mt, xreg, st);
   }
 }
 
-// Largest M tile (1, 2, 4, 8) whose fp32 activation tile fits kMaxXsBytes of shared memory,
-// leaving the rest of the SM's 256 KB to L1 for codebook rows.
+// Largest M tile (1, 2, 4, 8) whose fp32 activation tile fits kMaxXsBytes of shared memory.
 static int pick_mt(int64_t M, int64_t n) {
   int mt = M >= 8 ? 8 : M >= 4 ? 4 : M >= 2 ? 2 : 1;
   while (mt > 1 && (int64_t)mt * xs_len((int)n) * 4 > kMaxXsBytes) mt >>= 1;
@@ -256,15 +501,27 @@ static int pick_lpr(int64_t ng) {
   return 0;
 }
 
-int run_gemv(const GemvArgs& a, int K, bool res, int val_dtype, cudaStream_t st) {
+static int check_act(const GemvArgs& a) {
+  if (a.x_mode == VQ2_ACT_ROTATED) return VQ2_OK;
+  if (a.x_mode != VQ2_ACT_RHT && a.x_mode != VQ2_ACT_SWIGLU_RHT) return VQ2_ERR_ARG;
+  if (!a.perm || !a.sign) return VQ2_ERR_ARG;
+  if (a.hb < 64 || a.hb > 2048 || (a.hb & (a.hb - 1)) != 0 || a.n % a.hb != 0) return VQ2_ERR_SHAPE;
+  if (a.x_mode == VQ2_ACT_SWIGLU_RHT && a.x_dtype != VQ2_F32) return VQ2_ERR_DTYPE;
+  return VQ2_OK;
+}
+
+int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st) {
   const int lpr = pick_lpr(a.n / 8);
   if (lpr == 0) return VQ2_ERR_SHAPE;
   if ((int64_t)xs_len(a.n) * 4 > kMaxXsBytes) return VQ2_ERR_SHAPE;  // n <= 19264
+  const int st_act = check_act(a);
+  if (st_act != VQ2_OK) return st_act;
   const int mt = pick_mt(a.M, a.n);
   if (val_dtype == VQ2_F16)
-    return res ? launch2<true, __half>(a, lpr, mt, K, st) : launch2<false, __half>(a, lpr, mt, K, st);
+    return res ? launch_lpr<true, __half>(a, total_rows, lpr, mt, st) : launch_lpr<false, __half>(a, total_rows, lpr, mt, st);
   if (val_dtype == VQ2_BF16)
-    return res ? launch2<true, __nv_bfloat16>(a, lpr, mt, K, st) : launch2<false, __nv_bfloat16>(a, lpr, mt, K, st);
+    return res ? launch_lpr<true, __nv_bfloat16>(a, total_rows, lpr, mt, st)
+               : launch_lpr<false, __nv_bfloat16>(a, total_rows, lpr, mt, st);
   return VQ2_ERR_DTYPE;
 }
 
@@ -272,30 +529,66 @@ int run_gemv(const GemvArgs& a, int K, bool res, int val_dtype, cudaStream_t st)
 
 static bool dtype_ok(int d) { return d == VQ2_F32 || d == VQ2_F16 || d == VQ2_BF16; }
 
+extern "C" int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,
+                              const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale, int64_t P,
+                              const int16_t* const* idx0, const uint8_t* const* idx1, const int64_t* out,
+                              const void* const* scale, const void* cb0, const void* cb1, int val_dtype,
+                              void* const* y, int y_dtype, int64_t y_row_stride, int64_t n, float rs,
+                              void* stream) {
+  using namespace vq2;
+  if (!x || !idx0 || !out || !scale || !y || !cb0) return VQ2_ERR_ARG;
+  if (P <= 0 || P > kMaxProbs) return VQ2_ERR_SHAPE;
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQ2_ERR_DTYPE;
+  if (M <= 0 || n <= 0 || n % 64 != 0 || n > INT32_MAX || M > INT32_MAX) return VQ2_ERR_SHAPE;
+  const int64_t xrow = x_mode == VQ2_ACT_SWIGLU_RHT ? 2 * n : n;
+  if (x_row_stride < xrow) return VQ2_ERR_SHAPE;
+  if (!aligned(cb0, 16) || (cb1 && !aligned(cb1, 16))) return VQ2_ERR_ALIGN;
+  const bool res = idx1 != nullptr && idx1[0] != nullptr;
+  if (res != (cb1 != nullptr)) return VQ2_ERR_ARG;
+  GemvArgs a{};
+  int64_t total_rows = 0, max_out = 0;
+  for (int p = 0; p < P; ++p) {
+    if (!idx0[p] || !scale[p] || !y[p]) return VQ2_ERR_ARG;
+    if (res && !idx1[p]) return VQ2_ERR_ARG;
+    if (!res && idx1 && idx1[p]) return VQ2_ERR_ARG;
+    if (out[p] <= 0 || out[p] > INT32_MAX) return VQ2_ERR_SHAPE;
+    if (!aligned(idx0[p], 16) || (res && !aligned(idx1[p], 8))) return VQ2_ERR_ALIGN;
+    a.p_idx0[p] = idx0[p];
+    a.p_idx1[p] = res ? idx1[p] : nullptr;
+    a.p_scale[p] = scale[p];
+    a.p_y[p] = y[p];
+    a.p_out[p] = (int)out[p];
+    total_rows += out[p];
+    max_out = out[p] > max_out ? out[p] : max_out;
+  }
+  if (y_row_stride < max_out && M > 1) return VQ2_ERR_SHAPE;
+  a.nprob = (int)P;
+  a.x = x; a.x_dtype = x_dtype; a.x_mode = x_mode; a.x_row_stride = x_row_stride; a.x_k_stride = 0; a.x_k_div = 1;
+  a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale;
+  a.M = (int)M; a.cb0 = cb0; a.cb1 = cb1; a.y_dtype = y_dtype; a.y_row_stride = y_row_stride;
+  a.n = (int)n; a.rs = rs; a.K = 1; a.out = (int)max_out;
+  return run_gemv(a, total_rows, res, val_dtype, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_stride, const int16_t* idx0,
                         const uint8_t* idx1, const void* cb0, const void* cb1, const void* scale, int val_dtype,
                         void* y, int y_dtype, int64_t y_row_stride, int64_t out, int64_t n, float rs,
                         void* stream) {
-  using namespace vq2;
   if (!xr || !idx0 || !cb0 || !scale || !y) return VQ2_ERR_ARG;
   if ((idx1 == nullptr) != (cb1 == nullptr)) return VQ2_ERR_ARG;
-  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQ2_ERR_DTYPE;
-  if (M <= 0 || out <= 0 || n <= 0 || n % 64 != 0 || out > INT32_MAX || n > INT32_MAX || M > INT32_MAX)
-    return VQ2_ERR_SHAPE;
-  if (x_row_stride < n || y_row_stride < out) return VQ2_ERR_SHAPE;
-  if (!aligned(idx0, 16) || !aligned(cb0, 16) || (cb1 && !aligned(cb1, 16)) || (idx1 && !aligned(idx1, 8)))
-    return VQ2_ERR_ALIGN;
-  GemvArgs a{};
-  a.x = xr; a.x_dtype = x_dtype; a.x_row_stride = x_row_stride; a.x_k_stride = 0; a.x_k_div = 1;
-  a.M = (int)M;
-  a.idx0 = idx0; a.idx1 = idx1; a.cb0 = cb0; a.cb1 = cb1; a.scale = scale;
-  a.y = y; a.y_dtype = y_dtype; a.y_row_stride = y_row_stride; a.y_k_stride = 0;
-  a.e_ids = nullptr; a.num_experts = 1; a.idx_e_stride = 0; a.scale_e_stride = 0;
-  a.out = (int)out; a.n = (int)n; a.rs = rs;
-  return run_gemv(a, 1, idx1 != nullptr, val_dtype, static_cast<cudaStream_t>(stream));
+  if (out <= 0) return VQ2_ERR_SHAPE;
+  if (y_row_stride < out) return VQ2_ERR_SHAPE;
+  void* yp[1] = {y};
+  const void* sp[1] = {scale};
+  const int16_t* i0p[1] = {idx0};
+  const uint8_t* i1p[1] = {idx1};
+  const int64_t op[1] = {out};
+  return vq2_gemv_multi(xr, x_dtype, VQ2_ACT_ROTATED, M, x_row_stride, nullptr, nullptr, 0, 1.f, 1, i0p,
+                        idx1 ? i1p : nullptr, op, sp, cb0, cb1, val_dtype, yp, y_dtype, y_row_stride, n, rs, stream);
 }
 
-extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int64_t x_k_stride, int64_t x_k_div,
+extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_stride, int64_t x_k_div,
+                            const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
                             const int32_t* e_ids, int64_t K, int64_t num_experts, const int16_t* idx,
                             const void* cb0, const void* scale, int val_dtype, void* y, int y_dtype,
                             int64_t out, int64_t ng, float rs, void* stream) {
@@ -304,13 +597,15 @@ extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int64_t x_k_stride, int6
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQ2_ERR_DTYPE;
   if (K <= 0 || num_experts <= 0 || out <= 0 || ng <= 0 || ng % 8 != 0 || out > INT32_MAX || ng * 8 > INT32_MAX)
     return VQ2_ERR_SHAPE;
-  if (x_k_stride < 0 || x_k_div <= 0) return VQ2_ERR_SHAPE;
+  if (x_k_stride < 0 || x_k_div <= 0 || K > INT32_MAX) return VQ2_ERR_SHAPE;
   if (!aligned(idx, 16) || !aligned(cb0, 16)) return VQ2_ERR_ALIGN;
   GemvArgs a{};
-  a.x = x; a.x_dtype = x_dtype; a.x_row_stride = 0; a.x_k_stride = x_k_stride; a.x_k_div = x_k_div; a.M = 1;
+  a.nprob = 0;
+  a.x = x; a.x_dtype = x_dtype; a.x_mode = x_mode; a.x_row_stride = 0; a.x_k_stride = x_k_stride;
+  a.x_k_div = x_k_div; a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale; a.M = 1;
   a.idx0 = idx; a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr; a.scale = scale;
   a.y = y; a.y_dtype = y_dtype; a.y_row_stride = 0; a.y_k_stride = out;
   a.e_ids = e_ids; a.num_experts = num_experts; a.idx_e_stride = out * ng; a.scale_e_stride = out;
-  a.out = (int)out; a.n = (int)(ng * 8); a.rs = rs;
-  return run_gemv(a, (int)K, false, val_dtype, static_cast<cudaStream_t>(stream));
+  a.out = (int)out; a.n = (int)(ng * 8); a.rs = rs; a.K = (int)K;
+  return run_gemv(a, out * K, false, val_dtype, static_cast<cudaStream_t>(stream));
 }

@@ -13,8 +13,11 @@ because its codebooks are bf16); xr may be fp32/fp16/bf16; any number of leading
 is accepted by the dense GEMVs (the reference's Triton path is batch-1 only).
 
 Extra entry points used by the runtime: ``vq_gemv`` (batched, any output dtype),
-``moe_gemv``, ``swiglu_rht`` and ``moe_combine``.
+``gemv_multi`` (several matrices sharing one activation, with the input RHT or SwiGLU+RHT
+fused into the kernel prologue), ``moe_gemv``, ``swiglu_rht`` and ``moe_combine``.
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -92,12 +95,77 @@ def _ids32(ids):
     return ids.contiguous()
 
 
-def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.0):
-    """Expert-indexed GEMV: y[k] = rs * scale[e_k] * sum cb16[idx[e_k]] . x[k // x_k_div]."""
+def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=None, ys=None, y_row_stride=None):
+    """P <= 8 VQ matrices sharing one activation in ONE launch.
+
+    x: [..., n] (mode SWIGLU_RHT: fp32 [..., 2n]); mats: list of (idx0 int16 [out_p, n/8],
+    idx1 uint8 or None, scale [out_p]); rot: a vq.Rot applied in-kernel when mode is RHT or
+    SWIGLU_RHT (default: RHT when rot is given). Returns the list of outputs [..., out_p]
+    (or writes the given ``ys``)."""
+    if not 1 <= len(mats) <= 8:
+        raise ValueError("gemv_multi takes 1..8 matrices")
+    _lib.require_cuda(x, cb0, cb1)
+    if mode is None:
+        mode = _lib.VQ2_ACT_RHT if rot is not None else _lib.VQ2_ACT_ROTATED
+    ng = mats[0][0].shape[1]
+    n = ng * 8
+    xin = 2 * n if mode == _lib.VQ2_ACT_SWIGLU_RHT else n
+    if x.shape[-1] != xin:
+        raise ValueError(f"activation last dim {x.shape[-1]} != {xin}")
+    if mode != _lib.VQ2_ACT_ROTATED and (rot is None or rot.n != n):
+        raise ValueError("a rotation of size n is required for modes RHT / SWIGLU_RHT")
+    x2 = x.reshape(-1, xin)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    res = mats[0][1] is not None
+    _check_vals(cb0, cb1 if res else None, *[m[2] for m in mats])
+    i0s, i1s, scs, outs = [], [], [], []
+    for i0, i1, sc in mats:
+        _lib.require_cuda(i0, i1, sc)
+        if i0.dtype != torch.int16 or i0.shape[1] != ng or (i1 is not None) != res:
+            raise ValueError("matrices must share n and bpw; stage-1 indices are int16")
+        if i1 is not None and (i1.dtype != torch.uint8 or i1.shape != i0.shape):
+            raise ValueError("residual indices must be uint8 [out, n/8]")
+        i0s.append(_c(i0)); i1s.append(_c(i1)); scs.append(_c(sc)); outs.append(i0.shape[0])
+    out_dtype = out_dtype or cb0.dtype
+    if ys is None:
+        ys = [torch.empty(*x.shape[:-1], o, dtype=out_dtype, device=x.device) for o in outs]
+        y_row_stride = None
+    if y_row_stride is None:
+        if M > 1 and len(set(outs)) > 1:
+            raise ValueError("matrices of different heights need an explicit y_row_stride for M > 1")
+        y_row_stride = outs[0]
+    for y, o in zip(ys, outs):
+        if y.dtype != out_dtype or y.stride(-1) != 1:
+            raise ValueError("outputs must have dtype out_dtype and unit inner stride")
+        if y.numel() < o or (M > 1 and (y.dim() < 2 or y.shape[-2] < M)):
+            raise ValueError("output too small")
+    P = len(mats)
+    _lib.call("vq2_gemv_multi", _lib.ptr(x2), _lib.dtype_code(x2), int(mode), M, x2.stride(0),
+              _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
+              int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0, P,
+              _lib.ptr_array(ctypes.c_void_p, [i.data_ptr() for i in i0s]),
+              _lib.ptr_array(ctypes.c_void_p, [i.data_ptr() for i in i1s]) if res else None,
+              _lib.ptr_array(ctypes.c_int64, outs),
+              _lib.ptr_array(ctypes.c_void_p, [t.data_ptr() for t in scs]),
+              _lib.ptr(cb0), _lib.ptr(cb1) if res else None, _lib.dtype_code(cb0),
+              _lib.ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), _lib.dtype_code(ys[0]),
+              int(y_row_stride), n, float(rs), _lib.stream_ptr(x.device))
+    return ys
+
+
+def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.0, rot=None, mode=None):
+    """Expert-indexed GEMV: y[k] = rs * scale[e_k] * sum cb16[idx[e_k]] . act(x[k // x_k_div]).
+
+    ``act`` is the identity (mode ROTATED), the forward RHT ``rot`` (mode RHT) or SwiGLU then
+    ``rot`` (mode SWIGLU_RHT, x rows fp32 [gate | up])."""
     _lib.require_cuda(x, ids, pool_idx, cb16, pool_scale, y)
     if pool_idx.dtype != torch.int16 or pool_idx.dim() != 3:
         raise ValueError("pool_idx must be int16 [E, OUT, NG]")
     _check_vals(cb16, pool_scale)
+    if mode is None:
+        mode = _lib.VQ2_ACT_RHT if rot is not None else _lib.VQ2_ACT_ROTATED
     E, OUT, NG = pool_idx.shape
     ids = _ids32(ids)
     K = ids.numel()
@@ -105,12 +173,16 @@ def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.
         raise ValueError(f"y must be contiguous with at least [{K}, {OUT}] elements")
     if not x.is_contiguous():
         raise ValueError("x must be contiguous")
+    if mode != _lib.VQ2_ACT_ROTATED and (rot is None or rot.n != NG * 8):
+        raise ValueError("a rotation of size n is required for modes RHT / SWIGLU_RHT")
     pool_idx, pool_scale = _c(pool_idx), _c(pool_scale)
     if pool_scale.numel() != E * OUT:
         raise ValueError("pool_scale must be [E, OUT]")
-    _lib.call("vq2_moe_gemv", _lib.ptr(x), _lib.dtype_code(x), int(x_k_stride), int(x_k_div), _lib.ptr(ids), K, E,
-              _lib.ptr(pool_idx), _lib.ptr(cb16), _lib.ptr(pool_scale), _lib.dtype_code(cb16), _lib.ptr(y),
-              _lib.dtype_code(y), OUT, NG, float(rs), _lib.stream_ptr(x.device))
+    _lib.call("vq2_moe_gemv", _lib.ptr(x), _lib.dtype_code(x), int(mode), int(x_k_stride), int(x_k_div),
+              _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
+              int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0,
+              _lib.ptr(ids), K, E, _lib.ptr(pool_idx), _lib.ptr(cb16), _lib.ptr(pool_scale), _lib.dtype_code(cb16),
+              _lib.ptr(y), _lib.dtype_code(y), OUT, NG, float(rs), _lib.stream_ptr(x.device))
     return y
 
 
@@ -156,3 +228,22 @@ def moe_combine(y, w, top_k, add=None, out=None, out_dtype=torch.float16):
     _lib.call("vq2_moe_combine", _lib.ptr(y), _lib.ptr(w), T, top_k, H, _lib.ptr(add), _lib.ptr(out),
               _lib.dtype_code(out), _lib.stream_ptr(y.device))
     return out
+
+
+def gather_rate(cb, iters=256, blocks_per_sm=8, reps=5):
+    """Measured random 16-byte codebook-row gathers per second on cb's device (diagnostic)."""
+    _lib.require_cuda(cb)
+    dev = cb.device
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * blocks_per_sm
+    sink = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = _lib.stream_ptr(dev)
+    args = (_lib.ptr(cb), cb.shape[0], blocks, iters, _lib.ptr(sink), st)
+    _lib.call("vq2_gather_probe", *args)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        _lib.call("vq2_gather_probe", *args)
+    e1.record()
+    e1.synchronize()
+    return reps * blocks * 256 * iters * 8 / (e0.elapsed_time(e1) / 1e3)

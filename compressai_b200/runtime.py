@@ -1,11 +1,11 @@
 """Compressed-weight decode runtime, mirroring reference ``vq2/runtime.py``.
 
 ``PackedLinear`` is a drop-in ``nn.Linear`` whose weight stays VQ-compressed in HBM. Its
-forward rotates the input once with the fp32 RHT kernel (cached per input tensor, like
-the reference's ``FastRot``) and runs the codebook-decode GEMV kernel for any number of rows
-M (the reference's fused path is batch-1 only, vq2/runtime.py:92; larger M fall back to
-dequantize-then-matmul there, :105-110). Scales and codebooks stay in their container dtype
-(fp16); the output takes the input's dtype.
+forward is ONE kernel launch: the fp32 input rotation runs in the GEMV kernel's prologue, then
+the codebook-decode GEMV, for any number of rows M (the reference's fused path is batch-1 only,
+vq2/runtime.py:92; larger M fall back to dequantize-then-matmul there, :105-110). Scales and
+codebooks stay in their container dtype (fp16); the output takes the input's dtype.
+``PackedLinearGroup`` runs modules that share an input (q/k/v, gate/up) as one launch.
 """
 import os
 
@@ -106,17 +106,73 @@ class PackedLinear(nn.Module):
             rec = g if rec is None else rec + g
         return rec.reshape(r1 - r0, self.n) * self.scale[r0:r1, None]
 
-    def forward(self, x):
-        xr = rotate_cached(self.rot, x)
+    def mat(self):
+        return (self.idx0, getattr(self, "idx1", None), self.scale)
+
+    def codebooks(self):
         cbs = self._cbs[0]
+        return cbs[self.keys[0]], (cbs[self.keys[1]] if len(self.keys) > 1 else None)
+
+    def forward(self, x):
+        """y = x W^T: the input rotation runs in the GEMV kernel's prologue (fp32), one launch."""
+        cb0, cb1 = self.codebooks()
         out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float16
-        if self.cfg == (16, 8):
-            return kernels.vq_gemv(xr, self.idx0, cbs[self.keys[0]], self.scale, i1=self.idx1,
-                                   cb1=cbs[self.keys[1]], out_dtype=out_dtype)
-        return kernels.vq_gemv(xr, self.idx0, cbs[self.keys[0]], self.scale, out_dtype=out_dtype)
+        return kernels.gemv_multi(x, [self.mat()], cb0, cb1, rot=self.rot, out_dtype=out_dtype)[0]
 
     def nbytes(self):
         return sum(b.numel() * b.element_size() for b in self.buffers())
+
+
+class PackedLinearGroup:
+    """Several PackedLinear modules that read the same input (q/k/v, gate/up) run as ONE
+    multi-matrix launch: one input rotation per CTA, one launch instead of one per matrix.
+    The modules must share n, cfg, rotation tag and codebooks."""
+
+    def __init__(self, mods):
+        if not 1 <= len(mods) <= 8:
+            raise ValueError("a group holds 1..8 modules")
+        m0 = mods[0]
+        for m in mods[1:]:
+            if (m.n, m.cfg, m.rot) != (m0.n, m0.cfg, m0.rot) or m._cbs[0] is not m0._cbs[0]:
+                raise ValueError("grouped modules must share n, cfg, rotation and codebooks")
+        self.mods = list(mods)
+
+    def __call__(self, x, out_dtype=None):
+        m0 = self.mods[0]
+        cb0, cb1 = m0.codebooks()
+        out_dtype = out_dtype or (x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32)
+                                  else torch.float16)
+        return kernels.gemv_multi(x, [m.mat() for m in self.mods], cb0, cb1, rot=m0.rot, out_dtype=out_dtype)
+
+
+class PackedSwiGLUMLP(nn.Module):
+    """down(silu(gate(x)) * up(x)) over PackedLinear weights in TWO launches: gate and up as
+    one multi-matrix GEMV (input RHT in its prologue, fp32 [M, 2I] output), then down with the
+    SwiGLU and its input RHT in the prologue. Same math as the Qwen MLP block the reference
+    wraps (transformers Qwen3_5MoeMLP; vq2/paged_runtime.py:501-504 for the expert form)."""
+
+    def __init__(self, gate, up, down):
+        super().__init__()
+        if gate.out != up.out or down.n != gate.out:
+            raise ValueError("gate/up rows must equal down's input size")
+        self.gate, self.up, self.down = gate, up, down
+        self._gu = PackedLinearGroup([gate, up])
+
+    def forward(self, x):
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        M, inter = x2.shape[0], self.gate.out
+        gu = torch.empty(M, 2 * inter, dtype=torch.float32, device=x.device)
+        m0 = self.gate
+        cb0, cb1 = m0.codebooks()
+        kernels.gemv_multi(x2, [self.gate.mat(), self.up.mat()], cb0, cb1, rot=m0.rot, out_dtype=torch.float32,
+                           ys=[gu, gu[:, inter:]], y_row_stride=2 * inter)
+        d = self.down
+        cbd0, cbd1 = d.codebooks()
+        out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float16
+        y = kernels.gemv_multi(gu, [d.mat()], cbd0, cbd1, rot=d.rot, mode=kernels._lib.VQ2_ACT_SWIGLU_RHT,
+                               out_dtype=out_dtype)[0]
+        return y.reshape(*lead, d.out)
 
 
 class PackedEmbedding(nn.Module):

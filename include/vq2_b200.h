@@ -81,13 +81,34 @@ VQ2_API int vq2_swiglu_rht(const float* gu, int64_t gu_row_stride, int64_t M, in
                            int64_t hb, const int32_t* perm, const int8_t* sign, float out_scale,
                            float* xr, int64_t xr_row_stride, void* stream);
 
+/* activation operand modes of the GEMV entry points */
+#define VQ2_ACT_ROTATED 0     /* x is already rotated; used as is */
+#define VQ2_ACT_RHT 1         /* x is raw; the forward RHT (perm, sign, hb, rot_scale) runs in-kernel */
+#define VQ2_ACT_SWIGLU_RHT 2  /* x rows are fp32 [gate | up] of 2n: silu(gate) * up, then forward RHT */
+
 /*
- * VQ GEMV on a pre-rotated activation (fp32 accumulation):
+ * VQ GEMV of P <= 8 matrices sharing one activation (fp32 accumulation):
+ *   xr = act(x)                      (per x_mode: as is / RHT / SwiGLU then RHT, fp32)
+ *   y_p[m, r] = rs * scale_p[r] * sum_g dot(cb0[idx0_p[r, g]] (+ cb1[idx1_p[r, g]]), xr[m, 8g:8g+8])
+ * x: [M, n] (mode SWIGLU_RHT: fp32 [M, 2n]) in x_dtype, row stride x_row_stride; idx0_p: int16
+ * [out_p, n/8]; idx1_p: uint8 [out_p, n/8] (3 bpw, all or none); cb0: [65536, 8]; cb1: [256, 8]
+ * or NULL; scale_p: [out_p]; the codebooks and scales in val_dtype (fp16/bf16); y_p: [M, out_p]
+ * in y_dtype with row stride y_row_stride. idx0, idx1, out, scale and y are HOST arrays of P
+ * device pointers / sizes. n % 64 == 0; idx0_p, cb0, cb1 16-byte aligned, idx1_p 8-byte aligned.
+ * Replaces: the per-matrix FastRot + vq_gemv_16 / vq_gemv_16_8 sequence of PackedLinear.forward
+ * (vq2/runtime.py:91-104, vq2/kernels.py:32-78, 215-230), fused and batched over matrices
+ * that read the same input (q/k/v, gate/up), for any number of rows M.
+ */
+VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,
+                           const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
+                           int64_t P, const int16_t* const* idx0, const uint8_t* const* idx1,
+                           const int64_t* out, const void* const* scale, const void* cb0,
+                           const void* cb1, int val_dtype, void* const* y, int y_dtype,
+                           int64_t y_row_stride, int64_t n, float rs, void* stream);
+
+/*
+ * VQ GEMV on a pre-rotated activation, one matrix (vq2_gemv_multi with P = 1, mode ROTATED):
  *   y[m, r] = rs * scale[r] * sum_g dot(cb0[idx0[r, g]] (+ cb1[idx1[r, g]]), xr[m, 8g:8g+8])
- * xr: [M, n] in x_dtype (row stride x_row_stride); idx0: int16 [out, n/8]; idx1: uint8
- * [out, n/8] or NULL (2 bpw); cb0: [65536, 8]; cb1: [256, 8] or NULL; scale: [out], all
- * three in val_dtype (fp16/bf16); y: [M, out] in y_dtype (row stride y_row_stride).
- * n % 64 == 0; idx0, cb0, cb1 16-byte aligned, idx1 8-byte aligned.
  * Replaces: vq_gemv_16 / vq_gemv_16_8 (vq2/kernels.py:215-230) and the Triton kernels
  * _vq_gemv_16 / _vq_gemv_16_8 (vq2/kernels.py:32-78), which handle M = 1 only.
  */
@@ -98,17 +119,19 @@ VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_strid
 
 /*
  * Expert-indexed VQ GEMV over K problems (2 bpw):
- *   y[k, r] = rs * scale[e_k, r] * sum_g dot(cb0[idx[e_k, r, g]], x_k[8g:8g+8])
- *   e_k = e_ids[k],  x_k = x + (k / x_k_div) * x_k_stride
- * x_k_stride = 0 shares one activation among all problems (gate_up of one token);
- * x_k_div = top_k maps problem t*top_k + j to token t. e_ids: int32 [K] device (slots of a
- * paged pool or ids of a resident pool; ids outside [0, num_experts) give zero rows).
- * idx: int16 [num_experts, out, ng]; scale: [num_experts, out] in val_dtype; y: [K, out] in
- * y_dtype. ng % 8 == 0; idx and cb0 16-byte aligned.
+ *   xr_k = act(x + (k / x_k_div) * x_k_stride)        (per x_mode, as in vq2_gemv_multi)
+ *   y[k, r] = rs * scale[e_k, r] * sum_g dot(cb0[idx[e_k, r, g]], xr_k[8g:8g+8]),  e_k = e_ids[k]
+ * x_k_stride = 0 shares one activation among all problems (gate_up of one token); x_k_div =
+ * top_k maps problem t*top_k + j to token t. e_ids: int32 [K] device (slots of a paged pool or
+ * ids of a resident pool; ids outside [0, num_experts) give zero rows). idx: int16
+ * [num_experts, out, ng]; scale: [num_experts, out] in val_dtype; y: [K, out] in y_dtype.
+ * ng % 8 == 0; idx and cb0 16-byte aligned.
  * Replaces: vq_moe_parallel_gate_up / vq_moe_parallel_down (vq2/kernels.py:246-264) and
- * _parallel_moe_gate_up_kernel / _parallel_moe_down_kernel (vq2/kernels.py:117-176).
+ * _parallel_moe_gate_up_kernel / _parallel_moe_down_kernel (vq2/kernels.py:117-176), plus the
+ * rot_2048.fwd / SwiGLU / rot_512.fwd torch ops around them (vq2/paged_runtime.py:495-504).
  */
-VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int64_t x_k_stride, int64_t x_k_div,
+VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_stride, int64_t x_k_div,
+                         const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
                          const int32_t* e_ids, int64_t K, int64_t num_experts, const int16_t* idx,
                          const void* cb0, const void* scale, int val_dtype, void* y, int y_dtype,
                          int64_t out, int64_t ng, float rs, void* stream);
@@ -123,6 +146,15 @@ VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int64_t x_k_stride, int64_t
  */
 VQ2_API int vq2_moe_combine(const float* y, const float* w, int64_t T, int64_t top_k,
                             int64_t H, const float* add, void* out, int out_dtype, void* stream);
+
+/*
+ * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of rows
+ * [0, rows) of cb (uniform row indices, the load form the GEMV uses). Timing it gives the
+ * random codebook-gather rate that bounds the M = 1 VQ GEMV. sink: one uint32 of device memory.
+ * No reference counterpart (measurement aid).
+ */
+VQ2_API int vq2_gather_probe(const void* cb, int64_t rows, int64_t blocks, int64_t iters,
+                             uint32_t* sink, void* stream);
 
 #ifdef __cplusplus
 }

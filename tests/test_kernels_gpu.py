@@ -202,3 +202,108 @@ def test_moe_combine():
     out = kernels.moe_combine(y, w, K, add=add, out_dtype=torch.float32)
     ref = (y.view(T, K, H).double() * w.double()[:, :, None]).sum(1) + add.double()
     assert rel_err(out.cpu(), ref.cpu()) < 1e-6
+
+
+# ------------------------------------------------------------------ fused prologues / multi
+def _dev_mat(idx, scale, dtype=torch.float16):
+    i0 = torch.from_numpy(np.ascontiguousarray(idx[0])).to(DEV)
+    i1 = torch.from_numpy(np.ascontiguousarray(idx[1])).to(DEV) if len(idx) > 1 else None
+    return (i0, i1, torch.from_numpy(np.asarray(scale)).to(DEV, dtype))
+
+
+def test_packed_linear_fused_rht_golden(cbs):
+    """PackedLinear.forward (RHT fused in the GEMV prologue) on the reference-quantized cases."""
+    from compressai_b200 import runtime
+    d = golden("gemv.npz")
+    cbd = dev_cbs(cbs)
+    names = sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_meta")})
+    for nm in names:
+        out, n, nst, M = d[f"{nm}_meta"]
+        cfg = (16,) if nst == 1 else (16, 8)
+        idx = [torch.from_numpy(d[f"{nm}_idx0"])] + ([torch.from_numpy(d[f"{nm}_idx1"])] if nst > 1 else [])
+        lin = runtime.PackedLinear((int(out), int(n)), cfg, str(d[f"{nm}_tag"]), idx,
+                                   torch.from_numpy(d[f"{nm}_scale"]), cbd, DEV)
+        y = lin(torch.from_numpy(d[f"{nm}_x"]).to(DEV)).float().cpu().numpy()
+        assert rel_err(y, d[f"{nm}_y"]) < TOL_F16, nm
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("bits", [(16,), (16, 8)])
+def test_gemv_multi_shared_input(cbs, M, bits):
+    """q/k/v-style group: 3 matrices of different heights, one input, one launch."""
+    from compressai_b200 import runtime
+    cbd = dev_cbs(cbs)
+    outs = [2048, 512, 768]
+    mods = []
+    mats_np = []
+    for j, o in enumerate(outs):
+        idx, scale = synth.random_matrix(100 + j, o, 2048, bits)
+        mats_np.append((idx, scale))
+        mods.append(runtime.PackedLinear((o, 2048), bits, "attn_in", [torch.from_numpy(i) for i in idx],
+                                         torch.from_numpy(scale), cbd, DEV))
+    x = np.random.default_rng(M).standard_normal((M, 2048)).astype(np.float16)
+    ys = runtime.PackedLinearGroup(mods)(torch.from_numpy(x).to(DEV)) if M == 1 else \
+        [m(torch.from_numpy(x).to(DEV)) for m in mods]
+    perm, sign, hb = O.rot_params("attn_in", 2048)
+    for (idx, scale), y in zip(mats_np, ys):
+        ref = O.gemv_ref(x, idx, bits, cbs, scale, perm, sign, hb)
+        assert rel_err(y.float().cpu().numpy().reshape(ref.shape), ref) < TOL_F16
+    if M > 1:  # grouped with an explicit output row stride
+        yb = torch.empty(M, sum(outs), device=DEV, dtype=torch.float16)
+        offs = np.cumsum([0] + outs)
+        cb0, cb1 = mods[0].codebooks()
+        kernels.gemv_multi(torch.from_numpy(x).to(DEV), [m.mat() for m in mods], cb0, cb1, rot=mods[0].rot,
+                           ys=[yb[:, offs[j]:offs[j + 1]] for j in range(3)], y_row_stride=sum(outs))
+        for j, (idx, scale) in enumerate(mats_np):
+            ref = O.gemv_ref(x, idx, bits, cbs, scale, perm, sign, hb)
+            assert rel_err(yb[:, offs[j]:offs[j + 1]].float().cpu().numpy(), ref) < TOL_F16
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_packed_swiglu_mlp(cbs, M):
+    from compressai_b200 import runtime
+    cbd = dev_cbs(cbs)
+    gi, gs = synth.random_matrix(1, 6144, 2048)
+    ui, us = synth.random_matrix(2, 6144, 2048)
+    di, ds = synth.random_matrix(3, 2048, 6144)
+    mk = lambda idx, sc, o, n, tag: runtime.PackedLinear((o, n), (16,), tag, [torch.from_numpy(idx[0])],
+                                                         torch.from_numpy(sc), cbd, DEV)
+    mlp = runtime.PackedSwiGLUMLP(mk(gi, gs, 6144, 2048, "mlp_in"), mk(ui, us, 6144, 2048, "mlp_in"),
+                                  mk(di, ds, 2048, 6144, "mlp_down"))
+    x = np.random.default_rng(7).standard_normal((M, 2048)).astype(np.float16)
+    y = mlp(torch.from_numpy(x).to(DEV)).float().cpu().numpy()
+    r_in = O.rot_params("mlp_in", 2048)
+    g = O.gemv_ref(x, gi, (16,), cbs, gs, *r_in)
+    u = O.gemv_ref(x, ui, (16,), cbs, us, *r_in)
+    ref = O.gemv_ref(O.silu(g) * u, di, (16,), cbs, ds, *O.rot_params("mlp_down", 6144))
+    assert rel_err(y, ref) < TOL_F16
+
+
+def test_moe_gemv_fused_modes(cbs):
+    """Expert-indexed GEMVs with the RHT (gate_up) and SwiGLU+RHT (down) prologues."""
+    E = 10
+    gu_i, gu_s, dn_i, dn_s = _pool(E, 5)
+    cbd = dev_cbs(cbs)
+    r2048 = vq.get_rot("moe_expert_2048", 2048, DEV)
+    r512 = vq.get_rot("moe_expert_512", 512, DEV)
+    T, K = 3, 4
+    ids = np.array([[1, 4, 9, 0], [4, 4, 2, 7], [3, 8, 5, 6]], dtype=np.int32)
+    h = np.random.default_rng(3).standard_normal((T, 2048)).astype(np.float16)
+    ids_d = torch.from_numpy(ids.reshape(-1)).to(DEV)
+    gu = torch.empty(T * K, 1024, device=DEV)
+    kernels.moe_gemv(torch.from_numpy(h).to(DEV), ids_d, torch.from_numpy(gu_i).to(DEV), cbd["16"],
+                     torch.from_numpy(gu_s).to(DEV), gu, x_k_stride=2048, x_k_div=K, rot=r2048)
+    y_dn = torch.empty(T * K, 2048, device=DEV)
+    kernels.moe_gemv(gu, ids_d, torch.from_numpy(dn_i).to(DEV), cbd["16"], torch.from_numpy(dn_s).to(DEV), y_dn,
+                     x_k_stride=1024, rot=r512, mode=2)
+    rot2048 = O.rot_params("moe_expert_2048", 2048)
+    rot512 = O.rot_params("moe_expert_512", 512)
+    for t in range(T):
+        xr = O.rht_fwd(h[t].astype(np.float64), *rot2048)
+        for j in range(K):
+            e = ids[t, j]
+            g = O.vq_gemv_legacy(xr, gu_i[e], cbs["16"], gu_s[e], 1.0)
+            assert rel_err(gu[t * K + j].cpu().numpy(), g) < 2e-5
+            act_r = O.rht_fwd(O.silu(g[:512]) * g[512:], *rot512)
+            ref = O.vq_gemv_legacy(act_r, dn_i[e], cbs["16"], dn_s[e], 1.0)
+            assert rel_err(y_dn[t * K + j].cpu().numpy(), ref) < 2e-5
