@@ -1,0 +1,186 @@
+"""The paged ``.vq2m`` expert container: layout, parsing and writing.
+
+Layout (identical to the reference so files interchange; reference vq2/pack_35b_to_vq2m.py:
+22-35, 58, 138-152, 200-247 and the reader vq2/paged_runtime.py:89-123):
+
+* 64-byte header ``<4sHHHH QQQQQ 12s>``: magic ``VQ2M``, version 1, num_layers, num_experts,
+  pad, moe_table_off (64), moe_table_len, meta_json_off, meta_json_len, payload_start
+  (2 MiB), 12 pad bytes;
+* expert table of num_layers x num_experts entries ``<QIQIQIQI>`` (48 B):
+  (offset, size) of gate_up indices (int16), gate_up scales (fp16), down indices (int16),
+  down scales (fp16);
+* UTF-8 JSON meta (dims ``gu_rows``/``gu_cols``/``dn_rows``/``dn_cols``, optional
+  ``other_tensors`` and ``expert_modes``);
+* payload from 2 MiB: per layer, per expert, the four tensors back to back, so one expert is a
+  single contiguous record of ``expert_bytes`` bytes (792,576 B at the 35B-A3B shape).
+"""
+import json
+import os
+import struct
+
+import numpy as np
+
+from . import synth
+
+MAGIC = b"VQ2M"
+VERSION = 1
+HEADER_FMT = "<4sHHHH QQQQQ 12s"
+ENTRY_FMT = "<QIQIQIQI"
+HEADER_SIZE = struct.calcsize(HEADER_FMT)       # 64
+ENTRY_SIZE = struct.calcsize(ENTRY_FMT)         # 48
+RESERVED_HEADER_BYTES = 2 * 1024 * 1024
+DEFAULT_DIMS = dict(gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64)
+
+
+def record_bytes(gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64):
+    return gu_rows * gu_cols * 2 + gu_rows * 2 + dn_rows * dn_cols * 2 + dn_rows * 2
+
+
+class Vq2mLayout:
+    """Parsed header, table and meta of a .vq2m image (bytes-like or file head)."""
+
+    def __init__(self, num_layers, num_experts, payload_start, table, meta):
+        self.num_layers = num_layers
+        self.num_experts = num_experts
+        self.payload_start = payload_start
+        self.table = table          # [layer][expert] -> 8-tuple
+        self.meta = meta
+        self.gu_rows = meta.get("gu_rows", 1024)
+        self.gu_cols = meta.get("gu_cols", 256)
+        self.dn_rows = meta.get("dn_rows", 2048)
+        self.dn_cols = meta.get("dn_cols", 64)
+
+    @property
+    def expert_bytes(self):
+        return record_bytes(self.gu_rows, self.gu_cols, self.dn_rows, self.dn_cols)
+
+    def record(self, layer, expert):
+        """(offset, nbytes) of the contiguous record of one expert; raises if the four tensors
+        are not back to back (a file the paging fast path cannot serve with one copy)."""
+        og, sg, os_, ss, od, sd, ods, sds = self.table[layer][expert]
+        if sg == 0:
+            raise ValueError(f"expert ({layer}, {expert}) missing from the container")
+        if not (os_ == og + sg and od == os_ + ss and ods == od + sd):
+            raise ValueError(f"expert ({layer}, {expert}) is not stored contiguously")
+        return og, sg + ss + sd + sds
+
+
+def parse_header(head, file_size=None):
+    """Parse header + table + meta from the first bytes of a .vq2m (at least payload_start
+    bytes, or the whole image). Raises ValueError on a bad magic/version or out-of-range
+    offsets."""
+    head = memoryview(head)
+    if len(head) < HEADER_SIZE:
+        raise ValueError("truncated .vq2m header")
+    (magic, version, nl, ne, _, toff, tlen, moff, mlen, pstart, _) = struct.unpack(HEADER_FMT, head[:HEADER_SIZE])
+    if magic != MAGIC or version != VERSION:
+        raise ValueError("invalid .vq2m file or incompatible version")
+    if tlen != nl * ne * ENTRY_SIZE or toff + tlen > len(head) or moff + mlen > len(head):
+        raise ValueError("corrupt .vq2m header: table/meta outside the header region")
+    ents = list(struct.iter_unpack(ENTRY_FMT, head[toff:toff + tlen]))
+    table = [ents[ln * ne:(ln + 1) * ne] for ln in range(nl)]
+    meta = json.loads(bytes(head[moff:moff + mlen]).decode("utf-8"))
+    lay = Vq2mLayout(nl, ne, pstart, table, meta)
+    if file_size is not None:
+        for row in table:
+            for (og, sg, os_, ss, od, sd, ods, sds) in row:
+                if sg and max(og + sg, os_ + ss, od + sd, ods + sds) > file_size:
+                    raise ValueError("corrupt .vq2m: expert record beyond end of file")
+    return lay
+
+
+def _header_bytes(num_layers, num_experts, table, meta):
+    meta_b = json.dumps(meta).encode("utf-8")
+    tbl = bytearray()
+    for ln in range(num_layers):
+        for e in range(num_experts):
+            tbl += struct.pack(ENTRY_FMT, *table[ln][e])
+    toff = HEADER_SIZE
+    moff = toff + len(tbl)
+    if moff + len(meta_b) > RESERVED_HEADER_BYTES:
+        raise RuntimeError("header exceeds the reserved 2 MiB")
+    hdr = struct.pack(HEADER_FMT, MAGIC, VERSION, num_layers, num_experts, 0, toff, len(tbl), moff, len(meta_b),
+                      RESERVED_HEADER_BYTES, b"\x00" * 12)
+    out = bytearray(RESERVED_HEADER_BYTES)
+    out[:HEADER_SIZE] = hdr
+    out[toff:moff] = tbl
+    out[moff:moff + len(meta_b)] = meta_b
+    return bytes(out)
+
+
+def _table_and_meta(num_layers, num_experts, dims, meta_extra):
+    gr, gc, dr, dc = dims["gu_rows"], dims["gu_cols"], dims["dn_rows"], dims["dn_cols"]
+    sz = (gr * gc * 2, gr * 2, dr * dc * 2, dr * 2)
+    rec = sum(sz)
+    table = []
+    off = RESERVED_HEADER_BYTES
+    for ln in range(num_layers):
+        row = []
+        for e in range(num_experts):
+            o1 = off
+            o2 = o1 + sz[0]
+            o3 = o2 + sz[1]
+            o4 = o3 + sz[2]
+            row.append((o1, sz[0], o2, sz[1], o3, sz[2], o4, sz[3]))
+            off += rec
+        table.append(row)
+    meta = dict(num_layers=num_layers, num_experts=num_experts, hidden_dim=gc * 8, intermediate_dim=gr // 2,
+                other_tensors={}, **dims)
+    if meta_extra:
+        meta.update(meta_extra)
+    return table, meta, off
+
+
+def write_vq2m(path, num_layers, num_experts, expert_fn, dims=None, meta_extra=None):
+    """Write a .vq2m whose expert (layer, e) is ``expert_fn(layer, e)`` = (gu_idx int16,
+    gu_scale fp16, dn_idx int16, dn_scale fp16). Returns the file size."""
+    dims = dict(DEFAULT_DIMS, **(dims or {}))
+    table, meta, end = _table_and_meta(num_layers, num_experts, dims, meta_extra)
+    with open(path, "wb") as f:
+        f.write(_header_bytes(num_layers, num_experts, table, meta))
+        for ln in range(num_layers):
+            for e in range(num_experts):
+                gi, gs, di, ds = expert_fn(ln, e)
+                for a, dt in ((gi, np.int16), (gs, np.float16), (di, np.int16), (ds, np.float16)):
+                    f.write(np.ascontiguousarray(a, dtype=dt).tobytes())
+    return end
+
+
+def write_synthetic_vq2m(path, num_layers, num_experts, seed=0, **dims):
+    """Container of seeded synthetic experts (compressai_b200.synth.synth_expert, data seed
+    seed * 1_000_003 + layer)."""
+    d = dict(DEFAULT_DIMS, **dims)
+    return write_vq2m(path, num_layers, num_experts,
+                      lambda ln, e: synth.synth_expert(seed * 1_000_003 + ln, e, d["gu_rows"], d["gu_cols"],
+                                                       d["dn_rows"], d["dn_cols"]), dims=d)
+
+
+def synthetic_vq2m_image(num_layers, num_experts, seed=0, out=None, **dims):
+    """Whole .vq2m image in memory (numpy uint8, or written into ``out``, e.g. a pinned buffer)
+    for large paging benchmarks: expert payloads are tiled from a 64 MiB seeded random block
+    (uniform 16-bit indices) with fp16 scales ~0.02 patched in, which writes GBs in seconds."""
+    d = dict(DEFAULT_DIMS, **dims)
+    table, meta, end = _table_and_meta(num_layers, num_experts, d, None)
+    img = np.empty(end, dtype=np.uint8) if out is None else out
+    if img.nbytes < end:
+        raise ValueError("output buffer too small")
+    img[:RESERVED_HEADER_BYTES] = np.frombuffer(_header_bytes(num_layers, num_experts, table, meta), np.uint8)
+    rng = np.random.default_rng(seed)
+    block = rng.integers(0, 256, size=64 << 20, dtype=np.uint8)
+    scale_gu = (0.02 * np.exp(0.1 * rng.standard_normal(d["gu_rows"]))).astype(np.float16).view(np.uint8)
+    scale_dn = (0.02 * np.exp(0.1 * rng.standard_normal(d["dn_rows"]))).astype(np.float16).view(np.uint8)
+    pos = RESERVED_HEADER_BYTES
+    rec = record_bytes(d["gu_rows"], d["gu_cols"], d["dn_rows"], d["dn_cols"])
+    boff = 0
+    for ln in range(num_layers):
+        for e in range(num_experts):
+            n = rec
+            if boff + n > block.size:
+                boff = (boff * 7 + 4099) % (block.size - n)
+            img[pos:pos + n] = block[boff:boff + n]
+            og, sg, os_, ss, od, sd, ods, sds = table[ln][e]
+            img[os_:os_ + ss] = scale_gu
+            img[ods:ods + sds] = scale_dn
+            boff += n + 4096
+            pos += n
+    return img[:end], end

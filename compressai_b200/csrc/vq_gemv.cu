@@ -590,22 +590,24 @@ extern "C" int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_st
 extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_stride, int64_t x_k_div,
                             const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
                             const int32_t* e_ids, int64_t K, int64_t num_experts, const int16_t* idx,
-                            const void* cb0, const void* scale, int val_dtype, void* y, int y_dtype,
-                            int64_t out, int64_t ng, float rs, void* stream) {
+                            int64_t idx_e_stride, const void* cb0, const void* scale, int64_t scale_e_stride,
+                            int val_dtype, void* y, int y_dtype, int64_t out, int64_t ng, float rs,
+                            void* stream) {
   using namespace vq2;
   if (!x || !e_ids || !idx || !cb0 || !scale || !y) return VQ2_ERR_ARG;
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQ2_ERR_DTYPE;
   if (K <= 0 || num_experts <= 0 || out <= 0 || ng <= 0 || ng % 8 != 0 || out > INT32_MAX || ng * 8 > INT32_MAX)
     return VQ2_ERR_SHAPE;
   if (x_k_stride < 0 || x_k_div <= 0 || K > INT32_MAX) return VQ2_ERR_SHAPE;
-  if (!aligned(idx, 16) || !aligned(cb0, 16)) return VQ2_ERR_ALIGN;
+  if (idx_e_stride < out * ng || scale_e_stride < out) return VQ2_ERR_SHAPE;
+  if (!aligned(idx, 16) || !aligned(cb0, 16) || idx_e_stride % 8 != 0) return VQ2_ERR_ALIGN;
   GemvArgs a{};
   a.nprob = 0;
   a.x = x; a.x_dtype = x_dtype; a.x_mode = x_mode; a.x_row_stride = 0; a.x_k_stride = x_k_stride;
   a.x_k_div = x_k_div; a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale; a.M = 1;
   a.idx0 = idx; a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr; a.scale = scale;
   a.y = y; a.y_dtype = y_dtype; a.y_row_stride = 0; a.y_k_stride = out;
-  a.e_ids = e_ids; a.num_experts = num_experts; a.idx_e_stride = out * ng; a.scale_e_stride = out;
+  a.e_ids = e_ids; a.num_experts = num_experts; a.idx_e_stride = idx_e_stride; a.scale_e_stride = scale_e_stride;
   a.out = (int)out; a.n = (int)(ng * 8); a.rs = rs; a.K = (int)K;
   return run_gemv(a, out * K, false, val_dtype, static_cast<cudaStream_t>(stream));
 }

@@ -159,7 +159,9 @@ def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.
     """Expert-indexed GEMV: y[k] = rs * scale[e_k] * sum cb16[idx[e_k]] . act(x[k // x_k_div]).
 
     ``act`` is the identity (mode ROTATED), the forward RHT ``rot`` (mode RHT) or SwiGLU then
-    ``rot`` (mode SWIGLU_RHT, x rows fp32 [gate | up])."""
+    ``rot`` (mode SWIGLU_RHT, x rows fp32 [gate | up]). ``pool_idx`` [E, OUT, NG] and
+    ``pool_scale`` [E, OUT] may be strided views (e.g. into a pool of whole expert records)
+    as long as each expert's block is contiguous."""
     _lib.require_cuda(x, ids, pool_idx, cb16, pool_scale, y)
     if pool_idx.dtype != torch.int16 or pool_idx.dim() != 3:
         raise ValueError("pool_idx must be int16 [E, OUT, NG]")
@@ -167,6 +169,10 @@ def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.
     if mode is None:
         mode = _lib.VQ2_ACT_RHT if rot is not None else _lib.VQ2_ACT_ROTATED
     E, OUT, NG = pool_idx.shape
+    if pool_idx.stride(2) != 1 or pool_idx.stride(1) != NG or pool_scale.stride(-1) != 1:
+        raise ValueError("each expert's index block [OUT, NG] and scale vector must be contiguous")
+    idx_es = pool_idx.stride(0)
+    sc_es = pool_scale.stride(0) if pool_scale.dim() == 2 else OUT
     ids = _ids32(ids)
     K = ids.numel()
     if y.shape[0] < K or y.numel() < K * OUT or not y.is_contiguous():
@@ -175,14 +181,14 @@ def moe_gemv(x, ids, pool_idx, cb16, pool_scale, y, x_k_stride, x_k_div=1, rs=1.
         raise ValueError("x must be contiguous")
     if mode != _lib.VQ2_ACT_ROTATED and (rot is None or rot.n != NG * 8):
         raise ValueError("a rotation of size n is required for modes RHT / SWIGLU_RHT")
-    pool_idx, pool_scale = _c(pool_idx), _c(pool_scale)
-    if pool_scale.numel() != E * OUT:
+    if pool_scale.shape[0] != E or pool_scale.shape[-1] != OUT:
         raise ValueError("pool_scale must be [E, OUT]")
     _lib.call("vq2_moe_gemv", _lib.ptr(x), _lib.dtype_code(x), int(mode), int(x_k_stride), int(x_k_div),
               _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
               int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0,
-              _lib.ptr(ids), K, E, _lib.ptr(pool_idx), _lib.ptr(cb16), _lib.ptr(pool_scale), _lib.dtype_code(cb16),
-              _lib.ptr(y), _lib.dtype_code(y), OUT, NG, float(rs), _lib.stream_ptr(x.device))
+              _lib.ptr(ids), K, E, _lib.ptr(pool_idx), idx_es, _lib.ptr(cb16), _lib.ptr(pool_scale), sc_es,
+              _lib.dtype_code(cb16), _lib.ptr(y), _lib.dtype_code(y), OUT, NG, float(rs),
+              _lib.stream_ptr(x.device))
     return y
 
 

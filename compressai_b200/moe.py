@@ -1,0 +1,156 @@
+"""MoE expert path on VQ weights: router, resident expert pool, fused expert FFN.
+
+One MoE layer for T tokens with top-k routing is three launches on the device:
+
+1. ``vq2_moe_gemv`` gate_up over the T*k (token, expert) problems -- each CTA rotates its
+   token's hidden state (RHT 2048, fp32) in its prologue -- into fp32 [T*k, 1024];
+2. ``vq2_moe_gemv`` down with the SwiGLU and the 512-point RHT fused in its prologue, into fp32
+   [T*k, 2048];
+3. ``vq2_moe_combine``: routing-weighted sum per token in fixed order (+ the shared expert as
+   one more problem when present), cast to the hidden dtype;
+
+plus ``vq2_moe_route`` when the routing comes from logits. The reference runs the same math as
+rot_2048.fwd -> 2-D-grid Triton gate_up -> torch SiLU*up -> rot_512.fwd -> Triton down -> torch
+weighted sum (vq2/paged_runtime.py:491-511; vq2/load_and_test_full_35b.py:53-74), with a Python
+loop over tokens for T > 1 (:512-568 / :75-95).
+
+Experts are stored as whole records [gu_idx int16 1024x256 | gu_scale fp16 1024 | dn_idx int16
+2048x64 | dn_scale fp16 2048] (792,576 B), the .vq2m payload layout, so a pool is one
+[E, 792576] byte tensor and paging an expert is one copy.
+"""
+import torch
+import torch.nn as nn
+
+from . import _lib, kernels, vq
+from .synth import DN_COLS, DN_ROWS, GU_COLS, GU_ROWS
+
+
+class ExpertRecordPool:
+    """Device (or host) tensor of E expert records plus typed strided views into it:
+    gu_idx [E, gu_rows, gu_cols], gu_scale [E, gu_rows], dn_idx [E, dn_rows, dn_cols],
+    dn_scale [E, dn_rows]."""
+
+    def __init__(self, E, device, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_cols=DN_COLS,
+                 buf=None):
+        self.dims = (gu_rows, gu_cols, dn_rows, dn_cols)
+        o1 = gu_rows * gu_cols
+        o2 = o1 + gu_rows
+        o3 = o2 + dn_rows * dn_cols
+        o4 = o3 + dn_rows
+        self.record_bytes = 2 * o4
+        if (2 * o3) % 16 or self.record_bytes % 16:
+            raise ValueError("expert record layout breaks 16-byte alignment")
+        self.E = E
+        self.raw = buf if buf is not None else torch.empty(E, self.record_bytes, dtype=torch.uint8, device=device)
+        if self.raw.shape != (E, self.record_bytes):
+            raise ValueError("record buffer shape mismatch")
+        w = self.raw.view(torch.int16)
+        self.gu_idx = w[:, :o1].view(E, gu_rows, gu_cols)
+        self.gu_scale = w[:, o1:o2].view(torch.float16)
+        self.dn_idx = w[:, o2:o3].view(E, dn_rows, dn_cols)
+        self.dn_scale = w[:, o3:o4].view(torch.float16)
+
+    def set_expert(self, e, gu_idx, gu_scale, dn_idx, dn_scale):
+        self.gu_idx[e].copy_(torch.as_tensor(gu_idx))
+        self.gu_scale[e].copy_(torch.as_tensor(gu_scale).to(torch.float16))
+        self.dn_idx[e].copy_(torch.as_tensor(dn_idx))
+        self.dn_scale[e].copy_(torch.as_tensor(dn_scale).to(torch.float16))
+
+
+def route(logits, top_k=8, hidden=None, shared_gate=None):
+    """Router on device logits fp32 [T, E] -> (ids int32 [T, top_k], w fp32 [T, top_k]
+    [, shared_w fp32 [T]]); the math of Qwen3_5MoeTopKRouter (softmax, topk, renormalise) and
+    the shared expert's sigmoid gate."""
+    _lib.require_cuda(logits, hidden, shared_gate)
+    lg = logits.float().contiguous()
+    T, E = lg.shape
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=lg.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=lg.device)
+    sw = None
+    h = None
+    if shared_gate is not None:
+        h = hidden.reshape(T, -1).contiguous()
+        g = shared_gate.reshape(-1).float().contiguous()
+        sw = torch.empty(T, dtype=torch.float32, device=lg.device)
+    _lib.call("vq2_moe_route", _lib.ptr(lg), T, E, top_k, _lib.ptr(ids), _lib.ptr(w),
+              _lib.ptr(h) if h is not None else None, _lib.dtype_code(h) if h is not None else 0,
+              _lib.ptr(g) if shared_gate is not None else None, h.shape[1] if h is not None else 0,
+              _lib.ptr(sw) if sw is not None else None, _lib.stream_ptr(lg.device))
+    return (ids, w) if sw is None else (ids, w, sw)
+
+
+def expert_ffn(hidden, ids, weights, pool, cb16, rot_in, rot_mid, top_k, out=None, out_dtype=None):
+    """sum_j w[t, j] * Expert_{ids[t, j]}(h[t]) for T tokens, three launches.
+
+    hidden: [T, H]; ids: int32 [T*top_k] device (pool rows: expert ids or slots); weights:
+    fp32 [T, top_k]; pool: ExpertRecordPool on the device."""
+    T, H = hidden.shape
+    gr = pool.dims[0]
+    if H != rot_in.n or gr // 2 != rot_mid.n:
+        raise ValueError("rotation sizes do not match the expert shape")
+    h = hidden.contiguous()
+    K = T * top_k
+    gu = torch.empty(K, gr, dtype=torch.float32, device=h.device)
+    kernels.moe_gemv(h, ids, pool.gu_idx, cb16, pool.gu_scale, gu, x_k_stride=H, x_k_div=top_k, rot=rot_in)
+    y = torch.empty(K, pool.dims[2], dtype=torch.float32, device=h.device)
+    kernels.moe_gemv(gu, ids, pool.dn_idx, cb16, pool.dn_scale, y, x_k_stride=gr, rot=rot_mid,
+                     mode=_lib.VQ2_ACT_SWIGLU_RHT)
+    return kernels.moe_combine(y, weights.float().contiguous(), top_k, out=out, out_dtype=out_dtype or hidden.dtype)
+
+
+class PackedMoEExpertUniversal(nn.Module):
+    """All experts resident in HBM (reference vq2/load_and_test_full_35b.py:26-95):
+    forward(hidden_states [T, 2048], topk_idx [T, k], topk_weights [T, k]) -> [T, 2048].
+    The pool holds the 256 routed experts (+ the shared expert as row E when given)."""
+
+    def __init__(self, pool, cb16, device="cuda", shared=False):
+        super().__init__()
+        self.pool = pool
+        self.num_experts = pool.E - (1 if shared else 0)
+        self.shared = shared
+        self.cb16 = cb16
+        self.hidden_dim = pool.dims[1] * 8
+        self.intermediate_dim = pool.dims[0] // 2
+        self.rot_2048 = vq.get_rot("moe_expert_2048", self.hidden_dim, device)
+        self.rot_512 = vq.get_rot("moe_expert_512", self.intermediate_dim, device)
+
+    def forward(self, hidden_states, topk_idx, topk_weights, shared_weight=None):
+        T = hidden_states.shape[0]
+        k = topk_idx.shape[-1]
+        ids = topk_idx.reshape(T, k).to(torch.int32)
+        w = topk_weights.reshape(T, k).float()
+        if self.shared and shared_weight is not None:
+            ids = torch.cat([ids, torch.full((T, 1), self.num_experts, dtype=torch.int32, device=ids.device)], 1)
+            w = torch.cat([w, shared_weight.reshape(T, 1).float()], 1)
+            k += 1
+        return expert_ffn(hidden_states.reshape(T, -1), ids.reshape(-1).contiguous(), w, self.pool, self.cb16,
+                          self.rot_2048, self.rot_512, k)
+
+
+class MoEBlock(nn.Module):
+    """Sparse MoE block (Qwen3_5MoeSparseMoeBlock math) on VQ experts: router from logits (or a
+    dense router weight), top-k routed experts + the always-on shared expert weighted by
+    sigmoid(shared_gate . h), all resident. Four launches per layer."""
+
+    def __init__(self, experts, router_weight=None, shared_gate=None, top_k=8):
+        super().__init__()
+        self.experts = experts
+        self.router_weight = router_weight
+        self.shared_gate = shared_gate
+        self.top_k = top_k
+
+    def forward(self, hidden_states, router_logits=None):
+        T = hidden_states.shape[0]
+        if router_logits is None:
+            router_logits = torch.nn.functional.linear(hidden_states.to(self.router_weight.dtype), self.router_weight)
+        if self.shared_gate is not None and self.experts.shared:
+            ids, w, sw = route(router_logits, self.top_k, hidden_states, self.shared_gate)
+            ids = torch.cat([ids, torch.full((T, 1), self.experts.num_experts, dtype=torch.int32,
+                                             device=ids.device)], 1)
+            w = torch.cat([w, sw[:, None]], 1)
+            k = self.top_k + 1
+        else:
+            ids, w = route(router_logits, self.top_k)
+            k = self.top_k
+        ex = self.experts
+        return expert_ffn(hidden_states, ids.reshape(-1), w, ex.pool, ex.cb16, ex.rot_2048, ex.rot_512, k)

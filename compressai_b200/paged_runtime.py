@@ -1,0 +1,358 @@
+"""Paged MoE runtime over a ``.vq2m`` container, mirroring reference ``vq2/paged_runtime.py``.
+
+* ``PagedModelStore`` reads the container (offset mode: pread into pinned staging; mmap mode;
+  or an in-memory image, e.g. a pinned host tensor, which is DMA'd with no staging copy).
+* ``PagedMoEExpert`` keeps a static pool of C expert slots in HBM and decides hits, misses and
+  evictions on the host with exactly the reference's LRU (``_get_slot``,
+  vq2/paged_runtime.py:415-437: hit -> move_to_end; miss -> free_slots.pop(), else evict the
+  least recently used), so hit/miss/slot sequences match it bit for bit.
+* Differences from the reference: a miss is ONE copy of the contiguous 792,576-byte expert
+  record into a record-layout slot (the reference issues four), on a side CUDA stream; the
+  experts that hit are computed while the misses are in flight, the misses right after their
+  copy lands; scales stay fp16 (the reference converts them to bf16 on the host); the whole
+  (hits, misses, combine) step is three to five launches for any T instead of a Python loop
+  over tokens. There is no CPU compute path: CPU devices may hold the bookkeeping (for tests)
+  but forward() on them raises.
+"""
+import mmap
+import os
+import threading
+from collections import OrderedDict
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import container, moe, vq
+
+DEVICE = "cuda" if torch.cuda.is_available() else "cpu"
+
+
+class PagedModelStore:
+    """Reader of a .vq2m container (reference vq2/paged_runtime.py:49-284).
+
+    use_mmap=False: offset mode, each expert record is read with pread into a pinned staging
+    ring and copied to the device asynchronously. use_mmap=True: the file is memory-mapped and
+    records are copied from the mapping into the staging ring. ``PagedModelStore.from_image``
+    wraps an in-memory image (a pinned uint8 tensor is copied to the device directly)."""
+
+    STAGING_BUFFERS = 8
+
+    def __init__(self, file_path, use_mmap=False, device=None, _image=None):
+        self.device = device if device is not None else DEVICE
+        self.use_mmap = use_mmap
+        self.lock = threading.Lock()
+        self.mm = None
+        self.file = None
+        self.image = None
+        if _image is not None:
+            self.file_path = None
+            self.image = _image
+            head = _image[:container.RESERVED_HEADER_BYTES]
+            head = head.numpy() if isinstance(head, torch.Tensor) else head
+            self.layout = container.parse_header(memoryview(np.ascontiguousarray(head)), file_size=len(_image))
+        else:
+            self.file_path = os.fspath(file_path)
+            if not os.path.exists(self.file_path):
+                raise FileNotFoundError(f".vq2m container not found: {self.file_path}")
+            size = os.path.getsize(self.file_path)
+            self.file = open(self.file_path, "rb")
+            head = self.file.read(min(size, container.RESERVED_HEADER_BYTES))
+            self.layout = container.parse_header(head, file_size=size)
+            if use_mmap:
+                self.mm = mmap.mmap(self.file.fileno(), 0, access=mmap.ACCESS_READ)
+        lay = self.layout
+        self.num_layers, self.num_experts = lay.num_layers, lay.num_experts
+        self.payload_start = lay.payload_start
+        self.moe_offsets = lay.table
+        self.meta = lay.meta
+        self.other_tensors = self.meta.get("other_tensors", {})
+        self.gu_rows, self.gu_cols = lay.gu_rows, lay.gu_cols
+        self.dn_rows, self.dn_cols = lay.dn_rows, lay.dn_cols
+        self.expert_bytes = lay.expert_bytes
+        self._staging = None
+        self._staging_next = 0
+        self.bytes_paged = 0
+
+    @classmethod
+    def from_image(cls, image, device=None):
+        """Container held in host memory (numpy uint8 array or uint8 tensor, pinned for DMA)."""
+        return cls(None, device=device, _image=image)
+
+    # ---- raw record access -------------------------------------------------------------------
+    def _host_record(self, layer_idx, expert_id):
+        """Host bytes of one expert record: a tensor view (image / mmap) or None (offset mode)."""
+        off, nb = self.layout.record(layer_idx, expert_id)
+        if self.image is not None:
+            img = self.image
+            return img[off:off + nb] if isinstance(img, torch.Tensor) else torch.from_numpy(img[off:off + nb])
+        if self.mm is not None:
+            return np.frombuffer(self.mm, dtype=np.uint8, count=nb, offset=off)
+        return None
+
+    def read_record(self, layer_idx, expert_id, out=None):
+        """Copy one expert record into a host buffer (numpy/tensor uint8) and return it."""
+        off, nb = self.layout.record(layer_idx, expert_id)
+        if out is None:
+            out = np.empty(nb, dtype=np.uint8)
+        view = out.numpy() if isinstance(out, torch.Tensor) else out
+        src = self._host_record(layer_idx, expert_id)
+        if src is not None:
+            view[:nb] = src.numpy() if isinstance(src, torch.Tensor) else src
+        else:
+            with self.lock:
+                got = os.preadv(self.file.fileno(), [memoryview(view[:nb])], off)
+            if got != nb:
+                raise IOError(f"short read of expert ({layer_idx}, {expert_id}): {got} of {nb} bytes")
+        return out
+
+    def _staging_ring(self):
+        if self._staging is None:
+            pin = torch.cuda.is_available()
+            self._staging = [(torch.empty(self.expert_bytes, dtype=torch.uint8, pin_memory=pin),
+                              torch.cuda.Event() if pin else None) for _ in range(self.STAGING_BUFFERS)]
+        return self._staging
+
+    def load_record_async(self, layer_idx, expert_id, dst, stream=None):
+        """Copy one expert record into device memory ``dst`` (uint8 [expert_bytes]) on
+        ``stream`` without blocking the host on the copy: pinned images go straight to the
+        device; other sources pass through a ring of pinned staging buffers, each reused only
+        after its previous copy has completed."""
+        src = self._host_record(layer_idx, expert_id)
+        stream = stream or torch.cuda.current_stream(dst.device)
+        if isinstance(src, torch.Tensor) and src.is_pinned():
+            with torch.cuda.stream(stream):
+                dst.copy_(src, non_blocking=True)
+        else:
+            ring = self._staging_ring()
+            buf, ev = ring[self._staging_next]
+            self._staging_next = (self._staging_next + 1) % len(ring)
+            ev.synchronize()  # the previous copy out of this buffer is done
+            self.read_record(layer_idx, expert_id, out=buf)
+            with torch.cuda.stream(stream):
+                dst.copy_(buf, non_blocking=True)
+                ev.record(stream)
+        self.bytes_paged += self.expert_bytes
+
+    # ---- reference-compatible accessors -----------------------------------------------------
+    def _split(self, rec):
+        rec = torch.as_tensor(rec)
+        gr, gc, dr, dc = self.gu_rows, self.gu_cols, self.dn_rows, self.dn_cols
+        w = rec.view(torch.int16)
+        o1 = gr * gc
+        o2 = o1 + gr
+        o3 = o2 + dr * dc
+        return (w[:o1].view(gr, gc), w[o1:o2].view(torch.float16), w[o2:o3].view(dr, dc),
+                w[o3:o3 + dr].view(torch.float16))
+
+    def get_expert_weights(self, layer_idx, expert_id, device="cpu"):
+        """(gu_idx int16, gu_scale fp16, dn_idx int16, dn_scale fp16) of one expert
+        (vq2/paged_runtime.py:175-207; scales stay fp16 on every device)."""
+        parts = self._split(torch.from_numpy(self.read_record(layer_idx, expert_id)))
+        return tuple(p.clone() if str(device) == "cpu" else p.to(device) for p in parts)
+
+    def load_expert_into_slot(self, layer_idx, expert_id, slot, pool_gu_idx, pool_gu_scale, pool_dn_idx,
+                              pool_dn_scale, device=None):
+        """Copy one expert into slot `slot` of four separate pool tensors (reference signature,
+        vq2/paged_runtime.py:125-173); scales are converted to the pool's dtype."""
+        gi, gs, di, ds = self._split(torch.from_numpy(self.read_record(layer_idx, expert_id)))
+        nb = pool_gu_idx.is_cuda
+        pool_gu_idx[slot].copy_(gi, non_blocking=False)
+        pool_gu_scale[slot].copy_(gs.to(pool_gu_scale.dtype), non_blocking=nb)
+        pool_dn_idx[slot].copy_(di, non_blocking=False)
+        pool_dn_scale[slot].copy_(ds.to(pool_dn_scale.dtype), non_blocking=nb)
+        self.bytes_paged += self.expert_bytes
+
+    def get_dense_tensor(self, name, device="cpu"):
+        """Dense bf16 tensor listed in meta["other_tensors"] (vq2/paged_runtime.py:209-226)."""
+        info = self.other_tensors.get(name)
+        if not info or info.get("type") != "dense":
+            return None
+        raw = self._read_span(info["offset"], info["size"])
+        return torch.from_numpy(raw).view(torch.bfloat16).view(*info["shape"]).to(device)
+
+    def get_quant_linear(self, name, cbs_data=None, device="cpu"):
+        """Quantized linear listed in meta["other_tensors"]: a dict of indices and fp32 scales
+        (vq2/paged_runtime.py:228-279 without cbs_data); with cbs_data, the dequantized bf16
+        weight (inverse rotation on the device)."""
+        info = self.other_tensors.get(name)
+        if not info or info.get("type") != "quant_linear":
+            return None
+        idx = []
+        for im in info["idx_meta"]:
+            dt = np.int16 if im.get("dtype", "int16") == "int16" else np.uint8
+            idx.append(torch.from_numpy(self._read_span(im["offset"], im["size"]).view(dt).copy()).to(device))
+        sm = info["scale_meta"]
+        scale = torch.from_numpy(self._read_span(sm["offset"], sm["size"]).view(np.float16).copy()).to(device).float()
+        if cbs_data is None:
+            return {"shape": info["shape"], "cfg": info["cfg"], "tag": info["tag"], "idx": idx, "scale": scale}
+        rows, n = info["shape"]
+        rec = 0
+        for i, cfg_bits in enumerate(info["cfg"]):
+            cb = torch.as_tensor(cbs_data[vq.cfg_key(info["cfg"], i)]).to(device=device, dtype=torch.float32)
+            ix = idx[i].to(torch.int64) & (0xFFFF if cfg_bits > 8 else 0xFF)
+            rec = rec + cb[ix]
+        Q = rec.reshape(rows, n) * scale[:, None]
+        return vq.get_rot(info["tag"], n, device).inv_f32(Q).to(torch.bfloat16)
+
+    def _read_span(self, off, size):
+        out = np.empty(size, dtype=np.uint8)
+        if self.image is not None:
+            img = self.image
+            out[:] = (img[off:off + size].numpy() if isinstance(img, torch.Tensor) else img[off:off + size])
+        elif self.mm is not None:
+            out[:] = np.frombuffer(self.mm, dtype=np.uint8, count=size, offset=off)
+        else:
+            with self.lock:
+                got = os.preadv(self.file.fileno(), [memoryview(out)], off)
+            if got != size:
+                raise IOError("short read")
+        return out
+
+    def close(self):
+        if self.mm is not None:
+            self.mm.close()
+            self.mm = None
+        if self.file is not None:
+            self.file.close()
+            self.file = None
+
+
+class LRUExpertCache:
+    """Tuple cache of whole experts keyed by (layer, expert) (vq2/paged_runtime.py:287-313)."""
+
+    def __init__(self, capacity=128, device=DEVICE):
+        self.capacity = capacity
+        self.device = device
+        self.cache = OrderedDict()
+        self.hits = 0
+        self.misses = 0
+
+    def get(self, store, layer_idx, expert_id):
+        key = (layer_idx, expert_id)
+        if key in self.cache:
+            self.hits += 1
+            self.cache.move_to_end(key)
+            return self.cache[key]
+        self.misses += 1
+        w = store.get_expert_weights(layer_idx, expert_id, device=self.device)
+        self.cache[key] = w
+        if len(self.cache) > self.capacity:
+            self.cache.popitem(last=False)
+        return w
+
+
+class PagedMoEExpert(nn.Module):
+    """Routed experts of one MoE layer served from a static HBM pool of `capacity` slots
+    (vq2/paged_runtime.py:316-568). forward(hidden_states [T, H], topk_idx [T, k],
+    topk_weights [T, k]) -> [T, H] in the hidden dtype. topk_idx on the host avoids the
+    device-to-host read of the ids (the reference always reads them back, :443)."""
+
+    def __init__(self, layer_idx, store, cb16, capacity=96, device=DEVICE, copy_stream=None):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.store = store
+        self.cb16 = cb16
+        self.capacity = capacity
+        self.device = torch.device(device)
+        self.hidden_dim = store.gu_cols * 8
+        self.intermediate_dim = store.gu_rows // 2
+        modes = store.meta.get("expert_modes", {})
+        if any(modes.get(f"{layer_idx}:{e}") == 3 for e in range(store.num_experts)):
+            raise NotImplementedError("3-bit promoted experts (expert_modes) are not supported by the paged pool")
+        self.pool = moe.ExpertRecordPool(capacity, self.device, store.gu_rows, store.gu_cols, store.dn_rows,
+                                         store.dn_cols)
+        # reference attribute names, as views into the record pool
+        self.pool_gu_idx, self.pool_gu_scale = self.pool.gu_idx, self.pool.gu_scale
+        self.pool_dn_idx, self.pool_dn_scale = self.pool.dn_idx, self.pool.dn_scale
+        self.expert_to_slot = {}
+        self.free_slots = list(range(capacity))
+        self.access_order = OrderedDict()
+        self.hits = 0
+        self.misses = 0
+        self.activated_experts_set = set()
+        if self.device.type == "cuda":
+            self.rot_2048 = vq.get_rot("moe_expert_2048", self.hidden_dim, self.device)
+            self.rot_512 = vq.get_rot("moe_expert_512", self.intermediate_dim, self.device)
+            self.copy_stream = copy_stream or torch.cuda.Stream(self.device)
+            self._compute_done = torch.cuda.Event()
+            self._compute_done.record(torch.cuda.current_stream(self.device))
+        self._pending_loads = []
+
+    # ---- host LRU (reference semantics) -----------------------------------------------------
+    def _assign_slot(self, e_id):
+        """Bookkeeping of _get_slot (vq2/paged_runtime.py:415-437) without the copy:
+        returns (slot, hit)."""
+        self.activated_experts_set.add(e_id)
+        if e_id in self.expert_to_slot:
+            self.hits += 1
+            self.access_order.move_to_end(e_id)
+            return self.expert_to_slot[e_id], True
+        self.misses += 1
+        if self.free_slots:
+            slot = self.free_slots.pop()
+        else:
+            evict_id, _ = self.access_order.popitem(last=False)
+            slot = self.expert_to_slot.pop(evict_id)
+        self.expert_to_slot[e_id] = slot
+        self.access_order[e_id] = None
+        return slot, False
+
+    def _get_slot(self, e_id):
+        """Reference-compatible: assign a slot and start paging the expert in on a miss."""
+        slot, hit = self._assign_slot(e_id)
+        if not hit:
+            self._load(e_id, slot)
+        return slot
+
+    def _load(self, e_id, slot):
+        if self.device.type != "cuda":
+            self.store.load_expert_into_slot(self.layer_idx, e_id, slot, self.pool_gu_idx, self.pool_gu_scale,
+                                             self.pool_dn_idx, self.pool_dn_scale)
+            return
+        # the slot may still be read by compute already enqueued: order the copy after it
+        self.copy_stream.wait_event(self._compute_done)
+        self.store.load_record_async(self.layer_idx, e_id, self.pool.raw[slot], self.copy_stream)
+
+    # ---- compute ----------------------------------------------------------------------------
+    def _run(self, h, slots, w, out):
+        """Expert FFN of tokens h [t, H] on pool slots [t, k] with weights [t, k] into out."""
+        stream = torch.cuda.current_stream(self.device)
+        ids = torch.as_tensor(slots, dtype=torch.int32).reshape(-1).pin_memory().to(self.device, non_blocking=True)
+        moe.expert_ffn(h, ids, w, self.pool, self.cb16, self.rot_2048, self.rot_512, w.shape[1], out=out)
+        self._compute_done.record(stream)
+
+    def forward(self, hidden_states, topk_idx, topk_weights):
+        if self.device.type != "cuda" or not hidden_states.is_cuda:
+            raise ValueError("PagedMoEExpert computes on CUDA only (no CPU fallback)")
+        T = hidden_states.shape[0]
+        K = topk_idx.shape[-1]
+        ids = topk_idx.reshape(T, K)
+        ids_list = ids.tolist() if not ids.is_cuda else ids.cpu().tolist()  # reference: .tolist() sync
+        w = topk_weights.reshape(T, K).to(self.device, torch.float32)
+        h = hidden_states.reshape(T, -1)
+        out = torch.empty(T, self.hidden_dim, dtype=hidden_states.dtype, device=self.device)
+        stream = torch.cuda.current_stream(self.device)
+
+        seg_start, seg_slots, slot_rows = 0, set(), []
+        loads_in_seg = False
+        for t in range(T):
+            row = []
+            for e in ids_list[t]:
+                slot, hit = self._assign_slot(int(e))
+                if not hit and slot in seg_slots:
+                    # the slot is still to be read by earlier tokens of this batch: run them first
+                    if loads_in_seg:
+                        stream.wait_stream(self.copy_stream)
+                    self._run(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t])
+                    seg_start, seg_slots, slot_rows, loads_in_seg = t, set(), [], False
+                if not hit:
+                    self._load(int(e), slot)
+                    loads_in_seg = True
+                row.append(slot)
+            slot_rows.append(row)
+            seg_slots.update(row)
+        if loads_in_seg:
+            stream.wait_stream(self.copy_stream)
+        self._run(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T])
+        return out

@@ -123,9 +123,11 @@ VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_strid
  *   y[k, r] = rs * scale[e_k, r] * sum_g dot(cb0[idx[e_k, r, g]], xr_k[8g:8g+8]),  e_k = e_ids[k]
  * x_k_stride = 0 shares one activation among all problems (gate_up of one token); x_k_div =
  * top_k maps problem t*top_k + j to token t. e_ids: int32 [K] device (slots of a paged pool or
- * ids of a resident pool; ids outside [0, num_experts) give zero rows). idx: int16
- * [num_experts, out, ng]; scale: [num_experts, out] in val_dtype; y: [K, out] in y_dtype.
- * ng % 8 == 0; idx and cb0 16-byte aligned.
+ * ids of a resident pool; ids outside [0, num_experts) give zero rows). Expert e's indices are
+ * the int16 [out, ng] block at idx + e * idx_e_stride and its scales the [out] vector at
+ * scale + e * scale_e_stride (element strides; >= out * ng and >= out, so a pool may interleave
+ * whole expert records); scales in val_dtype; y: [K, out] in y_dtype. ng % 8 == 0; idx, cb0
+ * and every expert's index block 16-byte aligned.
  * Replaces: vq_moe_parallel_gate_up / vq_moe_parallel_down (vq2/kernels.py:246-264) and
  * _parallel_moe_gate_up_kernel / _parallel_moe_down_kernel (vq2/kernels.py:117-176), plus the
  * rot_2048.fwd / SwiGLU / rot_512.fwd torch ops around them (vq2/paged_runtime.py:495-504).
@@ -133,7 +135,8 @@ VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_strid
 VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_stride, int64_t x_k_div,
                          const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
                          const int32_t* e_ids, int64_t K, int64_t num_experts, const int16_t* idx,
-                         const void* cb0, const void* scale, int val_dtype, void* y, int y_dtype,
+                         int64_t idx_e_stride, const void* cb0, const void* scale,
+                         int64_t scale_e_stride, int val_dtype, void* y, int y_dtype,
                          int64_t out, int64_t ng, float rs, void* stream);
 
 /*
@@ -146,6 +149,22 @@ VQ2_API int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_str
  */
 VQ2_API int vq2_moe_combine(const float* y, const float* w, int64_t T, int64_t top_k,
                             int64_t H, const float* add, void* out, int out_dtype, void* stream);
+
+/*
+ * MoE router, per token t (one warp each):
+ *   ids[t, :] = the top_k experts by logit (descending, ties to the lower id)
+ *   w[t, j]   = softmax(logits[t])[ids[t, j]] / sum_j' softmax(logits[t])[ids[t, j']]
+ * and, when shared_gate != NULL, shared_w[t] = sigmoid(sum_i h[t, i] * shared_gate[i]).
+ * logits: fp32 [T, E] (E <= 1024); ids: int32 [T, top_k] (top_k <= 32); w: fp32 [T, top_k];
+ * h: [T, H] in h_dtype; shared_gate: fp32 [H]; shared_w: fp32 [T].
+ * Replaces: Qwen3_5MoeTopKRouter.forward's softmax/topk/renormalise and the
+ * sigmoid(shared_expert_gate(x)) of Qwen3_5MoeSparseMoeBlock.forward (installed transformers
+ * modeling_qwen3_5_moe.py:762-791), which the reference's MoE path consumes
+ * (vq2/paged_runtime.py:439-444).
+ */
+VQ2_API int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t top_k, int32_t* ids,
+                          float* w, const void* h, int h_dtype, const float* shared_gate, int64_t H,
+                          float* shared_w, void* stream);
 
 /*
  * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of rows

@@ -50,11 +50,14 @@ def test_argument_validation_without_device():
     # RHT block size not a power of two
     assert lib.vq2_rht(p, 2, 2048, 1, 2048, 1000, p, p, 1.0, 0, p, 2048, None) == _lib.VQ2_ERR_SHAPE
     # moe: zero experts
-    assert lib.vq2_moe_gemv(p, 2, 0, 0, 1, None, None, 0, 1.0, p, 8, 0, p, p, p, 0, p, 2, 1024, 256, 1.0,
-                            None) == _lib.VQ2_ERR_SHAPE
+    assert lib.vq2_moe_gemv(p, 2, 0, 0, 1, None, None, 0, 1.0, p, 8, 0, p, 262144, p, p, 1024, 0, p, 2, 1024,
+                            256, 1.0, None) == _lib.VQ2_ERR_SHAPE
     # fused RHT mode without a rotation
-    assert lib.vq2_moe_gemv(p, 2, 1, 0, 1, None, None, 2048, 1.0, p, 8, 16, p, p, p, 0, p, 2, 1024, 256, 1.0,
-                            None) == _lib.VQ2_ERR_ARG
+    assert lib.vq2_moe_gemv(p, 2, 1, 0, 1, None, None, 2048, 1.0, p, 8, 16, p, 262144, p, p, 1024, 0, p, 2, 1024,
+                            256, 1.0, None) == _lib.VQ2_ERR_ARG
+    # expert stride smaller than one expert
+    assert lib.vq2_moe_gemv(p, 2, 0, 0, 1, None, None, 0, 1.0, p, 8, 16, p, 1000, p, p, 1024, 0, p, 2, 1024,
+                            256, 1.0, None) == _lib.VQ2_ERR_SHAPE
     # multi-matrix: too many matrices
     arr = (ctypes.c_void_p * 9)(*([16] * 9))
     outs = (ctypes.c_int64 * 9)(*([64] * 9))

@@ -1,0 +1,107 @@
+"""Host-side paging logic (CPU): the .vq2m container against the reference reader's output,
+corrupt-file handling, and the product LRU against the reference _get_slot sequences."""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from compressai_b200 import container, paged_runtime, synth
+from tests.conftest import golden
+
+DIMS = dict(gu_rows=16, gu_cols=8, dn_rows=32, dn_cols=2)
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture()
+def small_vq2m(tmp_path):
+    path = str(tmp_path / "small.vq2m")
+    container.write_synthetic_vq2m(path, num_layers=2, num_experts=5, seed=7, **DIMS)
+    return path
+
+
+def test_writer_matches_golden_file(small_vq2m):
+    d = golden("vq2m.npz")
+    assert hashlib.sha256(open(small_vq2m, "rb").read()).hexdigest() == str(d["file_sha"])
+
+
+@pytest.mark.parametrize("mode", ["offset", "mmap", "image"])
+def test_reader_matches_reference_reader(small_vq2m, mode):
+    d = golden("vq2m.npz")
+    if mode == "image":
+        st = paged_runtime.PagedModelStore.from_image(np.fromfile(small_vq2m, dtype=np.uint8), device="cpu")
+    else:
+        st = paged_runtime.PagedModelStore(small_vq2m, use_mmap=(mode == "mmap"), device="cpu")
+    hdr = d["m0_hdr"]
+    assert (st.num_layers, st.num_experts, st.payload_start, st.gu_rows, st.gu_cols, st.dn_rows,
+            st.dn_cols) == tuple(int(v) for v in hdr)
+    assert np.array_equal(np.array(st.moe_offsets, dtype=np.int64), d["m0_entries"])
+    for ln in range(2):
+        for e in range(5):
+            got = [sha(t.numpy()) for t in st.get_expert_weights(ln, e, device="cpu")]
+            assert got == list(d[f"m0_{ln}_{e}"]), (ln, e)
+            assert got == list(d[f"m1_{ln}_{e}"]), (ln, e)
+            # and the content is the seeded expert
+            ref = synth.synth_expert(7 * 1_000_003 + ln, e, **DIMS)
+            for a, b in zip(st.get_expert_weights(ln, e), ref):
+                assert np.array_equal(a.numpy(), b)
+    st.close()
+
+
+def test_corrupt_containers(tmp_path, small_vq2m):
+    with pytest.raises(FileNotFoundError):
+        paged_runtime.PagedModelStore(str(tmp_path / "missing.vq2m"))
+    raw = bytearray(open(small_vq2m, "rb").read())
+    bad = tmp_path / "bad_magic.vq2m"
+    bad.write_bytes(b"XXXX" + bytes(raw[4:]))
+    with pytest.raises(ValueError):
+        paged_runtime.PagedModelStore(str(bad))
+    trunc = tmp_path / "trunc.vq2m"
+    trunc.write_bytes(bytes(raw[: len(raw) - 100]))
+    with pytest.raises(ValueError):
+        paged_runtime.PagedModelStore(str(trunc))
+    short = tmp_path / "short.vq2m"
+    short.write_bytes(bytes(raw[:40]))
+    with pytest.raises(ValueError):
+        paged_runtime.PagedModelStore(str(short))
+
+
+def test_synthetic_image_layout():
+    img, end = container.synthetic_vq2m_image(2, 3, seed=1, **DIMS)
+    st = paged_runtime.PagedModelStore.from_image(img, device="cpu")
+    rec = container.record_bytes(**DIMS)
+    assert end == container.RESERVED_HEADER_BYTES + 6 * rec
+    off, nb = st.layout.record(1, 2)
+    assert nb == rec and off == container.RESERVED_HEADER_BYTES + 5 * rec
+    gi, gs, di, ds = st.get_expert_weights(1, 2)
+    assert gs.dtype == torch.float16 and np.all(gs.float().numpy() > 0)
+
+
+def _lru_module(cap):
+    img, _ = container.synthetic_vq2m_image(1, 256, seed=0, **DIMS)
+    st = paged_runtime.PagedModelStore.from_image(img, device="cpu")
+    return paged_runtime.PagedMoEExpert(0, st, cb16=None, capacity=cap, device="cpu")
+
+
+@pytest.mark.parametrize("case", ["cap39", "cap4", "cap8"])
+def test_product_lru_matches_reference_sequence(case):
+    d = golden("lru.npz")
+    steps, layers, cap, seed = (int(v) for v in d[f"{case}_meta"])
+    trace = d[f"{case}_trace"]
+    ref_slots, ref_hits, ref_cnt = d[f"{case}_slots"], d[f"{case}_hits"], d[f"{case}_counters"]
+    for ln in range(min(layers, 6)):
+        m = _lru_module(cap)
+        got = [m._assign_slot(int(e)) for e in trace[:, ln, :].reshape(-1)]
+        assert np.array_equal(np.array([g[0] for g in got]).reshape(steps, -1), ref_slots[:, ln, :])
+        assert np.array_equal(np.array([g[1] for g in got]).reshape(steps, -1), ref_hits[:, ln, :].astype(bool))
+        assert (m.hits, m.misses, len(m.activated_experts_set)) == tuple(ref_cnt[ln])
+
+
+def test_cpu_forward_is_refused():
+    m = _lru_module(4)
+    with pytest.raises(ValueError, match="CUDA"):
+        m(torch.zeros(1, 64), torch.zeros(1, 8, dtype=torch.long), torch.zeros(1, 8))

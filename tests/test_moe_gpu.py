@@ -1,0 +1,133 @@
+"""MoE path on the GPU vs the oracle and the reference's golden outputs: router, resident
+experts, MoE block with shared expert, paged experts (all store modes) with bit-exact LRU."""
+import numpy as np
+import pytest
+import torch
+
+from compressai_b200 import container, moe, paged_runtime, synth
+from oracle import vq2_oracle as O
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 1e-3
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30)
+
+
+@pytest.fixture(scope="module")
+def cbs():
+    try:
+        d = golden("codebooks.npz")
+        return {"16": d["cb16"], "16_8": d["cb16_8"]}
+    except pytest.skip.Exception:
+        return synth.random_codebooks(1)
+
+
+def cb16_dev(cbs):
+    return torch.from_numpy(cbs["16"]).to(DEV)
+
+
+ROT2048 = O.rot_params("moe_expert_2048", 2048)
+ROT512 = O.rot_params("moe_expert_512", 512)
+
+
+@pytest.mark.parametrize("T,E,K", [(1, 256, 8), (32, 256, 8), (5, 64, 4), (3, 1000, 16)])
+def test_router_matches_reference_math(T, E, K):
+    logits = np.random.default_rng(T * E).standard_normal((T, E)).astype(np.float32)
+    ids, w = moe.route(torch.from_numpy(logits).to(DEV), K)
+    rid, rw = O.router_ref(logits, K)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    assert np.abs(w.cpu().numpy() - rw).max() < 1e-6
+
+
+def test_router_golden_and_shared_gate():
+    d = golden("moe.npz")
+    for nm in ("t1", "t4"):
+        ids, w = moe.route(torch.from_numpy(d[f"{nm}_logits"]).to(DEV), 8)
+        assert np.array_equal(ids.cpu().numpy(), d[f"{nm}_ids"])
+        assert np.abs(w.cpu().numpy() - d[f"{nm}_w"]).max() < 1e-6
+    h = np.random.default_rng(0).standard_normal((4, 2048)).astype(np.float16)
+    g = (0.02 * np.random.default_rng(1).standard_normal(2048)).astype(np.float32)
+    lg = torch.randn(4, 256, device=DEV)
+    _, _, sw = moe.route(lg, 8, torch.from_numpy(h).to(DEV), torch.from_numpy(g).to(DEV))
+    ref = 1 / (1 + np.exp(-(h.astype(np.float64) @ g.astype(np.float64))))
+    assert np.abs(sw.cpu().numpy() - ref).max() < 1e-5
+
+
+def resident_pool(seed, E, extra=None):
+    pool = moe.ExpertRecordPool(E + (1 if extra is not None else 0), DEV)
+    for e in range(E):
+        pool.set_expert(e, *[torch.from_numpy(a) for a in synth.synth_expert(seed, e)])
+    if extra is not None:
+        pool.set_expert(E, *[torch.from_numpy(a) for a in extra])
+    return pool
+
+
+def test_resident_moe_matches_reference_golden(cbs):
+    """PackedMoEExpertUniversal vs the reference's own CPU expert path (golden)."""
+    d = golden("moe.npz")
+    seed = int(d["t1_seed"])
+    pool = resident_pool(seed, 256)
+    ex = moe.PackedMoEExpertUniversal(pool, cb16_dev(cbs), DEV)
+    for nm in ("t1", "t4"):
+        h = torch.from_numpy(d[f"{nm}_h"]).to(DEV)
+        y = ex(h, torch.from_numpy(d[f"{nm}_ids"]).to(DEV), torch.from_numpy(d[f"{nm}_w"]).to(DEV))
+        assert y.dtype == torch.float16
+        assert rel_err(y.float().cpu().numpy(), d[f"{nm}_y"]) < TOL, nm
+
+
+@pytest.mark.parametrize("T", [1, 32])
+def test_moe_block_with_shared_expert(cbs, T):
+    seed = 11
+    shared = synth.synth_expert(99, 0)
+    pool = resident_pool(seed, 256, extra=shared)
+    ex = moe.PackedMoEExpertUniversal(pool, cb16_dev(cbs), DEV, shared=True)
+    g = (0.05 * np.random.default_rng(2).standard_normal(2048)).astype(np.float32)
+    blk = moe.MoEBlock(ex, shared_gate=torch.from_numpy(g).to(DEV))
+    logits = np.random.default_rng(3 + T).standard_normal((T, 256)).astype(np.float32)
+    h = np.random.default_rng(4 + T).standard_normal((T, 2048)).astype(np.float16)
+    y = blk(torch.from_numpy(h).to(DEV), torch.from_numpy(logits).to(DEV)).float().cpu().numpy()
+    ids, w = O.router_ref(logits, 8)
+    sw = 1 / (1 + np.exp(-(h.astype(np.float64) @ g.astype(np.float64))))
+    ref = O.moe_layer_ref(h, ids, w, lambda e: synth.synth_expert(seed, e), cbs["16"], ROT2048, ROT512,
+                          shared=shared, shared_w=sw)
+    assert rel_err(y, ref) < TOL
+
+
+@pytest.mark.parametrize("mode", ["image_pinned", "offset", "mmap"])
+@pytest.mark.parametrize("T,cap", [(1, 12), (3, 10), (4, 8)])
+def test_paged_experts_outputs_and_lru(cbs, tmp_path, mode, T, cap):
+    layers, E, seed = 2, 24, 5
+    if mode == "image_pinned":
+        img, _ = container.synthetic_vq2m_image(layers, E, seed=seed)
+        store = paged_runtime.PagedModelStore.from_image(torch.from_numpy(img).pin_memory(), device=DEV)
+    else:
+        path = str(tmp_path / "p.vq2m")
+        container.write_synthetic_vq2m(path, layers, E, seed=seed)
+        store = paged_runtime.PagedModelStore(path, use_mmap=(mode == "mmap"), device=DEV)
+    cb = cb16_dev(cbs)
+    mods = [paged_runtime.PagedMoEExpert(ln, store, cb, capacity=cap, device=DEV) for ln in range(layers)]
+    oracles = [O.LRUSlotOracle(cap) for _ in range(layers)]
+    rng = np.random.default_rng(T * 10 + cap)
+    for step in range(6):
+        h = rng.standard_normal((T, 2048)).astype(np.float16)
+        for ln in range(layers):
+            ids = np.stack([rng.choice(E, 8, replace=False) for _ in range(T)])
+            w = rng.random((T, 8)).astype(np.float32)
+            w /= w.sum(1, keepdims=True)
+            y = mods[ln](torch.from_numpy(h).to(DEV), torch.from_numpy(ids), torch.from_numpy(w))
+            for e in ids.reshape(-1):
+                oracles[ln].get_slot(int(e))
+            assert (mods[ln].hits, mods[ln].misses) == (oracles[ln].hits, oracles[ln].misses)
+            assert mods[ln].expert_to_slot == oracles[ln].expert_to_slot
+            expert = lambda e, ln=ln: tuple(t.numpy() for t in store.get_expert_weights(ln, e))
+            ref = O.moe_layer_ref(h, ids, w, expert, cbs["16"], ROT2048, ROT512)
+            assert rel_err(y.float().cpu().numpy(), ref) < TOL, (mode, step, ln)
+            h = y.cpu().numpy().astype(np.float16)
+    assert store.bytes_paged == sum(m.misses for m in mods) * store.expert_bytes
+    store.close()
