@@ -40,6 +40,9 @@ SIGNATURES = {
     "vq2_moe_combine": [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p],
     "vq2_gather_probe": [_p, _i64, _i64, _i64, _p, _p],
     "vq2_moe_route": [_p, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p, _p],
+    "vq2_moe_expert_ffn": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
+                           _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _p],
+    "vq2_moe_expert_ffn_workspace": [_i64, _i64, _i64, _i64],
 }
 ABI_VERSION = 1
 
@@ -66,7 +69,8 @@ def load():
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_char_p if name == "vq2_status_string" else ctypes.c_int
+            fn.restype = (ctypes.c_char_p if name == "vq2_status_string" else
+                          ctypes.c_int64 if name.endswith("_workspace") else ctypes.c_int)
         if lib.vq2_abi_version() != ABI_VERSION:
             raise VQ2Error(f"ABI version mismatch: library {lib.vq2_abi_version()}, python {ABI_VERSION}")
         _lib = lib

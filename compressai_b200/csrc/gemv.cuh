@@ -1,0 +1,61 @@
+// Internal interface of the VQ GEMV kernel family (vq_gemv.cu), shared with the fused MoE
+// entry points.
+#pragma once
+#include "common.cuh"
+
+namespace vq2 {
+
+constexpr int kMaxProbs = 8;  // matrices sharing one activation in a multi-matrix launch
+
+struct GemvArgs {
+  const void* x;          // activations, x_dtype (mode SWIGLU_RHT: fp32 [gate | up] rows)
+  int x_dtype;
+  int x_mode;             // VQ2_ACT_ROTATED / VQ2_ACT_RHT / VQ2_ACT_SWIGLU_RHT
+  int64_t x_row_stride;   // elements between activation rows m
+  int64_t x_k_stride;     // elements between activation groups of problems (0 = shared)
+  int64_t x_k_div;        // problem k reads activation group k / x_k_div
+  const int32_t* perm;    // rotation (modes RHT, SWIGLU_RHT)
+  const int8_t* sign;
+  int hb;
+  float rot_scale;
+  int M;                  // activation rows
+  // expert-indexed problems (nprob == 0): problem k uses expert e_ids[k] of one pool
+  const int16_t* idx0;    // [E, out, ng]
+  const uint8_t* idx1;    // [E, out, ng] or null
+  const void* scale;      // [E, out] val
+  void* y;                // [K, M, out] y_dtype
+  const int32_t* e_ids;   // [K] or null (problem k uses expert 0)
+  int64_t num_experts;
+  int64_t idx_e_stride;   // out * ng
+  int64_t scale_e_stride; // out
+  int64_t y_k_stride;     // elements between problems k
+  // multi-matrix problems (nprob > 0): problem p has its own weights/outputs, one shared x
+  int nprob;
+  const int16_t* p_idx0[kMaxProbs];
+  const uint8_t* p_idx1[kMaxProbs];
+  const void* p_scale[kMaxProbs];
+  void* p_y[kMaxProbs];
+  int p_out[kMaxProbs];
+  int p_rb0[kMaxProbs + 1];  // first row block of each problem
+  // common
+  const void* cb0;        // [65536, 8] val
+  const void* cb1;        // [256, 8] val or null
+  int y_dtype;
+  int64_t y_row_stride;   // elements between output rows m
+  int out;                // rows (expert-indexed mode)
+  int n;
+  float rs;
+  int K;                  // problems (expert-indexed mode)
+  int mtiles;             // M tiles
+  int row_blocks;         // row blocks per (problem, M tile) (expert mode) / total (multi mode)
+};
+
+// Launch the GEMV described by `a` (expert-indexed when a.nprob == 0, multi-matrix otherwise);
+// total_rows = rows of all problems (sizes the work split); res = 3 bpw.
+int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st);
+
+// Launch the routing-weighted combine out[t] = sum_j w[t, j] y[t*top_k + j] (+ add[t]) (moe.cu).
+int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H, const float* add, void* out,
+                int out_dtype, cudaStream_t st);
+
+}  // namespace vq2

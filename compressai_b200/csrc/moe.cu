@@ -1,7 +1,7 @@
 // MoE helper kernels: router (softmax top-k) and routing-weighted combine of expert outputs.
 #include <cfloat>
 
-#include "common.cuh"
+#include "gemv.cuh"
 
 namespace vq2 {
 
@@ -92,6 +92,15 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restric
   else static_cast<float*>(out)[i] = s;
 }
 
+int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H, const float* add, void* out,
+                int out_dtype, cudaStream_t st) {
+  const int64_t total = T * H;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > INT32_MAX) return VQ2_ERR_SHAPE;
+  return launch_kernel(moe_combine_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, y, w, T, top_k,
+                       H, add, out, out_dtype);
+}
+
 }  // namespace vq2
 
 extern "C" int vq2_moe_combine(const float* y, const float* w, int64_t T, int64_t top_k, int64_t H,
@@ -100,11 +109,7 @@ extern "C" int vq2_moe_combine(const float* y, const float* w, int64_t T, int64_
   if (!y || !w || !out) return VQ2_ERR_ARG;
   if (T <= 0 || top_k <= 0 || top_k > 64 || H <= 0) return VQ2_ERR_SHAPE;
   if (out_dtype != VQ2_F32 && out_dtype != VQ2_F16 && out_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
-  const int64_t total = T * H;
-  const int64_t blocks = (total + 255) / 256;
-  if (blocks > INT32_MAX) return VQ2_ERR_SHAPE;
-  return launch_kernel(moe_combine_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-                       static_cast<cudaStream_t>(stream), y, w, T, (int)top_k, H, add, out, out_dtype);
+  return run_combine(y, w, T, (int)top_k, H, add, out, out_dtype, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t K, int32_t* ids, float* w,

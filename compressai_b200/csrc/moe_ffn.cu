@@ -1,0 +1,94 @@
+// Routed-expert FFN of one MoE layer as one C-ABI call: gate_up GEMV (input RHT fused), down
+// GEMV (SwiGLU + RHT fused), routing-weighted combine -- three launches on one stream, the two
+// fp32 intermediates in a caller-provided workspace.
+// Semantics: the compute part of reference PagedMoEExpert.forward (vq2/paged_runtime.py:
+// 491-511, T > 1 :553-566) and PackedMoEExpertUniversal.forward
+// (vq2/load_and_test_full_35b.py:53-95), in fp32 with fp16 storage.
+#include "gemv.cuh"
+
+namespace vq2 {
+
+struct RecordLayout {
+  int64_t gu_idx, gu_scale, dn_idx, dn_scale, bytes;  // byte offsets within one expert record
+};
+
+static RecordLayout record_layout(int64_t gr, int64_t gc, int64_t dr, int64_t dc) {
+  RecordLayout r;
+  r.gu_idx = 0;
+  r.gu_scale = gr * gc * 2;
+  r.dn_idx = r.gu_scale + gr * 2;
+  r.dn_scale = r.dn_idx + dr * dc * 2;
+  r.bytes = r.dn_scale + dr * 2;
+  return r;
+}
+
+static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+int64_t moe_ffn_workspace(int64_t P, int64_t gu_rows, int64_t dn_rows) {
+  return align256(P * gu_rows * 4) + align256(P * dn_rows * 4);
+}
+
+// Shared body of vq2_moe_expert_ffn and its variants: `ws` must hold moe_ffn_workspace bytes.
+int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids, const float* w,
+                   const void* pool, int64_t num_experts, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                   int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
+                   int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
+                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st) {
+  if (!h || !ids || !w || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid || !ws || !out)
+    return VQ2_ERR_ARG;
+  if (T <= 0 || top_k <= 0 || top_k > 64 || num_experts <= 0) return VQ2_ERR_SHAPE;
+  if (gu_rows <= 0 || gu_rows % 2 != 0 || gu_cols % 8 != 0 || dn_cols % 8 != 0 || gu_cols <= 0 || dn_cols <= 0)
+    return VQ2_ERR_SHAPE;
+  if (dn_cols * 8 != gu_rows / 2 || dn_rows != gu_cols * 8) return VQ2_ERR_SHAPE;  // SwiGLU width / hidden size
+  if (h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (out_dtype != VQ2_F32 && out_dtype != VQ2_F16 && out_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  const RecordLayout L = record_layout(gu_rows, gu_cols, dn_rows, dn_cols);
+  if (L.bytes % 16 != 0 || L.dn_idx % 16 != 0) return VQ2_ERR_ALIGN;
+  if (!aligned(pool, 16) || !aligned(cb0, 16) || !aligned(ws, 256)) return VQ2_ERR_ALIGN;
+  const int64_t P = T * top_k;
+  if (P > INT32_MAX) return VQ2_ERR_SHAPE;
+  const int64_t H = gu_cols * 8, I = gu_rows / 2;
+  float* gu = static_cast<float*>(ws);
+  float* yd = reinterpret_cast<float*>(static_cast<char*>(ws) + align256(P * gu_rows * 4));
+  const char* base = static_cast<const char*>(pool);
+
+  GemvArgs a{};
+  a.nprob = 0;
+  a.x = h; a.x_dtype = h_dtype; a.x_mode = VQ2_ACT_RHT; a.x_row_stride = 0; a.x_k_stride = H; a.x_k_div = top_k;
+  a.perm = perm_in; a.sign = sign_in; a.hb = (int)hb_in; a.rot_scale = scale_in; a.M = 1;
+  a.idx0 = reinterpret_cast<const int16_t*>(base + L.gu_idx); a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr;
+  a.scale = base + L.gu_scale; a.y = gu; a.y_dtype = VQ2_F32; a.y_row_stride = 0; a.y_k_stride = gu_rows;
+  a.e_ids = ids; a.num_experts = num_experts; a.idx_e_stride = L.bytes / 2; a.scale_e_stride = L.bytes / 2;
+  a.out = (int)gu_rows; a.n = (int)H; a.rs = 1.f; a.K = (int)P;
+  int s = run_gemv(a, gu_rows * P, false, val_dtype, st);
+  if (s != VQ2_OK) return s;
+
+  GemvArgs b = a;
+  b.x = gu; b.x_dtype = VQ2_F32; b.x_mode = VQ2_ACT_SWIGLU_RHT; b.x_k_stride = gu_rows; b.x_k_div = 1;
+  b.perm = perm_mid; b.sign = sign_mid; b.hb = (int)hb_mid; b.rot_scale = scale_mid;
+  b.idx0 = reinterpret_cast<const int16_t*>(base + L.dn_idx); b.scale = base + L.dn_scale;
+  b.y = yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
+  s = run_gemv(b, dn_rows * P, false, val_dtype, st);
+  if (s != VQ2_OK) return s;
+  return run_combine(yd, w, T, (int)top_k, H, nullptr, out, out_dtype, st);
+}
+
+}  // namespace vq2
+
+extern "C" int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows, int64_t dn_rows) {
+  if (T <= 0 || top_k <= 0 || gu_rows <= 0 || dn_rows <= 0) return -1;
+  return vq2::moe_ffn_workspace(T * top_k, gu_rows, dn_rows);
+}
+
+extern "C" int vq2_moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids,
+                                  const float* w, const void* pool, int64_t num_experts, int64_t gu_rows,
+                                  int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
+                                  const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in,
+                                  const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid,
+                                  void* workspace, int64_t workspace_bytes, void* out, int out_dtype, void* stream) {
+  if (T <= 0 || top_k <= 0 || gu_rows <= 0 || dn_rows <= 0) return VQ2_ERR_SHAPE;
+  if (workspace_bytes < vq2::moe_ffn_workspace(T * top_k, gu_rows, dn_rows)) return VQ2_ERR_ARG;
+  return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
+                             cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
+                             scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream));
+}

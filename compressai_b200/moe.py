@@ -1,6 +1,7 @@
 """MoE expert path on VQ weights: router, resident expert pool, fused expert FFN.
 
-One MoE layer for T tokens with top-k routing is three launches on the device:
+One MoE layer for T tokens with top-k routing is one C-ABI call (vq2_moe_expert_ffn), three
+launches on the device:
 
 1. ``vq2_moe_gemv`` gate_up over the T*k (token, expert) problems -- each CTA rotates its
    token's hidden state (RHT 2048, fp32) in its prologue -- into fp32 [T*k, 1024];
@@ -80,22 +81,34 @@ def route(logits, top_k=8, hidden=None, shared_gate=None):
 
 
 def expert_ffn(hidden, ids, weights, pool, cb16, rot_in, rot_mid, top_k, out=None, out_dtype=None):
-    """sum_j w[t, j] * Expert_{ids[t, j]}(h[t]) for T tokens, three launches.
+    """sum_j w[t, j] * Expert_{ids[t*top_k + j]}(h[t]) for T tokens: one C-ABI call
+    (vq2_moe_expert_ffn, three launches) with its fp32 intermediates in a workspace from the
+    caching allocator.
 
     hidden: [T, H]; ids: int32 [T*top_k] device (pool rows: expert ids or slots); weights:
     fp32 [T, top_k]; pool: ExpertRecordPool on the device."""
+    _lib.require_cuda(hidden, ids, weights, cb16)
     T, H = hidden.shape
-    gr = pool.dims[0]
-    if H != rot_in.n or gr // 2 != rot_mid.n:
-        raise ValueError("rotation sizes do not match the expert shape")
+    gr, gc, dr, dc = pool.dims
+    if H != rot_in.n or gr // 2 != rot_mid.n or ids.numel() != T * top_k or ids.dtype != torch.int32:
+        raise ValueError("shape/dtype mismatch between hidden, ids, rotations and the expert pool")
+    if cb16.dtype != torch.float16:
+        raise ValueError("the expert pools hold fp16 scales; the codebook must be fp16")
     h = hidden.contiguous()
-    K = T * top_k
-    gu = torch.empty(K, gr, dtype=torch.float32, device=h.device)
-    kernels.moe_gemv(h, ids, pool.gu_idx, cb16, pool.gu_scale, gu, x_k_stride=H, x_k_div=top_k, rot=rot_in)
-    y = torch.empty(K, pool.dims[2], dtype=torch.float32, device=h.device)
-    kernels.moe_gemv(gu, ids, pool.dn_idx, cb16, pool.dn_scale, y, x_k_stride=gr, rot=rot_mid,
-                     mode=_lib.VQ2_ACT_SWIGLU_RHT)
-    return kernels.moe_combine(y, weights.float().contiguous(), top_k, out=out, out_dtype=out_dtype or hidden.dtype)
+    ids = ids.contiguous()
+    w = weights.float().contiguous()
+    out_dtype = out_dtype or hidden.dtype
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=h.device)
+    lib = _lib.load()
+    ws_bytes = lib.vq2_moe_expert_ffn_workspace(T, top_k, gr, dr)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=h.device)
+    _lib.call("vq2_moe_expert_ffn", _lib.ptr(h), _lib.dtype_code(h), T, top_k, _lib.ptr(ids), _lib.ptr(w),
+              _lib.ptr(pool.raw), pool.E, gr, gc, dr, dc, _lib.ptr(cb16), _lib.dtype_code(cb16),
+              _lib.ptr(rot_in.perm), _lib.ptr(rot_in.sign), rot_in.hb, float(rot_in.scale),
+              _lib.ptr(rot_mid.perm), _lib.ptr(rot_mid.sign), rot_mid.hb, float(rot_mid.scale),
+              _lib.ptr(ws), ws_bytes, _lib.ptr(out), _lib.dtype_code(out), _lib.stream_ptr(h.device))
+    return out
 
 
 class PackedMoEExpertUniversal(nn.Module):

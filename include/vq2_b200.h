@@ -167,6 +167,38 @@ VQ2_API int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t top
                           float* shared_w, void* stream);
 
 /*
+ * Routed-expert FFN of one MoE layer for T tokens with top_k experts each (P = T * top_k
+ * (token, expert) problems; three kernels on `stream`):
+ *   gu[p]  = GateUp_{ids[p]} . RHT_in(h[p / top_k])                  fp32 [P, gu_rows]
+ *   yd[p]  = Down_{ids[p]} . RHT_mid(silu(gu[p, :I]) * gu[p, I:])     fp32 [P, dn_rows]
+ *   out[t] = sum_j w[t, j] * yd[t * top_k + j]                        [T, H] in out_dtype
+ * with I = gu_rows / 2 = dn_cols * 8 and H = gu_cols * 8 = dn_rows. ids: int32 [P] device,
+ * rows of `pool` (expert ids of a resident pool or slots of a paged one; ids outside
+ * [0, num_experts) contribute zero); w: fp32 [T, top_k]. pool: num_experts expert records
+ * of the .vq2m payload layout, back to back: gate_up indices int16 [gu_rows, gu_cols], gate_up
+ * scales [gu_rows], down indices int16 [dn_rows, dn_cols], down scales [dn_rows] (scales in
+ * val_dtype), 16-byte aligned. RHT_in = (perm_in, sign_in, hb_in, scale_in), RHT_mid likewise
+ * (as vq2_rht forward). workspace: device memory of >= vq2_moe_expert_ffn_workspace(T, top_k,
+ * gu_rows, dn_rows) bytes, 256-byte aligned, holding gu and yd.
+ * Replaces: the compute of PagedMoEExpert.forward (vq2/paged_runtime.py:495-511, T > 1
+ * :553-566) and PackedMoEExpertUniversal.forward (vq2/load_and_test_full_35b.py:53-95):
+ * rot_2048.fwd, vq_moe_parallel_gate_up, SiLU*up, rot_512.fwd, vq_moe_parallel_down and the
+ * weighted sum, for all T tokens at once.
+ */
+VQ2_API int vq2_moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k,
+                               const int32_t* ids, const float* w, const void* pool,
+                               int64_t num_experts, int64_t gu_rows, int64_t gu_cols,
+                               int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
+                               const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in,
+                               float scale_in, const int32_t* perm_mid, const int8_t* sign_mid,
+                               int64_t hb_mid, float scale_mid, void* workspace,
+                               int64_t workspace_bytes, void* out, int out_dtype, void* stream);
+
+/* Workspace bytes vq2_moe_expert_ffn needs for T tokens x top_k experts (-1 on bad sizes). */
+VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows,
+                                             int64_t dn_rows);
+
+/*
  * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of rows
  * [0, rows) of cb (uniform row indices, the load form the GEMV uses). Timing it gives the
  * random codebook-gather rate that bounds the M = 1 VQ GEMV. sink: one uint32 of device memory.

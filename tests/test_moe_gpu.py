@@ -131,3 +131,34 @@ def test_paged_experts_outputs_and_lru(cbs, tmp_path, mode, T, cap):
             h = y.cpu().numpy().astype(np.float16)
     assert store.bytes_paged == sum(m.misses for m in mods) * store.expert_bytes
     store.close()
+
+
+def test_expert_ffn_abi_workspace_and_errors(cbs):
+    """vq2_moe_expert_ffn through the C-ABI: workspace sizing, too-small workspace refused,
+    out-of-range ids contribute zero."""
+    from compressai_b200 import _lib, vq
+    lib = _lib.load()
+    assert lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048) == 8 * 1024 * 4 + 8 * 2048 * 4
+    assert lib.vq2_moe_expert_ffn_workspace(0, 8, 1024, 2048) == -1
+    seed, E = 21, 6
+    pool = resident_pool(seed, E)
+    cb = cb16_dev(cbs)
+    r_in, r_mid = vq.get_rot("moe_expert_2048", 2048, DEV), vq.get_rot("moe_expert_512", 512, DEV)
+    T, K = 2, 3
+    h = torch.randn(T, 2048, device=DEV).half()
+    ids = torch.tensor([0, 5, 99, 2, -1, 3], dtype=torch.int32, device=DEV)
+    w = torch.rand(T, K, device=DEV)
+    out = torch.empty(T, 2048, device=DEV, dtype=torch.float32)
+    ws = torch.empty(lib.vq2_moe_expert_ffn_workspace(T, K, 1024, 2048), dtype=torch.uint8, device=DEV)
+    args = lambda nbytes: (_lib.ptr(h), _lib.VQ2_F16, T, K, _lib.ptr(ids), _lib.ptr(w), _lib.ptr(pool.raw), E, 1024,
+                           256, 2048, 64, _lib.ptr(cb), _lib.VQ2_F16, _lib.ptr(r_in.perm), _lib.ptr(r_in.sign), 2048,
+                           float(r_in.scale), _lib.ptr(r_mid.perm), _lib.ptr(r_mid.sign), 512, float(r_mid.scale),
+                           _lib.ptr(ws), nbytes, _lib.ptr(out), _lib.VQ2_F32, _lib.stream_ptr(DEV))
+    assert lib.vq2_moe_expert_ffn(*args(ws.numel() - 1)) == _lib.VQ2_ERR_ARG
+    _lib.call("vq2_moe_expert_ffn", *args(ws.numel()))
+    ids_np = ids.cpu().numpy().reshape(T, K)
+    wn = w.cpu().numpy()
+    zero = tuple(np.zeros_like(a) for a in synth.synth_expert(seed, 0))
+    expert = lambda e: synth.synth_expert(seed, e) if 0 <= e < E else zero
+    ref = O.moe_layer_ref(h.cpu().numpy(), ids_np, wn, expert, cbs["16"], ROT2048, ROT512)
+    assert rel_err(out.cpu().numpy(), ref) < 2e-5
