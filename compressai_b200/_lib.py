@@ -43,6 +43,8 @@ SIGNATURES = {
     "vq2_moe_expert_ffn": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
                            _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _p],
     "vq2_moe_expert_ffn_workspace": [_i64, _i64, _i64, _i64],
+    "vq2_moe_expert_ffn_noalloc": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p,
+                                   _i64, _f32, _p, _p, _i64, _f32, _p, _i32, _p],
 }
 ABI_VERSION = 1
 

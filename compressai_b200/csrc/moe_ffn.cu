@@ -4,6 +4,8 @@
 // Semantics: the compute part of reference PagedMoEExpert.forward (vq2/paged_runtime.py:
 // 491-511, T > 1 :553-566) and PackedMoEExpertUniversal.forward
 // (vq2/load_and_test_full_35b.py:53-95), in fp32 with fp16 storage.
+#include <atomic>
+
 #include "gemv.cuh"
 
 namespace vq2 {
@@ -91,4 +93,59 @@ extern "C" int vq2_moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
                              scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---- allocation-free variant -----------------------------------------------------------------
+// Scratch for vq2_moe_expert_ffn_noalloc: one static device array per device that loads this
+// library, held until the process exits. Every call on a device shares it, so calls that
+// overlap on the GPU (different streams, no ordering between them) race on it. The two
+// intermediates it holds (gate|up and down outputs) are written in full by each call before
+// they are read, so nothing needs clearing between calls.
+static __device__ __align__(256) unsigned char g_moe_ffn_scratch[VQ2_MOE_FFN_NOALLOC_MAX_BYTES];
+
+namespace vq2 {
+
+// Device address of g_moe_ffn_scratch for the current device. In host code the symbol names a
+// host-side stand-in, never the device array, so its address must come from
+// cudaGetSymbolAddress, called with the device current; the result is cached per device.
+static void* noalloc_scratch(int* status) {
+  static std::atomic<void*> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    *status = VQ2_ERR_LAUNCH;
+    return nullptr;
+  }
+  void* p = dev < 64 ? cache[dev].load() : nullptr;
+  if (p == nullptr) {
+    e = cudaGetSymbolAddress(&p, g_moe_ffn_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_last_cuda_error(e);
+      *status = VQ2_ERR_LAUNCH;
+      return nullptr;
+    }
+    if (dev < 64) cache[dev].store(p);
+  }
+  return p;
+}
+
+}  // namespace vq2
+
+extern "C" int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids,
+                                          const float* w, const void* pool, int64_t num_experts, int64_t gu_rows,
+                                          int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0,
+                                          int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
+                                          int64_t hb_in, float scale_in, const int32_t* perm_mid,
+                                          const int8_t* sign_mid, int64_t hb_mid, float scale_mid, void* out,
+                                          int out_dtype, void* stream) {
+  if (T <= 0 || top_k <= 0 || gu_rows <= 0 || dn_rows <= 0) return VQ2_ERR_SHAPE;
+  if (vq2::moe_ffn_workspace(T * top_k, gu_rows, dn_rows) > (int64_t)VQ2_MOE_FFN_NOALLOC_MAX_BYTES)
+    return VQ2_ERR_SHAPE;  // more (token, expert) problems than the static scratch holds
+  int status = VQ2_OK;
+  void* ws = vq2::noalloc_scratch(&status);
+  if (ws == nullptr) return status;
+  return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
+                             cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
+                             scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream));
 }

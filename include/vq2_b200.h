@@ -199,6 +199,35 @@ VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t g
                                              int64_t dn_rows);
 
 /*
+ * vq2_moe_expert_ffn without a workspace argument and without allocating anything, for
+ * callers that cannot obtain device memory at call time: code that enqueues work while a
+ * stream is being captured into a CUDA graph, plugin or real-time interfaces whose enqueue
+ * step must not allocate, and hosts reached through an FFI that have no device allocator of
+ * their own. No counterpart in the reference (its PyTorch code always allocates).
+ *
+ * The intermediates live in a static device array of VQ2_MOE_FFN_NOALLOC_MAX_BYTES inside this
+ * library, present on every GPU that loads it until the process exits. Limit: the call is
+ * refused with VQ2_ERR_SHAPE when vq2_moe_expert_ffn_workspace(T, top_k, gu_rows, dn_rows)
+ * exceeds that size (4 MiB: up to 341 (token, expert) problems at the 35B-A3B shape, e.g.
+ * T = 32 at top-8 plus a shared expert). The first call on a device looks up the array's
+ * device address with that device current; make that first call before starting any stream
+ * capture. All calls share the array: calls that may run concurrently on the GPU (on streams
+ * with no ordering between them) race on it and must be serialized by the caller. Each call
+ * overwrites the intermediates in full before reading them; nothing needs clearing.
+ * Otherwise identical to vq2_moe_expert_ffn.
+ */
+#define VQ2_MOE_FFN_NOALLOC_MAX_BYTES (4u * 1024u * 1024u)
+VQ2_API int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, int64_t top_k,
+                                       const int32_t* ids, const float* w, const void* pool,
+                                       int64_t num_experts, int64_t gu_rows, int64_t gu_cols,
+                                       int64_t dn_rows, int64_t dn_cols, const void* cb0,
+                                       int val_dtype, const int32_t* perm_in,
+                                       const int8_t* sign_in, int64_t hb_in, float scale_in,
+                                       const int32_t* perm_mid, const int8_t* sign_mid,
+                                       int64_t hb_mid, float scale_mid, void* out, int out_dtype,
+                                       void* stream);
+
+/*
  * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of rows
  * [0, rows) of cb (uniform row indices, the load form the GEMV uses). Timing it gives the
  * random codebook-gather rate that bounds the M = 1 VQ GEMV. sink: one uint32 of device memory.
