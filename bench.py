@@ -305,6 +305,116 @@ def run_ours(args, dist, rank, world):
     return res, stack
 
 
+# ------------------------------------------------------------------------------ MoE (config 3/5)
+def run_moe(args, dev, dist, world, T, steps, warmup):
+    """Decode step of a 40-layer stack of MoE blocks (256 routed experts + 1 shared, top-8,
+    SwiGLU 2048->512->2048 at 2 bpw, all resident): router kernel + expert FFN per layer on
+    device logits, in a CUDA graph. Expert bytes per layer = (distinct experts + shared) x
+    792,576 B."""
+    from compressai_b200 import moe, synth
+    L, E = args.moe_layers, 256
+    g = torch.Generator(device=dev).manual_seed(4321)
+    cb = torch.from_numpy(synth.random_codebooks(1)["16"]).to(dev)
+    blocks, logits = [], []
+    for _ in range(L):
+        pool = moe.ExpertRecordPool(E + 1, dev)
+        w16 = pool.raw.view(torch.int16)
+        w16.copy_(torch.randint(-32768, 32768, w16.shape, generator=g, device=dev, dtype=torch.int16))
+        pool.gu_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.gu_scale.shape, generator=g, device=dev)))
+        pool.dn_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.dn_scale.shape, generator=g, device=dev)))
+        ex = moe.PackedMoEExpertUniversal(pool, cb, dev, shared=True)
+        gate = 0.02 * torch.randn(HIDDEN, generator=g, device=dev)
+        blocks.append(moe.MoEBlock(ex, shared_gate=gate))
+        logits.append(torch.randn(T, E, generator=g, device=dev))
+    h0 = torch.randn(T, HIDDEN, generator=g, device=dev).half()
+
+    def step(h):
+        for blk, lg in zip(blocks, logits):
+            h = blk(h, lg)
+        return h
+
+    distinct = sum(int(torch.unique(moe.route(lg, 8)[0]).numel()) + 1 for lg in logits)
+    step_bytes = distinct * blocks[0].experts.pool.record_bytes
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        step(h0)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        out = step(h0)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            gr.replay()
+    barrier(dist)
+    t = max_over_ranks(time_graph(gr, steps, stream), dist)
+    peak = load_peaks()[0]
+    ach = step_bytes * steps / t / 1e9
+    res = {"T": T, "layers": L, "tok_s": round(world * T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
+           "expert_bytes_per_step": step_bytes, "distinct_experts_per_layer": round(distinct / L, 2),
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(ach / peak, 4)},
+           "launches_per_step": 4 * L, "finite": bool(torch.isfinite(out.float()).all())}
+    del gr, blocks
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------------------ paging (config 4)
+def run_paged(args, dev):
+    """40 MoE layers x 256 experts in a pinned host .vq2m image (8.12 GB); one PagedMoEExpert
+    per layer with 39 slots (1.25 GB of HBM: floor(1.25e9 / (40 x 792,576))); 512 decode steps
+    whose top-8 routing is the seeded Zipf(1.1) trace; hidden state chained through the layers."""
+    import numpy as np
+
+    from compressai_b200 import container, paged_runtime, synth
+    L, E, steps, cap = 40, 256, args.paged_steps, 39
+    t0 = time.perf_counter()
+    nbytes = container.RESERVED_HEADER_BYTES + L * E * synth.EXPERT_BYTES
+    pinned = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    container.synthetic_vq2m_image(L, E, seed=5, out=pinned.numpy())
+    store = paged_runtime.PagedModelStore.from_image(pinned, device=dev)
+    setup_s = time.perf_counter() - t0
+    cb = torch.from_numpy(synth.random_codebooks(1)["16"]).to(dev)
+    copy_stream = torch.cuda.Stream(dev)
+    mods = [paged_runtime.PagedMoEExpert(ln, store, cb, capacity=cap, device=dev, copy_stream=copy_stream)
+            for ln in range(L)]
+    trace = synth.zipf_trace(steps, L, seed=0)
+    w = torch.full((1, 8), 1.0 / 8)
+    h = torch.randn(1, HIDDEN, device=dev).half()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t1 = time.perf_counter()
+    e0.record()
+    for s in range(steps):
+        for ln in range(L):
+            h = mods[ln](h, torch.from_numpy(trace[s, ln][None].astype(np.int64)), w)
+    e1.record()
+    e1.synchronize()
+    wall = time.perf_counter() - t1
+    hits = sum(m.hits for m in mods)
+    misses = sum(m.misses for m in mods)
+    # H2D link bandwidth on the same pinned source, for the fraction
+    buf = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+    src = pinned[: 64 << 20]
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(10):
+        buf.copy_(src, non_blocking=True)
+    c1.record()
+    c1.synchronize()
+    h2d = 10 * buf.numel() / (c0.elapsed_time(c1) / 1e3) / 1e9
+    paged_gbs = store.bytes_paged / wall / 1e9
+    res = {"steps": steps, "layers": L, "capacity_per_layer": cap, "hbm_budget_bytes": L * cap * synth.EXPERT_BYTES,
+           "hit_rate": round(hits / (hits + misses), 4), "hits": hits, "misses": misses,
+           "bytes_paged": store.bytes_paged, "tok_s": round(steps / wall, 2), "ms_per_step": round(wall / steps * 1e3, 3),
+           "device_ms_per_step": round(e0.elapsed_time(e1) / steps, 3),
+           "paging_GBs": round(paged_gbs, 2), "h2d_link_GBs": round(h2d, 2), "link_frac": round(paged_gbs / h2d, 4),
+           "container_bytes": nbytes, "setup_s": round(setup_s, 1), "source": "pinned host image"}
+    del mods, store, pinned
+    torch.cuda.empty_cache()
+    return res
+
+
 def load_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -353,6 +463,9 @@ def main():
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--moe-layers", type=int, default=40)
+    ap.add_argument("--paged-steps", type=int, default=512)
+    ap.add_argument("--dense-only", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -376,6 +489,13 @@ def main():
                                        "cores": torch.get_num_threads(), "kind": "port",
                                        "sample": f"layer 0's 7 GEMVs x{reps} ({t:.1f} s), gather+einsum fp32 "
                                                  "(scratch/test_cpu_vq_gemv.py:53-70)"}
+            if not args.dense_only:
+                dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+                del stack
+                torch.cuda.empty_cache()
+                res["moe"] = [run_moe(args, dev, dist, world, T, args.steps, args.warmup) for T in (1, 32)]
+                if world == 1:
+                    res["paged"] = run_paged(args, dev)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:

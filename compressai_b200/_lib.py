@@ -38,7 +38,7 @@ SIGNATURES = {
     "vq2_moe_gemv": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i32,
                      _p, _i32, _i64, _i64, _f32, _p],
     "vq2_moe_combine": [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p],
-    "vq2_gather_probe": [_p, _i64, _i64, _i64, _p, _p],
+    "vq2_gather_probe": [_p, _i64, _i32, _i64, _i64, _p, _p],
     "vq2_moe_route": [_p, _i64, _i64, _i64, _p, _p, _p, _i32, _p, _i64, _p, _p],
     "vq2_moe_expert_ffn": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
                            _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _p],

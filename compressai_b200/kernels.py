@@ -236,15 +236,17 @@ def moe_combine(y, w, top_k, add=None, out=None, out_dtype=torch.float16):
     return out
 
 
-def gather_rate(cb, iters=256, blocks_per_sm=8, reps=5):
-    """Measured random 16-byte codebook-row gathers per second on cb's device (diagnostic)."""
+def gather_rate(cb, mode=0, rows=None, iters=256, blocks_per_sm=8, reps=5):
+    """Measured random 16-byte codebook-row gathers per second on cb's device (diagnostic;
+    mode 0 global memory, 1 shared memory, 2 cluster distributed shared memory)."""
     _lib.require_cuda(cb)
     dev = cb.device
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    blocks = sms * blocks_per_sm
+    blocks = sms * blocks_per_sm if mode == 0 else (sms if mode == 1 else sms // 8 * 8)
+    rows = rows or cb.shape[0]
     sink = torch.zeros(1, dtype=torch.int32, device=dev)
     st = _lib.stream_ptr(dev)
-    args = (_lib.ptr(cb), cb.shape[0], blocks, iters, _lib.ptr(sink), st)
+    args = (_lib.ptr(cb), rows, mode, blocks, iters, _lib.ptr(sink), st)
     _lib.call("vq2_gather_probe", *args)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()

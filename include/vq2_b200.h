@@ -228,13 +228,16 @@ VQ2_API int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, in
                                        void* stream);
 
 /*
- * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of rows
- * [0, rows) of cb (uniform row indices, the load form the GEMV uses). Timing it gives the
- * random codebook-gather rate that bounds the M = 1 VQ GEMV. sink: one uint32 of device memory.
- * No reference counterpart (measurement aid).
+ * Diagnostic: `blocks` x 256 threads each perform 8 * iters random 16-byte gathers of the rows
+ * of a [65536, 8] fp16/bf16 codebook cb, with uniform random row indices, through
+ *   mode 0: global memory (the GEMV's load form); rows <= 65536 limits the rows touched;
+ *   mode 1: shared memory (each CTA stages the first 12,288 rows; rows must be 65536);
+ *   mode 2: distributed shared memory of an 8-CTA cluster holding the whole table (rows 65536).
+ * Timing it gives the random codebook-gather rate that bounds the M = 1 VQ GEMV.
+ * sink: one uint32 of device memory. No reference counterpart (measurement aid).
  */
-VQ2_API int vq2_gather_probe(const void* cb, int64_t rows, int64_t blocks, int64_t iters,
-                             uint32_t* sink, void* stream);
+VQ2_API int vq2_gather_probe(const void* cb, int64_t rows, int mode, int64_t blocks,
+                             int64_t iters, uint32_t* sink, void* stream);
 
 #ifdef __cplusplus
 }
