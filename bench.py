@@ -309,24 +309,33 @@ def run_ours(args, dist, rank, world):
 def run_moe(args, dev, dist, world, T, steps, warmup):
     """Decode step of a 40-layer stack of MoE blocks (256 routed experts + 1 shared, top-8,
     SwiGLU 2048->512->2048 at 2 bpw, all resident): router kernel + expert FFN per layer on
-    device logits, in a CUDA graph. Expert bytes per layer = (distinct experts + shared) x
-    792,576 B."""
-    from compressai_b200 import moe, synth
+    device logits. N = 1: MoEBlock in a CUDA graph. N > 1: expert parallel -- each rank holds
+    256/N experts of every layer (+ the shared expert on rank 0), replicated router, one NCCL
+    all_reduce of the fp32 partial per layer. Expert bytes per layer = (distinct experts + shared)
+    x 792,576 B, all ranks together."""
+    from compressai_b200 import ep, moe, synth, vq
     L, E = args.moe_layers, 256
-    g = torch.Generator(device=dev).manual_seed(4321)
+    rank = dist.get_rank() if dist is not None else 0
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
     cb = torch.from_numpy(synth.random_codebooks(1)["16"]).to(dev)
+    gl = torch.Generator(device=dev).manual_seed(999)  # identical router inputs on every rank
+    lo, hi = ep.partition(E, world, rank)
+    n_local = (hi - lo) + (1 if rank == 0 else 0)
+    r_in, r_mid = vq.get_rot("moe_expert_2048", HIDDEN, dev), vq.get_rot("moe_expert_512", 512, dev)
     blocks, logits = [], []
     for _ in range(L):
-        pool = moe.ExpertRecordPool(E + 1, dev)
+        pool = moe.ExpertRecordPool(n_local if world > 1 else E + 1, dev)
         w16 = pool.raw.view(torch.int16)
         w16.copy_(torch.randint(-32768, 32768, w16.shape, generator=g, device=dev, dtype=torch.int16))
         pool.gu_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.gu_scale.shape, generator=g, device=dev)))
         pool.dn_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.dn_scale.shape, generator=g, device=dev)))
-        ex = moe.PackedMoEExpertUniversal(pool, cb, dev, shared=True)
-        gate = 0.02 * torch.randn(HIDDEN, generator=g, device=dev)
-        blocks.append(moe.MoEBlock(ex, shared_gate=gate))
-        logits.append(torch.randn(T, E, generator=g, device=dev))
-    h0 = torch.randn(T, HIDDEN, generator=g, device=dev).half()
+        gate = 0.02 * torch.randn(HIDDEN, generator=gl, device=dev)
+        if world > 1:
+            blocks.append(ep.ExpertParallelMoEBlock(pool, cb, E, r_in, r_mid, shared_gate=gate))
+        else:
+            blocks.append(moe.MoEBlock(moe.PackedMoEExpertUniversal(pool, cb, dev, shared=True), shared_gate=gate))
+        logits.append(torch.randn(T, E, generator=gl, device=dev))
+    h0 = torch.randn(T, HIDDEN, generator=gl, device=dev).half()
 
     def step(h):
         for blk, lg in zip(blocks, logits):
@@ -334,27 +343,52 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
         return h
 
     distinct = sum(int(torch.unique(moe.route(lg, 8)[0]).numel()) + 1 for lg in logits)
-    step_bytes = distinct * blocks[0].experts.pool.record_bytes
+    step_bytes = distinct * synth.EXPERT_BYTES
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         step(h0)
     torch.cuda.synchronize()
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gr, stream=stream):
-        out = step(h0)
+    gr, graphed = None, True
+    try:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            out = step(h0)
+    except Exception:  # capture of the NCCL all_reduce refused: time the eager step instead
+        gr, graphed = None, False
+        torch.cuda.synchronize()
+    barrier(dist)
+
+    def replay():
+        if gr is not None:
+            gr.replay()
+        else:
+            step(h0)
+
     with torch.cuda.stream(stream):
         for _ in range(warmup):
-            gr.replay()
+            replay()
     barrier(dist)
-    t = max_over_ranks(time_graph(gr, steps, stream), dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            replay()
+        e1.record(stream)
+    e1.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1e3, dist)
+    with torch.cuda.stream(stream):
+        out = step(h0)
+    torch.cuda.synchronize()
     peak = load_peaks()[0]
     ach = step_bytes * steps / t / 1e9
-    res = {"T": T, "layers": L, "tok_s": round(world * T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
+    res = {"T": T, "layers": L, "tok_s": round(T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
+           "parallelism": f"expert-parallel x{world}" if world > 1 else "single GPU",
            "expert_bytes_per_step": step_bytes, "distinct_experts_per_layer": round(distinct / L, 2),
-           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(ach / peak, 4)},
-           "launches_per_step": 4 * L, "finite": bool(torch.isfinite(out.float()).all())}
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world, "unit": "GB/s",
+                        "frac": round(ach / (peak * world), 4)},
+           "launches_per_step": 4 * L, "graph": graphed, "finite": bool(torch.isfinite(out.float()).all())}
     del gr, blocks
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return res
 

@@ -25,6 +25,8 @@ struct GemvArgs {
   const void* scale;      // [E, out] val
   void* y;                // [K, M, out] y_dtype
   const int32_t* e_ids;   // [K] or null (problem k uses expert 0)
+  const int32_t* prob_count;  // device problem count (<= K) or null: problems [count, K) are skipped
+  const int32_t* prob_map;    // [K] original problem index of each (compacted) problem, or null
   int64_t num_experts;
   int64_t idx_e_stride;   // out * ng
   int64_t scale_e_stride; // out
@@ -54,8 +56,14 @@ struct GemvArgs {
 // total_rows = rows of all problems (sizes the work split); res = 3 bpw.
 int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st);
 
-// Launch the routing-weighted combine out[t] = sum_j w[t, j] y[t*top_k + j] (+ add[t]) (moe.cu).
+// Launch the routing-weighted combine out[t] = sum_j w[t, j] y[t*top_k + j] (+ add[t]) (moe.cu);
+// with ids != null, rows whose id is outside [0, num_experts) are skipped.
 int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H, const float* add, void* out,
-                int out_dtype, cudaStream_t st);
+                int out_dtype, cudaStream_t st, const int32_t* ids = nullptr, int64_t num_experts = 0);
+
+// Stable compaction of the problems whose id is in [0, num_experts): out_ids[c] = ids[p],
+// out_map[c] = p, *out_count = number kept (moe.cu). One CTA; P <= 65536.
+int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
+                int32_t* out_count, cudaStream_t st);
 
 }  // namespace vq2

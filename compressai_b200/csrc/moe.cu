@@ -80,25 +80,74 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
 
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ y, const float* __restrict__ w,
                                                           int64_t T, int top_k, int64_t H,
-                                                          const float* __restrict__ add, void* out, int out_dtype) {
+                                                          const float* __restrict__ add, void* out, int out_dtype,
+                                                          const int32_t* __restrict__ ids, int64_t num_experts) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   pdl_wait();
   if (i >= T * H) return;
   const int64_t t = i / H, h = i - t * H;
   float s = add ? add[i] : 0.f;
-  for (int j = 0; j < top_k; ++j) s = fmaf(w[t * top_k + j], y[(t * top_k + j) * H + h], s);
+  for (int j = 0; j < top_k; ++j) {
+    const int64_t p = t * top_k + j;
+    if (ids && (ids[p] < 0 || ids[p] >= num_experts)) continue;  // problem not computed here
+    s = fmaf(w[p], y[p * H + h], s);
+  }
   if (out_dtype == VQ2_F16) static_cast<__half*>(out)[i] = __float2half_rn(s);
   else if (out_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(s);
   else static_cast<float*>(out)[i] = s;
 }
 
 int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H, const float* add, void* out,
-                int out_dtype, cudaStream_t st) {
+                int out_dtype, cudaStream_t st, const int32_t* ids, int64_t num_experts) {
   const int64_t total = T * H;
   const int64_t blocks = (total + 255) / 256;
   if (blocks > INT32_MAX) return VQ2_ERR_SHAPE;
   return launch_kernel(moe_combine_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, y, w, T, top_k,
-                       H, add, out, out_dtype);
+                       H, add, out, out_dtype, ids, num_experts);
+}
+
+// Stable compaction with one CTA of 1024 threads: per 1024-problem chunk, a ballot gives each
+// warp's count, a scan over the 32 warp counts gives offsets, and kept problems are written
+// in their original order.
+__global__ void __launch_bounds__(1024) moe_compact_kernel(const int32_t* __restrict__ ids, int64_t P,
+                                                           int64_t num_experts, int32_t* __restrict__ out_ids,
+                                                           int32_t* __restrict__ out_map, int32_t* __restrict__ count) {
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  for (int64_t c0 = 0; c0 < P; c0 += 1024) {
+    const int64_t p = c0 + threadIdx.x;
+    const int32_t id = p < P ? ids[p] : -1;
+    const bool keep = p < P && id >= 0 && id < num_experts;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int off = base;
+    for (int w = 0; w < warp; ++w) off += warp_tot[w];
+    if (keep) {
+      const int pos = off + __popc(m & ((1u << lane) - 1u));
+      out_ids[pos] = id;
+      out_map[pos] = static_cast<int32_t>(p);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tot = 0;
+      for (int w = 0; w < 32; ++w) tot += warp_tot[w];
+      base += tot;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = base;
+}
+
+int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
+                int32_t* out_count, cudaStream_t st) {
+  if (P <= 0 || P > 65536) return VQ2_ERR_SHAPE;
+  return launch_kernel(moe_compact_kernel, dim3(1), dim3(1024), 0, st, ids, P, num_experts, out_ids, out_map,
+                       out_count);
 }
 
 }  // namespace vq2

@@ -27,7 +27,7 @@ static RecordLayout record_layout(int64_t gr, int64_t gc, int64_t dr, int64_t dc
 static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
 int64_t moe_ffn_workspace(int64_t P, int64_t gu_rows, int64_t dn_rows) {
-  return align256(P * gu_rows * 4) + align256(P * dn_rows * 4);
+  return align256(P * gu_rows * 4) + align256(P * dn_rows * 4) + align256(P * 8 + 4);
 }
 
 // Shared body of vq2_moe_expert_ffn and its variants: `ws` must hold moe_ffn_workspace bytes.
@@ -48,11 +48,19 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   if (L.bytes % 16 != 0 || L.dn_idx % 16 != 0) return VQ2_ERR_ALIGN;
   if (!aligned(pool, 16) || !aligned(cb0, 16) || !aligned(ws, 256)) return VQ2_ERR_ALIGN;
   const int64_t P = T * top_k;
-  if (P > INT32_MAX) return VQ2_ERR_SHAPE;
+  if (P > 65536) return VQ2_ERR_SHAPE;
   const int64_t H = gu_cols * 8, I = gu_rows / 2;
   float* gu = static_cast<float*>(ws);
   float* yd = reinterpret_cast<float*>(static_cast<char*>(ws) + align256(P * gu_rows * 4));
+  int32_t* c_ids = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(yd) + align256(P * dn_rows * 4));
+  int32_t* c_map = c_ids + P;
+  int32_t* c_cnt = c_map + P;
   const char* base = static_cast<const char*>(pool);
+
+  // Only problems whose expert is in the pool are computed (remote experts of an expert-parallel
+  // rank are -1): compact them so the GEMV grid covers real work only.
+  int s = run_compact(ids, P, num_experts, c_ids, c_map, c_cnt, st);
+  if (s != VQ2_OK) return s;
 
   GemvArgs a{};
   a.nprob = 0;
@@ -60,9 +68,10 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   a.perm = perm_in; a.sign = sign_in; a.hb = (int)hb_in; a.rot_scale = scale_in; a.M = 1;
   a.idx0 = reinterpret_cast<const int16_t*>(base + L.gu_idx); a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr;
   a.scale = base + L.gu_scale; a.y = gu; a.y_dtype = VQ2_F32; a.y_row_stride = 0; a.y_k_stride = gu_rows;
-  a.e_ids = ids; a.num_experts = num_experts; a.idx_e_stride = L.bytes / 2; a.scale_e_stride = L.bytes / 2;
+  a.e_ids = c_ids; a.prob_count = c_cnt; a.prob_map = c_map;
+  a.num_experts = num_experts; a.idx_e_stride = L.bytes / 2; a.scale_e_stride = L.bytes / 2;
   a.out = (int)gu_rows; a.n = (int)H; a.rs = 1.f; a.K = (int)P;
-  int s = run_gemv(a, gu_rows * P, false, val_dtype, st);
+  s = run_gemv(a, gu_rows * P, false, val_dtype, st);
   if (s != VQ2_OK) return s;
 
   GemvArgs b = a;
@@ -72,7 +81,7 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   b.y = yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
   s = run_gemv(b, dn_rows * P, false, val_dtype, st);
   if (s != VQ2_OK) return s;
-  return run_combine(yd, w, T, (int)top_k, H, nullptr, out, out_dtype, st);
+  return run_combine(yd, w, T, (int)top_k, H, nullptr, out, out_dtype, st, ids, num_experts);
 }
 
 }  // namespace vq2

@@ -155,7 +155,6 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   const int sub = lane / LPR, li = lane % LPR;
   const int chunks = ng / (8 * LPR);
   const bool multi = a.nprob > 0;
-  const int64_t items = multi ? (int64_t)a.row_blocks * a.mtiles : (int64_t)a.row_blocks * a.K * a.mtiles;
   const uint4* cb0 = static_cast<const uint4*>(a.cb0);
   const uint64_t pol_s = policy_evict_first();
   const uint64_t pol_c = policy_evict_last();
@@ -163,7 +162,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 
   // One work item = RPC rows of one problem for one M tile. Each CTA owns a contiguous range
   // of items, so consecutive items mostly share their problem and activation tile.
-  struct Item { int rb, mt, k, out; int64_t e; const int16_t* i0; const uint8_t* i1; bool valid; };
+  struct Item { int rb, mt, k, o, out; int64_t e; const int16_t* i0; const uint8_t* i1; bool valid; };
   auto decode = [&](int64_t it) -> Item {
     Item w;
     if (multi) {
@@ -173,6 +172,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 #pragma unroll 1
       while (p + 1 < a.nprob && rbg >= a.p_rb0[p + 1]) ++p;
       w.k = p;
+      w.o = p;
       w.rb = rbg - a.p_rb0[p];
       w.out = a.p_out[p];
       w.e = 0;
@@ -184,6 +184,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
       const int64_t q = it / a.row_blocks;
       w.mt = (int)(q % a.mtiles);
       w.k = (int)(q / a.mtiles);
+      w.o = a.prob_map ? a.prob_map[w.k] : w.k;
       w.out = a.out;
       int64_t e = 0;
       w.valid = true;
@@ -213,9 +214,11 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     }
   };
 
-  const int64_t per = (items + gridDim.x - 1) / gridDim.x;
+  // Items are known before the dependency wait unless the problem count lives on the device.
+  const int64_t items_max = multi ? (int64_t)a.row_blocks * a.mtiles : (int64_t)a.row_blocks * a.K * a.mtiles;
+  int64_t per = (items_max + gridDim.x - 1) / gridDim.x;
   int64_t item = (int64_t)blockIdx.x * per;
-  const int64_t item_end = min(items, item + per);
+  int64_t item_end = min(items_max, item + per);
   int chunk = 0;
   uint4 iv[RW];
   uint2 jv[RW];
@@ -225,6 +228,13 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     load_idx(cur, 0, iv, jv);
   }
   pdl_wait();
+  if (!multi && a.prob_count) {  // device-side problem count (compacted problem lists)
+    const int kc = min(a.K, max(0, *a.prob_count));
+    const int64_t items = (int64_t)a.row_blocks * kc * a.mtiles;
+    per = (items + gridDim.x - 1) / gridDim.x;
+    item = (int64_t)blockIdx.x * per;
+    item_end = min(items, item + per);
+  }
   if (!weights_known && item < item_end) {
     cur = decode(item);
     load_idx(cur, 0, iv, jv);
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   while (item < item_end) {
     const int m0 = cur.mt * MT;
     const int mcount = min(MT, a.M - m0);
-    const int64_t xoff = (int64_t)m0 * a.x_row_stride + (multi ? 0 : (int64_t)(cur.k / a.x_k_div) * a.x_k_stride);
+    const int64_t xoff = (int64_t)m0 * a.x_row_stride + (multi ? 0 : (int64_t)(cur.o / a.x_k_div) * a.x_k_stride);
     if (xoff != cur_xoff) {  // uniform over the CTA
       __syncthreads();
       stage_activations<MT>(a, xoff, mcount, xs, xl, scratch);
@@ -327,7 +337,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
         const TV* sc = multi ? static_cast<const TV*>(a.p_scale[cur.k])
                              : static_cast<const TV*>(a.scale) + cur.e * a.scale_e_stride;
         void* ybase = multi ? a.p_y[cur.k] : a.y;
-        const int64_t yk = multi ? 0 : (int64_t)cur.k * a.y_k_stride;
+        const int64_t yk = multi ? 0 : (int64_t)cur.o * a.y_k_stride;
 #pragma unroll
         for (int rw = 0; rw < RW; ++rw) {
           const int r = cur.rb * RPC + warp * RPW + rw * RPL + sub;

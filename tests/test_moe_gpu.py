@@ -138,7 +138,7 @@ def test_expert_ffn_abi_workspace_and_errors(cbs):
     out-of-range ids contribute zero."""
     from compressai_b200 import _lib, vq
     lib = _lib.load()
-    assert lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048) == 8 * 1024 * 4 + 8 * 2048 * 4
+    assert lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048) == 8 * 1024 * 4 + 8 * 2048 * 4 + 256
     assert lib.vq2_moe_expert_ffn_workspace(0, 8, 1024, 2048) == -1
     seed, E = 21, 6
     pool = resident_pool(seed, E)
