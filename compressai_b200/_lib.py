@@ -33,8 +33,9 @@ SIGNATURES = {
     "vq2_rht": [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _f32, _i32, _p, _i64, _p],
     "vq2_swiglu_rht": [_p, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _i64, _p],
     "vq2_gemv_multi": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _i64, _p, _p, _p, _p, _p, _p, _i32, _p,
-                       _i32, _i64, _i64, _f32, _p],
-    "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p],
+                       _i32, _i64, _i64, _f32, _p, _i64, _p],
+    "vq2_gemv_workspace": [_i64, _i64],
+    "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p, _i64, _p],
     "vq2_moe_gemv": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i32,
                      _p, _i32, _i64, _i64, _f32, _p],
     "vq2_moe_combine": [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p],

@@ -54,7 +54,14 @@ struct GemvArgs {
 
 // Launch the GEMV described by `a` (expert-indexed when a.nprob == 0, multi-matrix otherwise);
 // total_rows = rows of all problems (sizes the work split); res = 3 bpw.
-int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st);
+int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st, void* ws = nullptr,
+             int64_t ws_bytes = 0);
+
+// Tensor-core batched path (vq_gemm_tc.cu) for multi-matrix problems on pre-rotated
+// activations; `ws` holds gemm_tc_workspace(M, n) bytes; returns -1 when not eligible.
+int run_gemm_tc(const GemvArgs& a, bool res, int val_dtype, void* ws, cudaStream_t st);
+// Workspace bytes of the tensor-core path: the 16-bit hi/lo split of the [M, n] activations.
+int64_t gemm_tc_workspace(int64_t M, int64_t n);
 
 // Launch the routing-weighted combine out[t] = sum_j w[t, j] y[t*top_k + j] (+ add[t]) (moe.cu);
 // with ids != null, rows whose id is outside [0, num_experts) are skipped.

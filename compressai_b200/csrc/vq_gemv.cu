@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 
 // ---- host dispatch ------------------------------------------------------------------------
 constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the SM's 256 KB stays L1
+constexpr int kTcMinRows = 8;           // activation rows from which the tensor-core path is used
 
 template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
 static int launch_cfg(GemvArgs a, cudaStream_t st) {
@@ -475,12 +476,16 @@ static int check_act(const GemvArgs& a) {
   return VQ2_OK;
 }
 
-int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st) {
+int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st, void* ws, int64_t ws_bytes) {
   const int lpr = pick_lpr(a.n / 8);
   if (lpr == 0) return VQ2_ERR_SHAPE;
   if ((int64_t)xs_len(a.n) * 4 > kMaxXsBytes) return VQ2_ERR_SHAPE;  // n <= 19264
   const int st_act = check_act(a);
   if (st_act != VQ2_OK) return st_act;
+  if (a.M >= kTcMinRows && a.nprob > 0 && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
+    const int r = run_gemm_tc(a, res, val_dtype, ws, st);  // batched: decode into tensor-core MMAs
+    if (r != -1) return r;
+  }
   const int mt = pick_mt(a.M, a.n);
   if (val_dtype == VQ2_F16)
     return res ? launch_lpr<true, __half>(a, total_rows, lpr, mt, st) : launch_lpr<false, __half>(a, total_rows, lpr, mt, st);
@@ -494,12 +499,17 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
 
 static bool dtype_ok(int d) { return d == VQ2_F32 || d == VQ2_F16 || d == VQ2_BF16; }
 
+extern "C" int64_t vq2_gemv_workspace(int64_t M, int64_t n) {
+  if (M <= 0 || n <= 0) return -1;
+  return M >= vq2::kTcMinRows ? vq2::gemm_tc_workspace(M, n) : 0;
+}
+
 extern "C" int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,
                               const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale, int64_t P,
                               const int16_t* const* idx0, const uint8_t* const* idx1, const int64_t* out,
                               const void* const* scale, const void* cb0, const void* cb1, int val_dtype,
                               void* const* y, int y_dtype, int64_t y_row_stride, int64_t n, float rs,
-                              void* stream) {
+                              void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace vq2;
   if (!x || !idx0 || !out || !scale || !y || !cb0) return VQ2_ERR_ARG;
   if (P <= 0 || P > kMaxProbs) return VQ2_ERR_SHAPE;
@@ -532,13 +542,13 @@ extern "C" int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M,
   a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale;
   a.M = (int)M; a.cb0 = cb0; a.cb1 = cb1; a.y_dtype = y_dtype; a.y_row_stride = y_row_stride;
   a.n = (int)n; a.rs = rs; a.K = 1; a.out = (int)max_out;
-  return run_gemv(a, total_rows, res, val_dtype, static_cast<cudaStream_t>(stream));
+  return run_gemv(a, total_rows, res, val_dtype, static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
 }
 
 extern "C" int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_stride, const int16_t* idx0,
                         const uint8_t* idx1, const void* cb0, const void* cb1, const void* scale, int val_dtype,
                         void* y, int y_dtype, int64_t y_row_stride, int64_t out, int64_t n, float rs,
-                        void* stream) {
+                        void* workspace, int64_t workspace_bytes, void* stream) {
   if (!xr || !idx0 || !cb0 || !scale || !y) return VQ2_ERR_ARG;
   if ((idx1 == nullptr) != (cb1 == nullptr)) return VQ2_ERR_ARG;
   if (out <= 0) return VQ2_ERR_SHAPE;
@@ -549,7 +559,8 @@ extern "C" int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_st
   const uint8_t* i1p[1] = {idx1};
   const int64_t op[1] = {out};
   return vq2_gemv_multi(xr, x_dtype, VQ2_ACT_ROTATED, M, x_row_stride, nullptr, nullptr, 0, 1.f, 1, i0p,
-                        idx1 ? i1p : nullptr, op, sp, cb0, cb1, val_dtype, yp, y_dtype, y_row_stride, n, rs, stream);
+                        idx1 ? i1p : nullptr, op, sp, cb0, cb1, val_dtype, yp, y_dtype, y_row_stride, n, rs,
+                        workspace, workspace_bytes, stream);
 }
 
 extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_stride, int64_t x_k_div,

@@ -23,6 +23,7 @@ import torch
 from . import _lib
 
 HAVE_TRITON = _lib.available()   # name kept for importers: "fused GPU kernels available"
+TC_MIN_ROWS = 8                  # activation rows from which the tensor-core GEMV is used
 HAVE_CUDA_KERNELS = HAVE_TRITON
 FUSED_KERNELS_ENABLED = True
 
@@ -68,10 +69,18 @@ def vq_gemv(xr, i0, cb0, scale, i1=None, cb1=None, rs=1.0, out_dtype=None, y=Non
     elif y.dtype != out_dtype or not y.is_contiguous():
         raise ValueError("y must be contiguous with dtype out_dtype")
     i0, i1, cb0, cb1, scale = _c(i0), _c(i1), _c(cb0), _c(cb1), _c(scale)
+    ws = _workspace(M, n, xr.device)
     _lib.call("vq2_gemv", _lib.ptr(x2), _lib.dtype_code(x2), M, x2.stride(0), _lib.ptr(i0), _lib.ptr(i1),
               _lib.ptr(cb0), _lib.ptr(cb1), _lib.ptr(scale), _lib.dtype_code(cb0), _lib.ptr(y),
-              _lib.dtype_code(y), out, out, n, float(rs), _lib.stream_ptr(xr.device))
+              _lib.dtype_code(y), out, out, n, float(rs), _lib.ptr(ws), ws.numel() if ws is not None else 0,
+              _lib.stream_ptr(xr.device))
     return y
+
+
+def _workspace(M, n, device):
+    """Device workspace of the batched (tensor-core) GEMV, from the caching allocator."""
+    nb = _lib.load().vq2_gemv_workspace(M, n)
+    return torch.empty(nb, dtype=torch.uint8, device=device) if nb > 0 else None
 
 
 def vq_gemv_16_8(xr, i0, i1, cb0, cb1, scale, out, n, rs=1.0):
@@ -118,6 +127,10 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     M = x2.shape[0]
+    if M >= TC_MIN_ROWS and mode != _lib.VQ2_ACT_ROTATED and n % 128 == 0:
+        # batched: rotate once with the standalone kernel, then the tensor-core GEMV
+        x2 = swiglu_rht(x2, rot) if mode == _lib.VQ2_ACT_SWIGLU_RHT else rot.fwd_f32(x2)
+        mode = _lib.VQ2_ACT_ROTATED
     res = mats[0][1] is not None
     _check_vals(cb0, cb1 if res else None, *[m[2] for m in mats])
     i0s, i1s, scs, outs = [], [], [], []
@@ -142,6 +155,7 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
         if y.numel() < o or (M > 1 and (y.dim() < 2 or y.shape[-2] < M)):
             raise ValueError("output too small")
     P = len(mats)
+    ws = _workspace(M, n, x.device) if mode == _lib.VQ2_ACT_ROTATED else None
     _lib.call("vq2_gemv_multi", _lib.ptr(x2), _lib.dtype_code(x2), int(mode), M, x2.stride(0),
               _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
               int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0, P,
@@ -151,7 +165,8 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
               _lib.ptr_array(ctypes.c_void_p, [t.data_ptr() for t in scs]),
               _lib.ptr(cb0), _lib.ptr(cb1) if res else None, _lib.dtype_code(cb0),
               _lib.ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), _lib.dtype_code(ys[0]),
-              int(y_row_stride), n, float(rs), _lib.stream_ptr(x.device))
+              int(y_row_stride), n, float(rs), _lib.ptr(ws), ws.numel() if ws is not None else 0,
+              _lib.stream_ptr(x.device))
     return ys
 
 

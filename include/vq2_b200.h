@@ -104,10 +104,21 @@ VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, in
                            int64_t P, const int16_t* const* idx0, const uint8_t* const* idx1,
                            const int64_t* out, const void* const* scale, const void* cb0,
                            const void* cb1, int val_dtype, void* const* y, int y_dtype,
-                           int64_t y_row_stride, int64_t n, float rs, void* stream);
+                           int64_t y_row_stride, int64_t n, float rs, void* workspace,
+                           int64_t workspace_bytes, void* stream);
 
 /*
- * VQ GEMV on a pre-rotated activation, one matrix (vq2_gemv_multi with P = 1, mode ROTATED):
+ * Workspace bytes vq2_gemv_multi / vq2_gemv use for M activation rows of length n (0 below 8
+ * rows; -1 on bad sizes). With M >= 8, mode ROTATED and n % 128 == 0 the GEMV runs on the
+ * tensor cores (mma.sync m16n8k16 fed directly by the codebook gathers, activations split into
+ * 16-bit hi + lo halves held in the workspace, 16-byte aligned); with no workspace, or one too
+ * small, it runs on the CUDA cores with the same result.
+ */
+VQ2_API int64_t vq2_gemv_workspace(int64_t M, int64_t n);
+
+/*
+ * VQ GEMV on a pre-rotated activation, one matrix (vq2_gemv_multi with P = 1, mode ROTATED;
+ * workspace as there, may be NULL):
  *   y[m, r] = rs * scale[r] * sum_g dot(cb0[idx0[r, g]] (+ cb1[idx1[r, g]]), xr[m, 8g:8g+8])
  * Replaces: vq_gemv_16 / vq_gemv_16_8 (vq2/kernels.py:215-230) and the Triton kernels
  * _vq_gemv_16 / _vq_gemv_16_8 (vq2/kernels.py:32-78), which handle M = 1 only.
@@ -115,7 +126,8 @@ VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, in
 VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_stride,
                      const int16_t* idx0, const uint8_t* idx1, const void* cb0, const void* cb1,
                      const void* scale, int val_dtype, void* y, int y_dtype, int64_t y_row_stride,
-                     int64_t out, int64_t n, float rs, void* stream);
+                     int64_t out, int64_t n, float rs, void* workspace, int64_t workspace_bytes,
+                     void* stream);
 
 /*
  * Expert-indexed VQ GEMV over K problems (2 bpw):

@@ -37,16 +37,16 @@ def test_argument_validation_without_device():
     lib = _lib.load()
     p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
     # null activation
-    assert lib.vq2_gemv(None, 2, 1, 2048, p, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None) == _lib.VQ2_ERR_ARG
+    assert lib.vq2_gemv(None, 2, 1, 2048, p, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_ARG
     # n not a multiple of 64
-    assert lib.vq2_gemv(p, 2, 1, 2040, p, None, p, None, p, 0, p, 0, 2048, 2048, 2040, 1.0, None) == _lib.VQ2_ERR_SHAPE
+    assert lib.vq2_gemv(p, 2, 1, 2040, p, None, p, None, p, 0, p, 0, 2048, 2048, 2040, 1.0, None, 0, None) == _lib.VQ2_ERR_SHAPE
     # bad dtype code
-    assert lib.vq2_gemv(p, 7, 1, 2048, p, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None) == _lib.VQ2_ERR_DTYPE
+    assert lib.vq2_gemv(p, 7, 1, 2048, p, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_DTYPE
     # misaligned index pointer
     q = ctypes.c_void_p(18)
-    assert lib.vq2_gemv(p, 2, 1, 2048, q, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None) == _lib.VQ2_ERR_ALIGN
+    assert lib.vq2_gemv(p, 2, 1, 2048, q, None, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_ALIGN
     # residual index without residual codebook
-    assert lib.vq2_gemv(p, 2, 1, 2048, p, p, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None) == _lib.VQ2_ERR_ARG
+    assert lib.vq2_gemv(p, 2, 1, 2048, p, p, p, None, p, 0, p, 0, 2048, 2048, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_ARG
     # RHT block size not a power of two
     assert lib.vq2_rht(p, 2, 2048, 1, 2048, 1000, p, p, 1.0, 0, p, 2048, None) == _lib.VQ2_ERR_SHAPE
     # moe: zero experts
@@ -62,7 +62,8 @@ def test_argument_validation_without_device():
     arr = (ctypes.c_void_p * 9)(*([16] * 9))
     outs = (ctypes.c_int64 * 9)(*([64] * 9))
     assert lib.vq2_gemv_multi(p, 2, 0, 1, 2048, None, None, 0, 1.0, 9, arr, None, outs, arr, p, None, 0, arr, 0,
-                              64, 2048, 1.0, None) == _lib.VQ2_ERR_SHAPE
+                              64, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_SHAPE
+    assert lib.vq2_gemv_workspace(4, 2048) == 0 and lib.vq2_gemv_workspace(16, 2048) == 2 * 16 * 2048 * 2
     assert lib.vq2_moe_combine(p, p, 1, 0, 2048, None, p, 0, None) == _lib.VQ2_ERR_SHAPE
 
 

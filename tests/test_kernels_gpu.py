@@ -307,3 +307,41 @@ def test_moe_gemv_fused_modes(cbs):
             act_r = O.rht_fwd(O.silu(g[:512]) * g[512:], *rot512)
             ref = O.vq_gemv_legacy(act_r, dn_i[e], cbs["16"], dn_s[e], 1.0)
             assert rel_err(y_dn[t * K + j].cpu().numpy(), ref) < 2e-5
+
+
+@pytest.mark.parametrize("M", [8, 24, 64, 100])
+@pytest.mark.parametrize("bits", [(16,), (16, 8)])
+@pytest.mark.parametrize("cbdt", [torch.float16, torch.bfloat16])
+def test_tensor_core_batched_gemv(cbs, M, bits, cbdt):
+    """M >= 8 runs on the tensor cores (activations split hi + lo): fp32 outputs agree with the
+    fp64 oracle to fp32-accumulation accuracy, for fp16 and bf16 codebooks, 2 and 3 bpw."""
+    out, n = 300, 2048
+    idx, scale = synth.random_matrix(M + len(bits), out, n, bits)
+    cbd = dev_cbs(cbs, cbdt)
+    cb_np = {k: v.float().cpu().numpy() for k, v in cbd.items()}   # the values the kernel sees
+    sc = torch.from_numpy(scale).to(DEV, cbdt)
+    x = np.random.default_rng(M).standard_normal((M, n)).astype(np.float32)
+    xr = torch.from_numpy(x).to(DEV)
+    i0 = torch.from_numpy(idx[0]).to(DEV)
+    i1 = torch.from_numpy(idx[1]).to(DEV) if len(bits) > 1 else None
+    y = kernels.vq_gemv(xr, i0, cbd["16"], sc, i1=i1, cb1=cbd["16_8"] if i1 is not None else None,
+                        out_dtype=torch.float32).cpu().numpy()
+    ref = np.stack([O.vq_gemv_legacy(x[m], idx[0], cb_np["16"], sc.float().cpu().numpy(), 1.0,
+                                     idx[1] if len(bits) > 1 else None, cb_np["16_8"]) for m in range(M)])
+    assert rel_err(y, ref) < 3e-5
+
+
+def test_tensor_core_path_without_workspace_falls_back_exactly(cbs):
+    """vq2_gemv with M >= 8 but no workspace runs the CUDA-core kernel: same result."""
+    from compressai_b200 import _lib
+    idx, scale = synth.random_matrix(3, 256, 2048)
+    cbd = dev_cbs(cbs)
+    x = torch.randn(16, 2048, device=DEV)
+    i0 = torch.from_numpy(idx[0]).to(DEV)
+    sc = torch.from_numpy(scale).to(DEV)
+    y_tc = kernels.vq_gemv(x, i0, cbd["16"], sc, out_dtype=torch.float32)
+    y_cc = torch.empty(16, 256, device=DEV)
+    _lib.call("vq2_gemv", _lib.ptr(x), _lib.VQ2_F32, 16, 2048, _lib.ptr(i0), None, _lib.ptr(cbd["16"]), None,
+              _lib.ptr(sc), _lib.VQ2_F16, _lib.ptr(y_cc), _lib.VQ2_F32, 256, 256, 2048, 1.0, None, 0,
+              _lib.stream_ptr(DEV))
+    assert rel_err(y_cc.cpu().numpy(), y_tc.cpu().numpy()) < 3e-5
