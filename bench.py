@@ -38,6 +38,9 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 HIDDEN, INTER, VOCAB = 2048, 6144, 151936
+# DRAM bytes of one lm_head GEMV launch (ncu dram__bytes rate x duration) over its algorithmic
+# bytes: 81.26 MB / 78.39 MB (profiles/vq_gemv_m1.md)
+NCU_TRAFFIC_RATIO = 1.037
 METRIC = "VQ GEMV HBM GB/s (compressed bytes)"
 UNIT = "GB/s"
 WORKLOAD = ("config2 decode step: 24 layers x (q,k,v,o 2048x2048; gate,up 2048->6144; down 6144->2048) "
@@ -293,7 +296,11 @@ def run_ours(args, dist, rank, world):
                 "ms_per_step": round(t_e2e / args.steps * 1e3, 4)},
         "roofline": {"bound": "hbm", "kernel": "vq_gemv_kernel", "achieved": round(achieved, 1),
                      "peak": peaks[0], "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
-                     "peak_source": peaks[1], "traffic": None,
+                     "peak_source": peaks[1],
+                     "traffic": round(NCU_TRAFFIC_RATIO * step_bytes / n_gemv, 0),
+                     "traffic_source": "ncu dram bytes of one lm_head launch / its algorithmic bytes = "
+                                       f"{NCU_TRAFFIC_RATIO} (profiles/vq_gemv_m1.md), x the mean "
+                                       "algorithmic bytes per launch",
                      "avg_launch_us": round(per_launch_s * 1e6, 3), "launches_per_step": n_gemv,
                      "gather_ceiling": {"measured_gathers_per_s": round(gather_ceiling, 0),
                                         "achieved_gathers_per_s": round(step_idx / (t_gemv / args.steps), 0),
@@ -449,6 +456,55 @@ def run_paged(args, dev):
     return res
 
 
+# ------------------------------------------------------------------------------ config-2 sweep
+def run_sweep(dev, Ms=(1, 4, 16, 64), reps=10):
+    """Per-launch device time of each config-2 shape x {2, 3} bpw x M on pre-rotated inputs,
+    over a rotating pool of distinct weight copies of >= 4x L2, in a CUDA graph."""
+    import math
+
+    from compressai_b200 import kernels, synth
+    cbn = synth.random_codebooks(1)
+    cb0, cb1 = (torch.from_numpy(cbn[k]).to(dev) for k in ("16", "16_8"))
+    g = torch.Generator(device=dev).manual_seed(77)
+    st = torch.cuda.Stream(dev)
+    out = []
+    for (rows, n) in [(HIDDEN, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER), (VOCAB, HIDDEN)]:
+        for bits in (2, 3):
+            nbytes = rows * (n // 8) * (3 if bits == 3 else 2)
+            copies = max(2, min(64, math.ceil(4 * 126e6 / nbytes)))
+            i0s = [torch.randint(-32768, 32768, (rows, n // 8), generator=g, device=dev, dtype=torch.int16)
+                   for _ in range(copies)]
+            i1s = [torch.randint(0, 256, (rows, n // 8), generator=g, device=dev, dtype=torch.uint8)
+                   for _ in range(copies)] if bits == 3 else [None] * copies
+            sc = (0.02 * torch.ones(rows, device=dev)).half()
+            for M in Ms:
+                xr = torch.randn(M, n, generator=g, device=dev)
+                y = torch.empty(M, rows, device=dev, dtype=torch.float16)
+
+                def body():
+                    for c in range(copies):
+                        kernels.vq_gemv(xr, i0s[c], cb0, sc, i1=i1s[c], cb1=cb1 if bits == 3 else None, y=y,
+                                        out_dtype=torch.float16)
+                with torch.cuda.stream(st):
+                    body()
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=st):
+                    body()
+                with torch.cuda.stream(st):
+                    gr.replay()
+                t = time_graph(gr, reps, st) / (reps * copies)
+                alg = gemv_bytes(rows, n, M, bits == 3)
+                out.append({"out": rows, "n": n, "bpw": bits, "M": M, "us": round(t * 1e6, 2),
+                            "GBs": round(alg / t / 1e9, 1), "gathers_per_s": round(rows * n / 8 / t, 0),
+                            "path": "tensor cores (mma.sync)" if (M >= 8 or (M >= 2 and rows >= 16384))
+                            else "CUDA cores"})
+                del gr
+            del i0s, i1s
+            torch.cuda.empty_cache()
+    return out
+
+
 def load_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -528,6 +584,8 @@ def main():
                 del stack
                 torch.cuda.empty_cache()
                 res["moe"] = [run_moe(args, dev, dist, world, T, args.steps, args.warmup) for T in (1, 32)]
+                if world == 1:
+                    res["sweep"] = run_sweep(dev)
                 if world == 1:
                     res["paged"] = run_paged(args, dev)
         if rank == 0 and res is not None:

@@ -371,6 +371,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 // ---- host dispatch ------------------------------------------------------------------------
 constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the SM's 256 KB stays L1
 constexpr int kTcMinRows = 8;           // activation rows from which the tensor-core path is used
+constexpr int64_t kTcTallRows = 16384;  // ...or from 2 rows when the matrices have this many rows
 
 template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
 static int launch_cfg(GemvArgs a, cudaStream_t st) {
@@ -482,7 +483,10 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
   if ((int64_t)xs_len(a.n) * 4 > kMaxXsBytes) return VQ2_ERR_SHAPE;  // n <= 19264
   const int st_act = check_act(a);
   if (st_act != VQ2_OK) return st_act;
-  if (a.M >= kTcMinRows && a.nprob > 0 && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
+  // Tensor cores from 8 activation rows, or from 2 when the matrices are tall enough to fill
+  // the GPU with 128-row items (measured: lm_head at M = 4 is faster there than on CUDA cores).
+  const bool tc = a.M >= kTcMinRows || (a.M >= 2 && total_rows >= kTcTallRows);
+  if (tc && a.nprob > 0 && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
     const int r = run_gemm_tc(a, res, val_dtype, ws, st);  // batched: decode into tensor-core MMAs
     if (r != -1) return r;
   }
@@ -501,7 +505,7 @@ static bool dtype_ok(int d) { return d == VQ2_F32 || d == VQ2_F16 || d == VQ2_BF
 
 extern "C" int64_t vq2_gemv_workspace(int64_t M, int64_t n) {
   if (M <= 0 || n <= 0) return -1;
-  return M >= vq2::kTcMinRows ? vq2::gemm_tc_workspace(M, n) : 0;
+  return M >= 2 ? vq2::gemm_tc_workspace(M, n) : 0;
 }
 
 extern "C" int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,

@@ -127,7 +127,8 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     M = x2.shape[0]
-    if M >= TC_MIN_ROWS and mode != _lib.VQ2_ACT_ROTATED and n % 128 == 0:
+    tall = sum(m[0].shape[0] for m in mats) >= 16384
+    if (M >= TC_MIN_ROWS or (M >= 2 and tall)) and mode != _lib.VQ2_ACT_ROTATED and n % 128 == 0:
         # batched: rotate once with the standalone kernel, then the tensor-core GEMV
         x2 = swiglu_rht(x2, rot) if mode == _lib.VQ2_ACT_SWIGLU_RHT else rot.fwd_f32(x2)
         mode = _lib.VQ2_ACT_ROTATED

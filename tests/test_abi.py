@@ -63,7 +63,7 @@ def test_argument_validation_without_device():
     outs = (ctypes.c_int64 * 9)(*([64] * 9))
     assert lib.vq2_gemv_multi(p, 2, 0, 1, 2048, None, None, 0, 1.0, 9, arr, None, outs, arr, p, None, 0, arr, 0,
                               64, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_SHAPE
-    assert lib.vq2_gemv_workspace(4, 2048) == 0 and lib.vq2_gemv_workspace(16, 2048) == 2 * 16 * 2048 * 2
+    assert lib.vq2_gemv_workspace(1, 2048) == 0 and lib.vq2_gemv_workspace(4, 2048) == 2 * 4 * 2048 * 2 and lib.vq2_gemv_workspace(16, 2048) == 2 * 16 * 2048 * 2
     assert lib.vq2_moe_combine(p, p, 1, 0, 2048, None, p, 0, None) == _lib.VQ2_ERR_SHAPE
 
 
