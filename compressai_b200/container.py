@@ -13,6 +13,12 @@ Layout (identical to the reference so files interchange; reference vq2/pack_35b_
   ``other_tensors`` and ``expert_modes``);
 * payload from 2 MiB: per layer, per expert, the four tensors back to back, so one expert is a
   single contiguous record of ``expert_bytes`` bytes (792,576 B at the 35B-A3B shape).
+
+ANS-coded variant (this repository's extension; meta ``"index_coding": "vq2a"``): the two index
+entries of each expert point at VQ2A rANS streams of the index bytes (compressai_b200.ans) and
+their sizes are the stream sizes; scales stay stored. A record is still contiguous, of variable
+size, and a paged miss copies it compressed and expands it into the slot on the GPU. Readers that
+do not know the key see the header unchanged and reject the mismatched sizes.
 """
 import json
 import os
@@ -50,9 +56,39 @@ class Vq2mLayout:
         self.dn_rows = meta.get("dn_rows", 2048)
         self.dn_cols = meta.get("dn_cols", 64)
 
+        self.index_coding = meta.get("index_coding", "raw")
+        if self.index_coding not in ("raw", "vq2a"):
+            raise ValueError(f"unknown index_coding {self.index_coding!r}")
+
     @property
     def expert_bytes(self):
+        """Bytes of one decoded expert record (the pool slot size)."""
         return record_bytes(self.gu_rows, self.gu_cols, self.dn_rows, self.dn_cols)
+
+    @property
+    def ans_coded(self):
+        return self.index_coding == "vq2a"
+
+    @property
+    def max_record_bytes(self):
+        """Largest stored record (== expert_bytes for raw containers)."""
+        m = 0
+        for row in self.table:
+            for (og, sg, os_, ss, od, sd, ods, sds) in row:
+                if sg:
+                    m = max(m, sg + ss + sd + sds)
+        return m
+
+    def segments(self, layer, expert):
+        """Decode plan of one record, relative to the record start: [(src_off, src_bytes,
+        dst_off, n, kind)] for gate_up indices, gate_up scales, down indices, down scales
+        (kind 0 = VQ2A stream, 1 = stored); dst offsets follow the decoded record layout."""
+        og, sg, os_, ss, od, sd, ods, sds = self.table[layer][expert]
+        n_gi, n_gs = self.gu_rows * self.gu_cols * 2, self.gu_rows * 2
+        n_di, n_ds = self.dn_rows * self.dn_cols * 2, self.dn_rows * 2
+        k = 0 if self.ans_coded else 1
+        return [(0, sg, 0, n_gi, k), (os_ - og, ss, n_gi, n_gs, 1), (od - og, sd, n_gi + n_gs, n_di, k),
+                (ods - og, sds, n_gi + n_gs + n_di, n_ds, 1)]
 
     def record(self, layer, expert):
         """(offset, nbytes) of the contiguous record of one expert; raises if the four tensors
@@ -81,6 +117,11 @@ def parse_header(head, file_size=None):
     table = [ents[ln * ne:(ln + 1) * ne] for ln in range(nl)]
     meta = json.loads(bytes(head[moff:moff + mlen]).decode("utf-8"))
     lay = Vq2mLayout(nl, ne, pstart, table, meta)
+    if lay.ans_coded:  # stored scales must have the dimensions' sizes
+        for row in table:
+            for (og, sg, os_, ss, od, sd, ods, sds) in row:
+                if sg and (ss, sds) != (lay.gu_rows * 2, lay.dn_rows * 2):
+                    raise ValueError("corrupt .vq2m: expert scale sizes disagree with the dimensions")
     if file_size is not None:
         for row in table:
             for (og, sg, os_, ss, od, sd, ods, sds) in row:
@@ -131,19 +172,47 @@ def _table_and_meta(num_layers, num_experts, dims, meta_extra):
     return table, meta, off
 
 
-def write_vq2m(path, num_layers, num_experts, expert_fn, dims=None, meta_extra=None):
+def write_vq2m(path, num_layers, num_experts, expert_fn, dims=None, meta_extra=None, index_coding="raw"):
     """Write a .vq2m whose expert (layer, e) is ``expert_fn(layer, e)`` = (gu_idx int16,
-    gu_scale fp16, dn_idx int16, dn_scale fp16). Returns the file size."""
+    gu_scale fp16, dn_idx int16, dn_scale fp16). index_coding "vq2a" stores the index tensors
+    as VQ2A rANS streams (host encoder of the C-ABI library). Returns the file size."""
     dims = dict(DEFAULT_DIMS, **(dims or {}))
-    table, meta, end = _table_and_meta(num_layers, num_experts, dims, meta_extra)
+    if index_coding == "raw":
+        table, meta, end = _table_and_meta(num_layers, num_experts, dims, meta_extra)
+        with open(path, "wb") as f:
+            f.write(_header_bytes(num_layers, num_experts, table, meta))
+            for ln in range(num_layers):
+                for e in range(num_experts):
+                    for a in _typed(expert_fn(ln, e)):
+                        f.write(a.tobytes())
+        return end
+    if index_coding != "vq2a":
+        raise ValueError(f"unknown index_coding {index_coding!r}")
+    from . import ans
+    _, meta, _ = _table_and_meta(num_layers, num_experts, dims, dict(meta_extra or {}, index_coding="vq2a"))
+    table = [[None] * num_experts for _ in range(num_layers)]
+    off = RESERVED_HEADER_BYTES
     with open(path, "wb") as f:
-        f.write(_header_bytes(num_layers, num_experts, table, meta))
+        f.write(b"\x00" * RESERVED_HEADER_BYTES)
         for ln in range(num_layers):
             for e in range(num_experts):
-                gi, gs, di, ds = expert_fn(ln, e)
-                for a, dt in ((gi, np.int16), (gs, np.float16), (di, np.int16), (ds, np.float16)):
-                    f.write(np.ascontiguousarray(a, dtype=dt).tobytes())
-    return end
+                gi, gs, di, ds = _typed(expert_fn(ln, e))
+                parts = [ans.encode(gi), gs.view(np.uint8), ans.encode(di), ds.view(np.uint8)]
+                ent = []
+                for p in parts:
+                    ent += [off, p.size]
+                    f.write(p.tobytes())
+                    off += p.size
+                table[ln][e] = tuple(ent)
+        f.seek(0)
+        f.write(_header_bytes(num_layers, num_experts, table, meta))
+    return off
+
+
+def _typed(parts):
+    gi, gs, di, ds = parts
+    return (np.ascontiguousarray(gi, dtype=np.int16), np.ascontiguousarray(gs, dtype=np.float16),
+            np.ascontiguousarray(di, dtype=np.int16), np.ascontiguousarray(ds, dtype=np.float16))
 
 
 def write_synthetic_vq2m(path, num_layers, num_experts, seed=0, **dims):

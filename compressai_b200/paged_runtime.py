@@ -23,7 +23,7 @@ import numpy as np
 import torch
 import torch.nn as nn
 
-from . import container, moe, vq
+from . import ans, container, moe, vq
 
 DEVICE = "cuda" if torch.cuda.is_available() else "cpu"
 
@@ -70,6 +70,10 @@ class PagedModelStore:
         self.gu_rows, self.gu_cols = lay.gu_rows, lay.gu_cols
         self.dn_rows, self.dn_cols = lay.dn_rows, lay.dn_cols
         self.expert_bytes = lay.expert_bytes
+        self.ans_coded = lay.ans_coded
+        self.max_record_bytes = lay.max_record_bytes if lay.ans_coded else lay.expert_bytes
+        self._dev_stage = {}     # (device, stream) -> device buffer of one compressed record
+        self._ans_status = {}    # device -> int32 decode status word
         self._staging = None
         self._staging_next = 0
         self.bytes_paged = 0
@@ -91,7 +95,8 @@ class PagedModelStore:
         return None
 
     def read_record(self, layer_idx, expert_id, out=None):
-        """Copy one expert record into a host buffer (numpy/tensor uint8) and return it."""
+        """Copy one stored expert record (compressed in an ANS-coded container) into a host
+        buffer (numpy/tensor uint8) and return it."""
         off, nb = self.layout.record(layer_idx, expert_id)
         if out is None:
             out = np.empty(nb, dtype=np.uint8)
@@ -109,7 +114,7 @@ class PagedModelStore:
     def _staging_ring(self):
         if self._staging is None:
             pin = torch.cuda.is_available()
-            self._staging = [(torch.empty(self.expert_bytes, dtype=torch.uint8, pin_memory=pin),
+            self._staging = [(torch.empty(self.max_record_bytes, dtype=torch.uint8, pin_memory=pin),
                               torch.cuda.Event() if pin else None) for _ in range(self.STAGING_BUFFERS)]
         return self._staging
 
@@ -117,12 +122,16 @@ class PagedModelStore:
         """Copy one expert record into device memory ``dst`` (uint8 [expert_bytes]) on
         ``stream`` without blocking the host on the copy: pinned images go straight to the
         device; other sources pass through a ring of pinned staging buffers, each reused only
-        after its previous copy has completed."""
+        after its previous copy has completed. In an ANS-coded container the compressed record
+        is copied into a device staging buffer of this stream and one decode launch expands it
+        into ``dst`` (decode errors raise the status word read by check_decode_status)."""
         src = self._host_record(layer_idx, expert_id)
         stream = stream or torch.cuda.current_stream(dst.device)
+        _, nb = self.layout.record(layer_idx, expert_id)
+        land = self._device_stage(dst.device, stream)[:nb] if self.ans_coded else dst
         if isinstance(src, torch.Tensor) and src.is_pinned():
             with torch.cuda.stream(stream):
-                dst.copy_(src, non_blocking=True)
+                land.copy_(src, non_blocking=True)
         else:
             ring = self._staging_ring()
             buf, ev = ring[self._staging_next]
@@ -130,9 +139,48 @@ class PagedModelStore:
             ev.synchronize()  # the previous copy out of this buffer is done
             self.read_record(layer_idx, expert_id, out=buf)
             with torch.cuda.stream(stream):
-                dst.copy_(buf, non_blocking=True)
+                land.copy_(buf[:nb], non_blocking=True)
                 ev.record(stream)
-        self.bytes_paged += self.expert_bytes
+        if self.ans_coded:
+            # same stream as the copy in and the next copy into this staging buffer: ordered
+            ans.decode_segments(land, self.layout.segments(layer_idx, expert_id), dst,
+                                self.decode_status(dst.device), stream)
+        self.bytes_paged += nb
+
+    def _device_stage(self, device, stream):
+        key = (str(device), stream.cuda_stream)
+        buf = self._dev_stage.get(key)
+        if buf is None:
+            buf = torch.empty(self.max_record_bytes, dtype=torch.uint8, device=device)
+            self._dev_stage[key] = buf
+        return buf
+
+    def decode_status(self, device):
+        """The device status word shared by every ANS decode of this store on ``device``."""
+        key = str(torch.device(device))
+        st = self._ans_status.get(key)
+        if st is None:
+            st = ans.new_status(device)
+            self._ans_status[key] = st
+        return st
+
+    def check_decode_status(self):
+        """Synchronize and raise ans.ANSDecodeError if any decode met a malformed stream."""
+        for st in self._ans_status.values():
+            ans.check_status(st)
+
+    def read_expert_record(self, layer_idx, expert_id):
+        """Decoded record of one expert (host uint8 [expert_bytes]); ANS-coded records are
+        decoded on the GPU."""
+        if not self.ans_coded:
+            return self.read_record(layer_idx, expert_id)
+        if not torch.cuda.is_available():
+            raise RuntimeError("ANS-coded containers are decoded on the GPU; no CUDA device is available")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        out = torch.empty(self.expert_bytes, dtype=torch.uint8, device=dev)
+        self.load_record_async(layer_idx, expert_id, out, torch.cuda.current_stream(dev))
+        self.check_decode_status()
+        return out.cpu().numpy()
 
     # ---- reference-compatible accessors -----------------------------------------------------
     def _split(self, rec):
@@ -148,14 +196,14 @@ class PagedModelStore:
     def get_expert_weights(self, layer_idx, expert_id, device="cpu"):
         """(gu_idx int16, gu_scale fp16, dn_idx int16, dn_scale fp16) of one expert
         (vq2/paged_runtime.py:175-207; scales stay fp16 on every device)."""
-        parts = self._split(torch.from_numpy(self.read_record(layer_idx, expert_id)))
+        parts = self._split(torch.from_numpy(self.read_expert_record(layer_idx, expert_id)))
         return tuple(p.clone() if str(device) == "cpu" else p.to(device) for p in parts)
 
     def load_expert_into_slot(self, layer_idx, expert_id, slot, pool_gu_idx, pool_gu_scale, pool_dn_idx,
                               pool_dn_scale, device=None):
         """Copy one expert into slot `slot` of four separate pool tensors (reference signature,
         vq2/paged_runtime.py:125-173); scales are converted to the pool's dtype."""
-        gi, gs, di, ds = self._split(torch.from_numpy(self.read_record(layer_idx, expert_id)))
+        gi, gs, di, ds = self._split(torch.from_numpy(self.read_expert_record(layer_idx, expert_id)))
         nb = pool_gu_idx.is_cuda
         pool_gu_idx[slot].copy_(gi, non_blocking=False)
         pool_gu_scale[slot].copy_(gs.to(pool_gu_scale.dtype), non_blocking=nb)

@@ -27,6 +27,17 @@ def synth_expert(seed, e, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_
     return gu_idx, gu_sc, dn_idx, dn_sc
 
 
+def synth_expert_skewed(seed, e, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_cols=DN_COLS,
+                        sigma=3000.0):
+    """As synth_expert, but indices |N(0, sigma)| (clipped to 65535): a codebook whose rows are
+    ordered by usage, the case where ANS coding of the index bytes pays (about 0.82 of the
+    stored size at sigma 3000)."""
+    gu_idx, gu_sc, dn_idx, dn_sc = synth_expert(seed, e, gu_rows, gu_cols, dn_rows, dn_cols)
+    rng = np.random.default_rng([int(seed), int(e), 0x5EED])
+    skew = lambda shape: np.minimum(np.abs(rng.normal(0.0, sigma, shape)), 65535).astype(np.uint16).view(np.int16)
+    return skew(gu_idx.shape), gu_sc, skew(dn_idx.shape), dn_sc
+
+
 def zipf_trace(steps, layers, seed=0, num_experts=256, top_k=8, s=1.1):
     """Routing trace [steps, layers, top_k] (int16) with a Zipf(s) expert popularity per layer.
 

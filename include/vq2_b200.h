@@ -251,6 +251,48 @@ VQ2_API int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, in
 VQ2_API int vq2_gather_probe(const void* cb, int64_t rows, int mode, int64_t blocks,
                              int64_t iters, uint32_t* sink, void* stream);
 
+/*
+ * ---- ANS-coded index streams ("VQ2A" interleaved rANS) ----
+ * Replaces the entropy coding of vq2/export.py:26-36 (constriction AnsCoder over the index
+ * bytes), which the reference runs on the host; here an ANS-coded container's index tensors
+ * are byte streams that a paged miss copies to the device and vq2_rans_decode expands there.
+ * Format (little-endian): u32 magic 0x41325156, u32 n_symbols, u32 n_chunks =
+ * ceil(n_symbols / 8192), u32 0, u16 freq[2][256] (context = symbol position parity, each row
+ * sums to 4096, no zero), u32 chunk_off[n_chunks + 1] (last = total size), zero pad to 16
+ * bytes; chunk c = u32 state[64], u16 nwords[64], then the u16 words of stream 0, 1, ... in
+ * decode order, zero pad to 16. Stream w codes chunk symbols w, w + 64, ...; rANS with 32-bit
+ * state, L = 2^16, 16-bit words, 12-bit scale; a stream holds at most one word per symbol and
+ * ends at state L with all its words used.
+ */
+/* Upper bound on the encoded size of n_symbols bytes (-1 if n_symbols is out of range). */
+VQ2_API int64_t vq2_rans_bound(int64_t n_symbols);
+/* Host encoder: symbols -> out (host memory, out_capacity >= vq2_rans_bound); *out_bytes = size. */
+VQ2_API int vq2_rans_encode(const uint8_t* symbols, int64_t n_symbols, uint8_t* out,
+                            int64_t out_capacity, int64_t* out_bytes);
+/*
+ * GPU decoder, asynchronous on `cuda_stream`: stream (device, stream_bytes long) -> out (device,
+ * n_symbols <= out_capacity bytes). *status (device int32) must be zero before the first decode;
+ * a malformed stream raises it to a nonzero code (1 magic, 2 counts, 3 frequencies, 4 chunk
+ * offsets, 5 word counts, 6 words exhausted, 7 bad final state) and decodes never lower it, so
+ * several decodes can share one status word that the caller reads after synchronizing. All
+ * reads stay inside stream_bytes and all writes inside out[0, n_symbols) whatever the stream
+ * holds. n_symbols = 0 decodes nothing and checks nothing.
+ */
+VQ2_API int vq2_rans_decode(const void* stream, int64_t stream_bytes, int64_t n_symbols,
+                            void* out, int64_t out_capacity, int32_t* status, void* cuda_stream);
+/*
+ * One launch over 1..8 segments of src (device, src_bytes) into dst (device, dst_bytes):
+ * segment i reads src[seg_src_off[i], + seg_src_bytes[i]) and writes dst[seg_dst_off[i],
+ * + seg_n[i]); seg_kind 0 = a VQ2A stream of seg_n symbols, 1 = stored bytes (seg_src_bytes ==
+ * seg_n, copied). The offset arrays are host memory. Status as for vq2_rans_decode. Used to
+ * expand one ANS-coded expert record (compressed indices, stored scales) into its pool slot.
+ */
+VQ2_API int vq2_rans_decode_segments(const void* src, int64_t src_bytes,
+                                     const int64_t* seg_src_off, const int64_t* seg_src_bytes,
+                                     const int64_t* seg_dst_off, const int64_t* seg_n,
+                                     const int32_t* seg_kind, int64_t nseg, void* dst,
+                                     int64_t dst_bytes, int32_t* status, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif
