@@ -401,18 +401,25 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
 
 
 # ------------------------------------------------------------------------------ paging (config 4)
-def run_paged(args, dev):
-    """40 MoE layers x 256 experts in a pinned host .vq2m image (8.12 GB); one PagedMoEExpert
+def run_paged(args, dev, coding="raw"):
+    """40 MoE layers x 256 experts in a pinned host .vq2m image (8.12 GB raw); one PagedMoEExpert
     per layer with 39 slots (1.25 GB of HBM: floor(1.25e9 / (40 x 792,576))); 512 decode steps
-    whose top-8 routing is the seeded Zipf(1.1) trace; hidden state chained through the layers."""
+    whose top-8 routing is the seeded Zipf(1.1) trace; hidden state chained through the layers.
+    coding "vq2a": the ANS-coded container (64 distinct skewed-index experts tiled over the
+    grid); each miss copies the compressed record and decodes it on the GPU."""
     import numpy as np
 
     from compressai_b200 import container, paged_runtime, synth
     L, E, steps, cap = 40, 256, args.paged_steps, 39
     t0 = time.perf_counter()
-    nbytes = container.RESERVED_HEADER_BYTES + L * E * synth.EXPERT_BYTES
-    pinned = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    container.synthetic_vq2m_image(L, E, seed=5, out=pinned.numpy())
+    if coding == "raw":
+        nbytes = container.RESERVED_HEADER_BYTES + L * E * synth.EXPERT_BYTES
+        pinned = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        container.synthetic_vq2m_image(L, E, seed=5, out=pinned.numpy())
+    else:
+        nbytes = container.ans_image_size(L, E, seed=5)
+        pinned = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        container.synthetic_ans_vq2m_image(L, E, seed=5, out=pinned.numpy())
     store = paged_runtime.PagedModelStore.from_image(pinned, device=dev)
     setup_s = time.perf_counter() - t0
     cb = torch.from_numpy(synth.random_codebooks(1)["16"]).to(dev)
@@ -420,7 +427,8 @@ def run_paged(args, dev):
     mods = [paged_runtime.PagedMoEExpert(ln, store, cb, capacity=cap, device=dev, copy_stream=copy_stream)
             for ln in range(L)]
     trace = synth.zipf_trace(steps, L, seed=0)
-    w = torch.full((1, 8), 1.0 / 8)
+    ids_host = [[torch.from_numpy(trace[s, ln][None].astype(np.int64)) for ln in range(L)] for s in range(steps)]
+    w = torch.full((1, 8), 1.0 / 8, device=dev)  # router weights stay on the device; ids come to the host
     h = torch.randn(1, HIDDEN, device=dev).half()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -428,7 +436,7 @@ def run_paged(args, dev):
     e0.record()
     for s in range(steps):
         for ln in range(L):
-            h = mods[ln](h, torch.from_numpy(trace[s, ln][None].astype(np.int64)), w)
+            h = mods[ln](h, ids_host[s][ln], w)
     e1.record()
     e1.synchronize()
     wall = time.perf_counter() - t1
@@ -450,7 +458,12 @@ def run_paged(args, dev):
            "bytes_paged": store.bytes_paged, "tok_s": round(steps / wall, 2), "ms_per_step": round(wall / steps * 1e3, 3),
            "device_ms_per_step": round(e0.elapsed_time(e1) / steps, 3),
            "paging_GBs": round(paged_gbs, 2), "h2d_link_GBs": round(h2d, 2), "link_frac": round(paged_gbs / h2d, 4),
-           "container_bytes": nbytes, "setup_s": round(setup_s, 1), "source": "pinned host image"}
+           "container_bytes": nbytes, "setup_s": round(setup_s, 1), "source": "pinned host image",
+           "index_coding": coding}
+    if coding != "raw":
+        store.check_decode_status()
+        res["record_bytes_vs_raw"] = round(store.bytes_paged / (misses * synth.EXPERT_BYTES), 4)
+        res["indices"] = "skewed |N(0, 3000)| (synth_expert_skewed), 64 distinct experts tiled"
     del mods, store, pinned
     torch.cuda.empty_cache()
     return res
@@ -588,6 +601,7 @@ def main():
                     res["sweep"] = run_sweep(dev)
                 if world == 1:
                     res["paged"] = run_paged(args, dev)
+                    res["paged_ans"] = run_paged(args, dev, coding="vq2a")
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:

@@ -50,7 +50,18 @@ SIGNATURES = {
     "vq2_rans_encode": [_p, _i64, _p, _i64, _p],
     "vq2_rans_decode": [_p, _i64, _i64, _p, _i64, _p, _p],
     "vq2_rans_decode_segments": [_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p],
+    "vq2_paged_moe_step": [_p, _p, _i32, _i64, _i64, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i32, _p],
 }
+
+
+class PagedLayer(ctypes.Structure):
+    """Mirror of ``vq2_paged_layer`` (include/vq2_b200.h), field for field."""
+    _fields_ = [("pool", _p), ("capacity", _i64), ("gu_rows", _i64), ("gu_cols", _i64), ("dn_rows", _i64),
+                ("dn_cols", _i64), ("cb0", _p), ("val_dtype", ctypes.c_int32), ("index_coding", ctypes.c_int32),
+                ("perm_in", _p), ("sign_in", _p), ("hb_in", _i64), ("perm_mid", _p), ("sign_mid", _p),
+                ("hb_mid", _i64), ("scale_in", _f32), ("scale_mid", _f32), ("stage", _p), ("stage_bytes", _i64),
+                ("status", _p), ("ids_host", _p), ("ids_dev", _p), ("ids_cap", _i64), ("copy_stream", _p),
+                ("copy_done", _p), ("compute_done", _p), ("ids_done", _p)]
 ABI_VERSION = 1
 
 _lib = None

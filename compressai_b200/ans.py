@@ -70,8 +70,8 @@ def decode(stream, n, out=None, status=None):
 
 
 def decode_segments(src, segments, dst, status, stream=None):
-    """One launch expanding ``segments`` [(src_off, src_bytes, dst_off, n, kind), ...] of the
-    device buffer ``src`` into the device buffer ``dst`` (kind SEG_ANS or SEG_STORED)."""
+    """One launch expanding ``segments`` [(src_off, src_bytes, dst_off, n, kind), ...] (at most
+    32) of the device buffer ``src`` into the device buffer ``dst`` (kind SEG_ANS or SEG_STORED)."""
     nseg = len(segments)
     arr = [np.ascontiguousarray([s[i] for s in segments], dtype=np.int64) for i in range(4)]
     kind = np.ascontiguousarray([s[4] for s in segments], dtype=np.int32)

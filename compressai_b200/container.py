@@ -253,3 +253,54 @@ def synthetic_vq2m_image(num_layers, num_experts, seed=0, out=None, **dims):
             boff += n + 4096
             pos += n
     return img[:end], end
+
+
+def synthetic_ans_vq2m_image(num_layers, num_experts, seed=0, distinct=64, out=None, **dims):
+    """ANS-coded (index_coding "vq2a") .vq2m image in memory for paging benchmarks: ``distinct``
+    skewed-index experts (synth.synth_expert_skewed) are encoded once and their records tiled
+    over the (layer, expert) grid, expert (l, e) taking record (l * num_experts + e) % distinct.
+    Returns (image, size); ``out`` (e.g. a pinned buffer of at least ``size`` bytes) may be
+    given, else use ``ans_image_size`` first to size it."""
+    from . import ans
+    d = dict(DEFAULT_DIMS, **dims)
+    recs = []
+    for i in range(distinct):
+        gi, gs, di, ds = _typed(synth.synth_expert_skewed(seed, i, d["gu_rows"], d["gu_cols"], d["dn_rows"],
+                                                          d["dn_cols"]))
+        recs.append([ans.encode(gi), gs.view(np.uint8), ans.encode(di), ds.view(np.uint8)])
+    _, meta, _ = _table_and_meta(num_layers, num_experts, d, {"index_coding": "vq2a"})
+    table = [[None] * num_experts for _ in range(num_layers)]
+    off = RESERVED_HEADER_BYTES
+    for ln in range(num_layers):
+        for e in range(num_experts):
+            ent = []
+            for p in recs[(ln * num_experts + e) % distinct]:
+                ent += [off, p.size]
+                off += p.size
+            table[ln][e] = tuple(ent)
+    img = np.empty(off, dtype=np.uint8) if out is None else out
+    if img.nbytes < off:
+        raise ValueError(f"output buffer too small: {img.nbytes} < {off}")
+    img[:RESERVED_HEADER_BYTES] = np.frombuffer(_header_bytes(num_layers, num_experts, table, meta), np.uint8)
+    flat = [np.concatenate(r) for r in recs]
+    for ln in range(num_layers):
+        for e in range(num_experts):
+            r = flat[(ln * num_experts + e) % distinct]
+            o = table[ln][e][0]
+            img[o:o + r.size] = r
+    return img[:off], off
+
+
+def ans_image_size(num_layers, num_experts, seed=0, distinct=64, **dims):
+    """Size in bytes of synthetic_ans_vq2m_image with the same arguments."""
+    from . import ans
+    d = dict(DEFAULT_DIMS, **dims)
+    sizes = []
+    for i in range(distinct):
+        gi, gs, di, ds = _typed(synth.synth_expert_skewed(seed, i, d["gu_rows"], d["gu_cols"], d["dn_rows"],
+                                                          d["dn_cols"]))
+        sizes.append(ans.encode(gi).size + gs.nbytes + ans.encode(di).size + ds.nbytes)
+    total = RESERVED_HEADER_BYTES
+    for k in range(num_layers * num_experts):
+        total += sizes[k % distinct]
+    return total

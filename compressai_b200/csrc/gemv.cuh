@@ -73,4 +73,19 @@ int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H,
 int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
                 int32_t* out_count, cudaStream_t st);
 
+// Routed-expert FFN of one MoE layer (moe_ffn.cu): compaction, gate_up GEMV (input RHT),
+// down GEMV (SwiGLU + RHT), combine; `ws` holds moe_ffn_workspace(T * top_k, ...) bytes.
+int64_t moe_ffn_workspace(int64_t P, int64_t gu_rows, int64_t dn_rows);
+int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids, const float* w,
+                   const void* pool, int64_t num_experts, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                   int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
+                   int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
+                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st);
+
+// VQ2A decode of up to 32 segments of src into dst in one launch (rans.cu); status as
+// vq2_rans_decode_segments.
+int ans_launch(const uint8_t* src, int64_t src_bytes, const int64_t* src_off, const int64_t* seg_bytes,
+               const int64_t* dst_off, const int64_t* seg_n, const int32_t* kind, int64_t nseg, uint8_t* dst,
+               int64_t dst_bytes, int32_t* status, cudaStream_t st);
+
 }  // namespace vq2

@@ -16,7 +16,7 @@
 #include <cstring>
 #include <vector>
 
-#include "common.cuh"
+#include "gemv.cuh"
 
 namespace vq2 {
 
@@ -121,7 +121,7 @@ static int64_t ans_encode(const uint8_t* sym, int64_t n, uint8_t* out, int64_t c
 }
 
 // ---- GPU decoder ------------------------------------------------------------------------------
-// One launch decodes a list of segments (<= 8) of one source buffer into one destination: kind 0
+// One launch decodes a list of segments (<= 32) of one source buffer into one destination: kind 0
 // segments are VQ2A streams, kind 1 segments are stored bytes (copied). An ANS-coded expert
 // record is four segments (gate_up indices, gate_up scales, down indices, down scales), so a paged
 // miss is one H2D copy of the compressed record and one launch that writes the whole slot.
@@ -138,7 +138,7 @@ static int64_t ans_encode(const uint8_t* sym, int64_t n, uint8_t* out, int64_t c
 enum AnsError { kAnsOk = 0, kAnsBadMagic = 1, kAnsBadCount = 2, kAnsBadFreq = 3, kAnsBadChunk = 4,
                 kAnsBadWords = 5, kAnsUnderflow = 6, kAnsBadFinal = 7 };
 enum AnsKind { kSegAns = 0, kSegStored = 1 };
-constexpr int kAnsMaxSegs = 8;
+constexpr int kAnsMaxSegs = 32;  // 8 expert records of 4 segments
 constexpr int kAnsWarps = 4;
 constexpr int kStoredBlockBytes = 128 * 16 * 4;  // bytes one CTA copies for a stored segment
 constexpr int kWordStage = 2 * kAnsChunk + 16;   // a chunk's words (<= one per symbol) + slack
@@ -348,8 +348,8 @@ __global__ void __launch_bounds__(128) ans_decode_kernel(AnsSegs a, int32_t* __r
   if (err != kAnsOk) atomicMax(status, err);
 }
 
-// Validate the segment list, fill the kernel parameters and launch.
-static int ans_launch(const uint8_t* src, int64_t src_bytes, const int64_t* src_off, const int64_t* seg_bytes,
+// Validate the segment list, fill the kernel parameters and launch (also used by the pager).
+int ans_launch(const uint8_t* src, int64_t src_bytes, const int64_t* src_off, const int64_t* seg_bytes,
                       const int64_t* dst_off, const int64_t* seg_n, const int32_t* kind, int64_t nseg, uint8_t* dst,
                       int64_t dst_bytes, int32_t* status, cudaStream_t st) {
   if (!src || !dst || !status || !src_off || !seg_bytes || !dst_off || !seg_n || !kind) return VQ2_ERR_ARG;

@@ -14,6 +14,7 @@
   over tokens. There is no CPU compute path: CPU devices may hold the bookkeeping (for tests)
   but forward() on them raises.
 """
+import ctypes
 import mmap
 import os
 import threading
@@ -23,7 +24,7 @@ import numpy as np
 import torch
 import torch.nn as nn
 
-from . import ans, container, moe, vq
+from . import _lib, ans, container, moe, vq
 
 DEVICE = "cuda" if torch.cuda.is_available() else "cpu"
 
@@ -72,7 +73,8 @@ class PagedModelStore:
         self.expert_bytes = lay.expert_bytes
         self.ans_coded = lay.ans_coded
         self.max_record_bytes = lay.max_record_bytes if lay.ans_coded else lay.expert_bytes
-        self._dev_stage = {}     # (device, stream) -> device buffer of one compressed record
+        self._dev_stage = {}     # (device, stream) -> staging ring / buffer for compressed records
+        self._rec_cache = {}     # (layer, expert) -> (offset, bytes, segment plan)
         self._ans_status = {}    # device -> int32 decode status word
         self._staging = None
         self._staging_next = 0
@@ -122,36 +124,100 @@ class PagedModelStore:
         """Copy one expert record into device memory ``dst`` (uint8 [expert_bytes]) on
         ``stream`` without blocking the host on the copy: pinned images go straight to the
         device; other sources pass through a ring of pinned staging buffers, each reused only
-        after its previous copy has completed. In an ANS-coded container the compressed record
-        is copied into a device staging buffer of this stream and one decode launch expands it
-        into ``dst`` (decode errors raise the status word read by check_decode_status)."""
+        after its previous copy has completed.
+
+        ANS-coded containers: the compressed record lands in one of a ring of device staging
+        buffers owned by ``stream``, and a decode stream paired with it expands the record into
+        ``dst`` (one launch), so the copy of the next miss overlaps this decode. Consumers wait
+        on ``load_streams(stream)``; decode errors raise the status word read by
+        check_decode_status."""
         src = self._host_record(layer_idx, expert_id)
         stream = stream or torch.cuda.current_stream(dst.device)
         _, nb = self.layout.record(layer_idx, expert_id)
-        land = self._device_stage(dst.device, stream)[:nb] if self.ans_coded else dst
+        if self.ans_coded:
+            ring = self._ans_ring(dst.device, stream)
+            land, ready, free = ring["bufs"][ring["next"]]
+            ring["next"] = (ring["next"] + 1) % len(ring["bufs"])
+            stream.wait_event(free)  # the decode that last read this staging buffer is done
+            land = land[:nb]
+        else:
+            land = dst
         if isinstance(src, torch.Tensor) and src.is_pinned():
             with torch.cuda.stream(stream):
                 land.copy_(src, non_blocking=True)
         else:
-            ring = self._staging_ring()
-            buf, ev = ring[self._staging_next]
-            self._staging_next = (self._staging_next + 1) % len(ring)
+            hring = self._staging_ring()
+            buf, ev = hring[self._staging_next]
+            self._staging_next = (self._staging_next + 1) % len(hring)
             ev.synchronize()  # the previous copy out of this buffer is done
             self.read_record(layer_idx, expert_id, out=buf)
             with torch.cuda.stream(stream):
                 land.copy_(buf[:nb], non_blocking=True)
                 ev.record(stream)
         if self.ans_coded:
-            # same stream as the copy in and the next copy into this staging buffer: ordered
+            dec = ring["decode_stream"]
+            ready.record(stream)
+            dec.wait_event(ready)
             ans.decode_segments(land, self.layout.segments(layer_idx, expert_id), dst,
-                                self.decode_status(dst.device), stream)
+                                self.decode_status(dst.device), dec)
+            free.record(dec)
         self.bytes_paged += nb
 
-    def _device_stage(self, device, stream):
+    ANS_STAGES = 4
+
+    def _ans_ring(self, device, stream):
         key = (str(device), stream.cuda_stream)
+        ring = self._dev_stage.get(key)
+        if ring is None:
+            ring = {"decode_stream": torch.cuda.Stream(device), "next": 0,
+                    "bufs": [(torch.empty(self.max_record_bytes, dtype=torch.uint8, device=device),
+                              torch.cuda.Event(), torch.cuda.Event()) for _ in range(self.ANS_STAGES)]}
+            self._dev_stage[key] = ring
+        return ring
+
+    def load_streams(self, stream):
+        """Streams whose work a consumer of records loaded on ``stream`` must wait for."""
+        ring = self._dev_stage.get((str(stream.device), stream.cuda_stream))
+        return [stream] if ring is None else [stream, ring["decode_stream"]]
+
+    # ---- native paged step support ------------------------------------------------------------
+    def pinned_image(self):
+        """True when records are read from a pinned host image (the native step's source)."""
+        return isinstance(self.image, torch.Tensor) and self.image.is_pinned()
+
+    def miss_arrays(self, layer_idx, misses):
+        """Host arrays describing the records of ``misses`` [(expert, slot)] for
+        vq2_paged_moe_step: (src pointers uint64, bytes int64, slots int32, segment plans
+        int64 [n, 20] or None, total bytes)."""
+        n = len(misses)
+        src = np.empty(n, dtype=np.uint64)
+        nbytes = np.empty(n, dtype=np.int64)
+        slots = np.empty(n, dtype=np.int32)
+        segs = np.empty((n, 20), dtype=np.int64) if self.ans_coded else None
+        base = self.image.data_ptr()
+        cache = self._rec_cache
+        for i, (e, slot) in enumerate(misses):
+            key = (layer_idx, e)
+            ent = cache.get(key)
+            if ent is None:
+                off, nb = self.layout.record(layer_idx, e)
+                plan = np.asarray(self.layout.segments(layer_idx, e), dtype=np.int64).reshape(-1) \
+                    if self.ans_coded else None
+                ent = cache[key] = (off, nb, plan)
+            src[i] = base + ent[0]
+            nbytes[i] = ent[1]
+            slots[i] = slot
+            if segs is not None:
+                segs[i] = ent[2]
+        return src, nbytes, slots, segs, int(nbytes.sum())
+
+    def pager_stage(self, device, copy_stream):
+        """Device staging buffer for the coded records of one native step group (8 records),
+        one per copy stream (its copies and decodes are ordered on that stream)."""
+        key = ("pager", str(device), copy_stream.cuda_stream)
         buf = self._dev_stage.get(key)
         if buf is None:
-            buf = torch.empty(self.max_record_bytes, dtype=torch.uint8, device=device)
+            buf = torch.empty(8 * ((self.max_record_bytes + 255) // 256 * 256), dtype=torch.uint8, device=device)
             self._dev_stage[key] = buf
         return buf
 
@@ -166,7 +232,8 @@ class PagedModelStore:
 
     def check_decode_status(self):
         """Synchronize and raise ans.ANSDecodeError if any decode met a malformed stream."""
-        for st in self._ans_status.values():
+        for key, st in self._ans_status.items():
+            torch.cuda.synchronize(torch.device(key))
             ans.check_status(st)
 
     def read_expert_record(self, layer_idx, expert_id):
@@ -179,7 +246,7 @@ class PagedModelStore:
         dev = torch.device("cuda", torch.cuda.current_device())
         out = torch.empty(self.expert_bytes, dtype=torch.uint8, device=dev)
         self.load_record_async(layer_idx, expert_id, out, torch.cuda.current_stream(dev))
-        self.check_decode_status()
+        self.check_decode_status()  # synchronizes the device, decode streams included
         return out.cpu().numpy()
 
     # ---- reference-compatible accessors -----------------------------------------------------
@@ -325,6 +392,17 @@ class PagedMoEExpert(nn.Module):
             self.copy_stream = copy_stream or torch.cuda.Stream(self.device)
             self._compute_done = torch.cuda.Event()
             self._compute_done.record(torch.cuda.current_stream(self.device))
+            # Native step (vq2_paged_moe_step) when records come from a pinned host image: the
+            # copies, decode, id upload and expert FFN of a step are one C-ABI call.
+            self.native = store.pinned_image()
+            if self.native:
+                self._copy_done, self._ids_done = torch.cuda.Event(), torch.cuda.Event()
+                cur = torch.cuda.current_stream(self.device)
+                self._copy_done.record(cur)
+                self._ids_done.record(cur)
+                self._ids_cap = 0
+                self._ws = torch.empty(0, dtype=torch.uint8, device=self.device)
+                self._layer = None
         self._pending_loads = []
 
     # ---- host LRU (reference semantics) -----------------------------------------------------
@@ -362,6 +440,78 @@ class PagedMoEExpert(nn.Module):
         self.copy_stream.wait_event(self._compute_done)
         self.store.load_record_async(self.layer_idx, e_id, self.pool.raw[slot], self.copy_stream)
 
+    # ---- native step ------------------------------------------------------------------------
+    def _native_layer(self, P):
+        """The vq2_paged_layer of this module, with id buffers for at least P problems."""
+        if self._layer is not None and P <= self._ids_cap:
+            return self._layer
+        if self._layer is not None:
+            self._ids_done.synchronize()  # the old pinned buffer is no longer being copied from
+        cap = max(P, 64)
+        self._ids_host = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+        self._ids_dev = torch.empty(cap, dtype=torch.int32, device=self.device)
+        self._ids_cap = cap
+        st = self.store
+        coded = st.ans_coded
+        stage = st.pager_stage(self.device, self.copy_stream) if coded else None
+        status = st.decode_status(self.device) if coded else None
+        r_in, r_mid = self.rot_2048, self.rot_512
+        self._layer = _lib.PagedLayer(
+            pool=self.pool.raw.data_ptr(), capacity=self.capacity, gu_rows=st.gu_rows, gu_cols=st.gu_cols,
+            dn_rows=st.dn_rows, dn_cols=st.dn_cols, cb0=self.cb16.data_ptr(), val_dtype=_lib.dtype_code(self.cb16),
+            index_coding=1 if coded else 0, perm_in=r_in.perm.data_ptr(), sign_in=r_in.sign.data_ptr(),
+            hb_in=r_in.hb, perm_mid=r_mid.perm.data_ptr(), sign_mid=r_mid.sign.data_ptr(), hb_mid=r_mid.hb,
+            scale_in=float(r_in.scale), scale_mid=float(r_mid.scale),
+            stage=stage.data_ptr() if coded else None, stage_bytes=stage.numel() if coded else 0,
+            status=status.data_ptr() if coded else None, ids_host=self._ids_host.data_ptr(),
+            ids_dev=self._ids_dev.data_ptr(), ids_cap=cap, copy_stream=self.copy_stream.cuda_stream,
+            copy_done=self._copy_done.cuda_event, compute_done=self._compute_done.cuda_event,
+            ids_done=self._ids_done.cuda_event)
+        return self._layer
+
+    def _step(self, h, slot_rows, w, out, misses, stream):
+        """Load ``misses`` and run the experts of tokens h on ``slot_rows`` in one native call."""
+        T, K = len(slot_rows), len(slot_rows[0])
+        layer = self._native_layer(T * K)
+        need = _lib.load().vq2_moe_expert_ffn_workspace(T, K, self.store.gu_rows, self.store.dn_rows)
+        if self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        slots = np.asarray(slot_rows, dtype=np.int32).reshape(-1)
+        n = len(misses)
+        if n:
+            src, nbytes, mslots, segs, total = self.store.miss_arrays(self.layer_idx, misses)
+            args = (n, src.ctypes.data, nbytes.ctypes.data, mslots.ctypes.data,
+                    segs.ctypes.data if segs is not None else None)
+            self.store.bytes_paged += total
+        else:
+            args = (0, None, None, None, None)
+        _lib.call("vq2_paged_moe_step", ctypes.byref(layer), h.data_ptr(), _lib.dtype_code(h), T, K,
+                  slots.ctypes.data, w.data_ptr(), *args, self._ws.data_ptr(), self._ws.numel(), out.data_ptr(),
+                  _lib.dtype_code(out), stream.cuda_stream)
+
+    def _forward_native(self, h, ids_list, w, out, stream):
+        T = h.shape[0]
+        seg_start, seg_slots, slot_rows, misses = 0, set(), [], []
+        for t in range(T):
+            row = []
+            for e in ids_list[t]:
+                slot, hit = self._assign_slot(int(e))
+                if not hit and slot in seg_slots:
+                    # the slot is still to be read by earlier tokens of this batch: run them first
+                    self._step(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t], misses, stream)
+                    seg_start, seg_slots, slot_rows, misses = t, set(), [], []
+                if not hit:
+                    misses.append((int(e), slot))
+                row.append(slot)
+            slot_rows.append(row)
+            seg_slots.update(row)
+        self._step(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T], misses, stream)
+        return out
+
+    def _join_loads(self, stream):
+        for s in self.store.load_streams(self.copy_stream):
+            stream.wait_stream(s)
+
     # ---- compute ----------------------------------------------------------------------------
     def _run(self, h, slots, w, out):
         """Expert FFN of tokens h [t, H] on pool slots [t, k] with weights [t, k] into out."""
@@ -377,10 +527,16 @@ class PagedMoEExpert(nn.Module):
         K = topk_idx.shape[-1]
         ids = topk_idx.reshape(T, K)
         ids_list = ids.tolist() if not ids.is_cuda else ids.cpu().tolist()  # reference: .tolist() sync
-        w = topk_weights.reshape(T, K).to(self.device, torch.float32)
-        h = hidden_states.reshape(T, -1)
+        w = topk_weights.reshape(T, K)
+        if w.is_cuda:
+            w = w.to(self.device, torch.float32).contiguous()
+        else:  # a pinned bounce keeps the upload asynchronous
+            w = w.to(torch.float32).contiguous().pin_memory().to(self.device, non_blocking=True)
+        h = hidden_states.reshape(T, -1).contiguous()
         out = torch.empty(T, self.hidden_dim, dtype=hidden_states.dtype, device=self.device)
         stream = torch.cuda.current_stream(self.device)
+        if self.native:
+            return self._forward_native(h, ids_list, w, out, stream)
 
         seg_start, seg_slots, slot_rows = 0, set(), []
         loads_in_seg = False
@@ -391,7 +547,7 @@ class PagedMoEExpert(nn.Module):
                 if not hit and slot in seg_slots:
                     # the slot is still to be read by earlier tokens of this batch: run them first
                     if loads_in_seg:
-                        stream.wait_stream(self.copy_stream)
+                        self._join_loads(stream)
                     self._run(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t])
                     seg_start, seg_slots, slot_rows, loads_in_seg = t, set(), [], False
                 if not hit:
@@ -401,6 +557,6 @@ class PagedMoEExpert(nn.Module):
             slot_rows.append(row)
             seg_slots.update(row)
         if loads_in_seg:
-            stream.wait_stream(self.copy_stream)
+            self._join_loads(stream)
         self._run(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T])
         return out

@@ -281,7 +281,7 @@ VQ2_API int vq2_rans_encode(const uint8_t* symbols, int64_t n_symbols, uint8_t* 
 VQ2_API int vq2_rans_decode(const void* stream, int64_t stream_bytes, int64_t n_symbols,
                             void* out, int64_t out_capacity, int32_t* status, void* cuda_stream);
 /*
- * One launch over 1..8 segments of src (device, src_bytes) into dst (device, dst_bytes):
+ * One launch over 1..32 segments of src (device, src_bytes) into dst (device, dst_bytes):
  * segment i reads src[seg_src_off[i], + seg_src_bytes[i]) and writes dst[seg_dst_off[i],
  * + seg_n[i]); seg_kind 0 = a VQ2A stream of seg_n symbols, 1 = stored bytes (seg_src_bytes ==
  * seg_n, copied). The offset arrays are host memory. Status as for vq2_rans_decode. Used to
@@ -292,6 +292,54 @@ VQ2_API int vq2_rans_decode_segments(const void* src, int64_t src_bytes,
                                      const int64_t* seg_dst_off, const int64_t* seg_n,
                                      const int32_t* seg_kind, int64_t nseg, void* dst,
                                      int64_t dst_bytes, int32_t* status, void* cuda_stream);
+
+/*
+ * ---- Paged MoE step (native executor) ----
+ * One step of a paged MoE layer after the caller's LRU bookkeeping has chosen the slots
+ * (reference PagedMoEExpert.forward, vq2/paged_runtime.py:439-568, with _get_slot :415-437 kept
+ * on the host so hit/miss/slot sequences stay bit-exact):
+ *   1. if n_miss > 0: copy_stream waits compute_done (earlier steps may still read the slots);
+ *      record i (miss_bytes[i] bytes at host address miss_src[i], pinned for asynchrony) is
+ *      copied to slot miss_slot[i] of the pool, or, with index_coding 1 (VQ2A-coded records), to
+ *      the staging buffer, from which one decode launch per 8 records expands them into their
+ *      slots following miss_seg (per record 4 segments of 5 int64: src_off, src_bytes, dst_off,
+ *      n, kind, as vq2_rans_decode_segments); copy_done is recorded and `stream` waits for it;
+ *   2. slots (host int32 [T * top_k]) go through ids_host (pinned; the call first waits on the
+ *      host for ids_done, the previous upload) to ids_dev on `stream`;
+ *   3. the routed-expert FFN (as vq2_moe_expert_ffn, on the pool with capacity rows) runs on
+ *      `stream`, then compute_done is recorded.
+ * All events must have been recorded once before the first call. Steps of one layer use one
+ * `stream`. Decode errors raise *status (see vq2_rans_decode).
+ */
+typedef struct vq2_paged_layer {
+  void* pool;                      /* device [capacity, record bytes] expert records */
+  int64_t capacity, gu_rows, gu_cols, dn_rows, dn_cols;
+  const void* cb0;                 /* [65536, 8] in val_dtype */
+  int32_t val_dtype, index_coding; /* index_coding: 0 raw records, 1 VQ2A-coded indices */
+  const int32_t* perm_in;
+  const int8_t* sign_in;
+  int64_t hb_in;
+  const int32_t* perm_mid;
+  const int8_t* sign_mid;
+  int64_t hb_mid;
+  float scale_in, scale_mid;
+  void* stage;                     /* device staging for coded records (index_coding 1) */
+  int64_t stage_bytes;
+  int32_t* status;                 /* device decode status word (index_coding 1) */
+  int32_t* ids_host;               /* pinned host int32 [ids_cap] */
+  int32_t* ids_dev;                /* device int32 [ids_cap] */
+  int64_t ids_cap;
+  void* copy_stream;               /* cudaStream_t */
+  void* copy_done;                 /* cudaEvent_t */
+  void* compute_done;              /* cudaEvent_t */
+  void* ids_done;                  /* cudaEvent_t */
+} vq2_paged_layer;
+
+VQ2_API int vq2_paged_moe_step(const vq2_paged_layer* layer, const void* h, int h_dtype, int64_t T,
+                               int64_t top_k, const int32_t* slots, const float* w, int64_t n_miss,
+                               const void* const* miss_src, const int64_t* miss_bytes,
+                               const int32_t* miss_slot, const int64_t* miss_seg, void* workspace,
+                               int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

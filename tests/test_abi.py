@@ -26,6 +26,39 @@ def test_library_exports_every_declared_symbol():
     assert lib.vq2_abi_version() == _lib.ABI_VERSION
 
 
+def test_paged_layer_struct_matches_header():
+    """The ctypes mirror of vq2_paged_layer declares the header's fields in order with the
+    natural C layout (pointers and int64 at 8-byte boundaries)."""
+    txt = open(_lib.HEADER_PATH).read()
+    body = txt[txt.index("typedef struct vq2_paged_layer {"):txt.index("} vq2_paged_layer;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S).split("{", 1)[1]
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if decl:
+            names += [n.strip().lstrip("*") for n in re.sub(r"^(const\s+)?\w+\*?\s+", "", decl).split(",")]
+    assert names == [f for f, _ in _lib.PagedLayer._fields_]
+    # sizes and offsets as the C compiler lays the struct out
+    import os
+    import shutil
+    import subprocess
+    import tempfile
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    d = tempfile.mkdtemp()
+    src = os.path.join(d, "layout.c")
+    with open(src, "w") as f:
+        f.write("#include <stdio.h>\n#include <stddef.h>\n#include \"vq2_b200.h\"\nint main(void){"
+                f"printf(\"%zu\", sizeof(vq2_paged_layer));"
+                + "".join(f"printf(\" %zu\", offsetof(vq2_paged_layer, {n}));" for n in names) + "return 0;}")
+    exe = os.path.join(d, "layout")
+    subprocess.run([cc, "-I", os.path.dirname(_lib.HEADER_PATH), src, "-o", exe], check=True)
+    got = [int(v) for v in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(_lib.PagedLayer)
+    assert got[1:] == [getattr(_lib.PagedLayer, n).offset for n in names]
+
+
 def test_status_strings():
     lib = _lib.load()
     assert lib.vq2_status_string(0) == b"ok"
@@ -65,6 +98,35 @@ def test_argument_validation_without_device():
                               64, 2048, 1.0, None, 0, None) == _lib.VQ2_ERR_SHAPE
     assert lib.vq2_gemv_workspace(1, 2048) == 0 and lib.vq2_gemv_workspace(4, 2048) == 2 * 4 * 2048 * 2 and lib.vq2_gemv_workspace(16, 2048) == 2 * 16 * 2048 * 2
     assert lib.vq2_moe_combine(p, p, 1, 0, 2048, None, p, 0, None) == _lib.VQ2_ERR_SHAPE
+
+
+def test_paged_step_validation_without_device():
+    lib = _lib.load()
+    slots = (ctypes.c_int32 * 8)()
+    layer = _lib.PagedLayer()  # null pool, events, ...
+    assert lib.vq2_paged_moe_step(None, None, 0, 1, 8, slots, None, 0, None, None, None, None, None, 0, None, 0,
+                                  None) == _lib.VQ2_ERR_ARG
+    assert lib.vq2_paged_moe_step(ctypes.byref(layer), None, 0, 1, 8, slots, None, 0, None, None, None, None, None,
+                                  0, None, 0, None) == _lib.VQ2_ERR_ARG
+    p = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+    layer = _lib.PagedLayer(pool=256, capacity=4, gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64, ids_host=256,
+                            ids_dev=256, ids_cap=8, copy_stream=256, copy_done=256, compute_done=256, ids_done=256)
+    big = lib.vq2_moe_expert_ffn_workspace(2, 8, 1024, 2048)
+    # more problems than the id buffers hold
+    assert lib.vq2_paged_moe_step(ctypes.byref(layer), p, 0, 2, 8, slots, p, 0, None, None, None, None, p, big, p, 0,
+                                  None) == _lib.VQ2_ERR_SHAPE
+    # a miss aimed outside the pool, and one of the wrong size
+    src = (ctypes.c_void_p * 1)(256)
+    ws = lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048)
+    for slot, nb in ((4, 792576), (0, 1000)):
+        bad_slot = (ctypes.c_int32 * 1)(slot)
+        nbytes = (ctypes.c_int64 * 1)(nb)
+        assert lib.vq2_paged_moe_step(ctypes.byref(layer), p, 0, 1, 8, slots, p, 1, src, nbytes, bad_slot, None, p,
+                                      ws, p, 0, None) == _lib.VQ2_ERR_SHAPE
+    # coded records without a staging buffer
+    layer.index_coding = 1
+    assert lib.vq2_paged_moe_step(ctypes.byref(layer), p, 0, 1, 8, slots, p, 0, None, None, None, None, p, ws, p, 0,
+                                  None) == _lib.VQ2_ERR_ARG
 
 
 def test_status_mapping_to_exceptions():

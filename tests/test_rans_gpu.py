@@ -128,7 +128,7 @@ def test_decode_segments_refuses_out_of_range_plans():
         with pytest.raises(ValueError):
             ans.decode_segments(src, segs, dst, status)
     with pytest.raises(ValueError):
-        ans.decode_segments(src, [(0, 16, 0, 16, 1)] * 9, dst, status)
+        ans.decode_segments(src, [(0, 16, 0, 16, 1)] * 33, dst, status)   # at most 32 segments
 
 
 @pytest.mark.parametrize("mode", ["image_pinned", "offset"])
