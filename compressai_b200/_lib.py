@@ -60,7 +60,8 @@ class PagedLayer(ctypes.Structure):
                 ("dn_cols", _i64), ("cb0", _p), ("val_dtype", ctypes.c_int32), ("index_coding", ctypes.c_int32),
                 ("perm_in", _p), ("sign_in", _p), ("hb_in", _i64), ("perm_mid", _p), ("sign_mid", _p),
                 ("hb_mid", _i64), ("scale_in", _f32), ("scale_mid", _f32), ("stage", _p), ("stage_bytes", _i64),
-                ("status", _p), ("ids_host", _p), ("ids_dev", _p), ("ids_cap", _i64), ("copy_stream", _p),
+                ("status", _p), ("stage_turn", _p), ("decode_stream", _p), ("stage_ready", _p), ("stage_free0", _p),
+                ("stage_free1", _p), ("ids_host", _p), ("ids_dev", _p), ("ids_cap", _i64), ("copy_stream", _p),
                 ("copy_done", _p), ("compute_done", _p), ("ids_done", _p)]
 ABI_VERSION = 1
 

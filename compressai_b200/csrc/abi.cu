@@ -18,6 +18,14 @@ bool pdl_enabled() {
   return on;
 }
 
+bool moe_fused_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VQ2_MOE_FUSED");  // A/B switch for the native paged step
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
 int sm_count() {
   static std::atomic<int> cache[64];
   int dev = 0;

@@ -112,6 +112,10 @@ int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   return launch_status();
 }
 
+// Whether decode-sized MoE FFNs use the fused single-launch kernel (environment VQ2_MOE_FUSED=0
+// selects the four-kernel path; both compute the same values).
+bool moe_fused_enabled();
+
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 

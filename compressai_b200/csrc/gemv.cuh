@@ -68,10 +68,18 @@ int64_t gemm_tc_workspace(int64_t M, int64_t n);
 int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H, const float* add, void* out,
                 int out_dtype, cudaStream_t st, const int32_t* ids = nullptr, int64_t num_experts = 0);
 
+// Up to 64 problem ids passed by value in launch parameters (no upload copy needed).
+constexpr int kIdsByValue = 64;
+struct IdsByValue {
+  int32_t v[kIdsByValue];
+};
+
 // Stable compaction of the problems whose id is in [0, num_experts): out_ids[c] = ids[p],
-// out_map[c] = p, *out_count = number kept (moe.cu). One CTA; P <= 65536.
+// out_map[c] = p, *out_count = number kept (moe.cu). One CTA; P <= 65536. With host_ids
+// (a HOST array, P <= 64) the ids travel in the launch parameters and are written to
+// ids_copy (device, P) for later kernels; ids is then ignored.
 int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
-                int32_t* out_count, cudaStream_t st);
+                int32_t* out_count, cudaStream_t st, const int32_t* host_ids = nullptr, int32_t* ids_copy = nullptr);
 
 // Routed-expert FFN of one MoE layer (moe_ffn.cu): compaction, gate_up GEMV (input RHT),
 // down GEMV (SwiGLU + RHT), combine; `ws` holds moe_ffn_workspace(T * top_k, ...) bytes.
@@ -80,7 +88,38 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    const void* pool, int64_t num_experts, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
                    int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
-                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st);
+                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host = false,
+                   bool counters_zeroed = false, int32_t* err = nullptr, bool prefer_fused = false);
+
+// Fused single-launch expert FFN for T * top_k <= 64 (moe_fused.cu).
+struct MoeFusedArgs {
+  const void* h;
+  int h_dtype, T, K, P;
+  const int32_t* ids;  // device ids [P], or null: ids by value in iv
+  IdsByValue iv;
+  const float* w;      // [T, K]
+  const uint8_t* pool; // [num_experts, rec] expert records
+  int64_t num_experts, rec, off_gs, off_di, off_ds;
+  int gu_rows, ng_gu, dn_rows, ng_dn;
+  const void* cb0;
+  const int32_t* perm_in;
+  const int8_t* sign_in;
+  int hb_in;
+  float scale_in;
+  const int32_t* perm_mid;
+  const int8_t* sign_mid;
+  int hb_mid;
+  float scale_mid;
+  int32_t* ctr;        // counters (zero between launches)
+  float* y_gu;         // [P, gu_rows]
+  float* y_dn;         // [P, dn_rows]
+  void* out;           // [T, dn_rows]
+  int out_dtype;
+  int32_t* err;        // optional status word
+};
+
+bool moe_fused_eligible(const MoeFusedArgs& a, int val_dtype);
+int moe_fused_ffn(const MoeFusedArgs& a, int val_dtype, cudaStream_t st);
 
 // VQ2A decode of up to 32 segments of src into dst in one launch (rans.cu); status as
 // vq2_rans_decode_segments.

@@ -108,10 +108,13 @@ int run_combine(const float* y, const float* w, int64_t T, int top_k, int64_t H,
 
 // Stable compaction with one CTA of 1024 threads: per 1024-problem chunk, a ballot gives each
 // warp's count, a scan over the 32 warp counts gives offsets, and kept problems are written
-// in their original order.
-__global__ void __launch_bounds__(1024) moe_compact_kernel(const int32_t* __restrict__ ids, int64_t P,
+// in their original order. The ids come from device memory, or (ids == nullptr, P <= 64) by
+// value in the launch parameters, in which case they are also written to ids_copy for the
+// kernels that follow.
+__global__ void __launch_bounds__(1024) moe_compact_kernel(const int32_t* __restrict__ ids, IdsByValue iv, int64_t P,
                                                            int64_t num_experts, int32_t* __restrict__ out_ids,
-                                                           int32_t* __restrict__ out_map, int32_t* __restrict__ count) {
+                                                           int32_t* __restrict__ out_map, int32_t* __restrict__ count,
+                                                           int32_t* __restrict__ ids_copy) {
   __shared__ int warp_tot[32];
   __shared__ int base;
   pdl_wait();
@@ -120,7 +123,8 @@ __global__ void __launch_bounds__(1024) moe_compact_kernel(const int32_t* __rest
   __syncthreads();
   for (int64_t c0 = 0; c0 < P; c0 += 1024) {
     const int64_t p = c0 + threadIdx.x;
-    const int32_t id = p < P ? ids[p] : -1;
+    const int32_t id = p < P ? (ids ? ids[p] : iv.v[p < kIdsByValue ? p : 0]) : -1;
+    if (ids_copy && p < P) ids_copy[p] = id;
     const bool keep = p < P && id >= 0 && id < num_experts;
     const unsigned m = __ballot_sync(0xffffffffu, keep);
     if (lane == 0) warp_tot[warp] = __popc(m);
@@ -144,10 +148,16 @@ __global__ void __launch_bounds__(1024) moe_compact_kernel(const int32_t* __rest
 }
 
 int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
-                int32_t* out_count, cudaStream_t st) {
+                int32_t* out_count, cudaStream_t st, const int32_t* host_ids, int32_t* ids_copy) {
   if (P <= 0 || P > 65536) return VQ2_ERR_SHAPE;
-  return launch_kernel(moe_compact_kernel, dim3(1), dim3(1024), 0, st, ids, P, num_experts, out_ids, out_map,
-                       out_count);
+  IdsByValue iv{};
+  if (host_ids) {
+    if (P > kIdsByValue || !ids_copy) return VQ2_ERR_SHAPE;
+    for (int64_t p = 0; p < P; ++p) iv.v[p] = host_ids[p];
+    ids = nullptr;
+  }
+  return launch_kernel(moe_compact_kernel, dim3(1), dim3(1024), 0, st, ids, iv, P, num_experts, out_ids, out_map,
+                       out_count, host_ids ? ids_copy : nullptr);
 }
 
 }  // namespace vq2

@@ -26,16 +26,23 @@ static RecordLayout record_layout(int64_t gr, int64_t gc, int64_t dr, int64_t dc
 
 static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
+// Workspace: [counters of the fused kernel, 1 KB][gate_up out fp32 P x gu_rows][down out fp32
+// P x dn_rows][compaction: ids, map, count, ids copy]. The counters sit at a fixed offset so a
+// workspace reused across calls of different P keeps them.
+constexpr int64_t kCtrBytes = 1024;
+
 int64_t moe_ffn_workspace(int64_t P, int64_t gu_rows, int64_t dn_rows) {
-  return align256(P * gu_rows * 4) + align256(P * dn_rows * 4) + align256(P * 8 + 4);
+  return kCtrBytes + align256(P * gu_rows * 4) + align256(P * dn_rows * 4) + align256(P * 12 + 4);
 }
 
 // Shared body of vq2_moe_expert_ffn and its variants: `ws` must hold moe_ffn_workspace bytes.
+// ids_on_host: `ids` is a HOST array of P <= 64 ids, passed to the GPU in launch parameters.
 int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids, const float* w,
                    const void* pool, int64_t num_experts, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
                    int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
-                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st) {
+                   float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host,
+                   bool counters_zeroed, int32_t* err, bool prefer_fused) {
   if (!h || !ids || !w || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid || !ws || !out)
     return VQ2_ERR_ARG;
   if (T <= 0 || top_k <= 0 || top_k > 64 || num_experts <= 0) return VQ2_ERR_SHAPE;
@@ -50,17 +57,50 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   const int64_t P = T * top_k;
   if (P > 65536) return VQ2_ERR_SHAPE;
   const int64_t H = gu_cols * 8, I = gu_rows / 2;
-  float* gu = static_cast<float*>(ws);
-  float* yd = reinterpret_cast<float*>(static_cast<char*>(ws) + align256(P * gu_rows * 4));
+  int32_t* ctr = static_cast<int32_t*>(ws);
+  float* gu = reinterpret_cast<float*>(static_cast<char*>(ws) + kCtrBytes);
+  float* yd = reinterpret_cast<float*>(reinterpret_cast<char*>(gu) + align256(P * gu_rows * 4));
   int32_t* c_ids = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(yd) + align256(P * dn_rows * 4));
   int32_t* c_map = c_ids + P;
   int32_t* c_cnt = c_map + P;
+  int32_t* c_all = c_cnt + 1;  // the ids themselves when they arrive by value
   const char* base = static_cast<const char*>(pool);
+  if (ids_on_host && P > kIdsByValue) return VQ2_ERR_SHAPE;
+
+  // Decode-sized batches where launch cost dominates (the native paged step, issued eagerly from
+  // the host): one fused launch (moe_fused.cu) instead of four. Inside a CUDA graph the four
+  // kernels are faster on the GPU (40 vs 47 us per 35B layer at T = 1, top-8), so the generic
+  // entry points keep them.
+  if (prefer_fused && P <= kIdsByValue && moe_fused_enabled()) {
+    MoeFusedArgs f{};
+    f.h = h; f.h_dtype = h_dtype; f.T = (int)T; f.K = (int)top_k; f.P = (int)P;
+    f.ids = ids_on_host ? nullptr : ids;
+    if (ids_on_host)
+      for (int64_t p = 0; p < P; ++p) f.iv.v[p] = ids[p];
+    f.w = w; f.pool = static_cast<const uint8_t*>(pool); f.num_experts = num_experts; f.rec = L.bytes;
+    f.off_gs = L.gu_scale; f.off_di = L.dn_idx; f.off_ds = L.dn_scale;
+    f.gu_rows = (int)gu_rows; f.ng_gu = (int)gu_cols; f.dn_rows = (int)dn_rows; f.ng_dn = (int)dn_cols;
+    f.cb0 = cb0; f.perm_in = perm_in; f.sign_in = sign_in; f.hb_in = (int)hb_in; f.scale_in = scale_in;
+    f.perm_mid = perm_mid; f.sign_mid = sign_mid; f.hb_mid = (int)hb_mid; f.scale_mid = scale_mid;
+    f.ctr = ctr; f.y_gu = gu; f.y_dn = yd; f.out = out; f.out_dtype = out_dtype; f.err = err;
+    if (moe_fused_eligible(f, val_dtype)) {
+      if (!counters_zeroed) {
+        const cudaError_t e = cudaMemsetAsync(ctr, 0, kCtrBytes, st);
+        if (e != cudaSuccess) {
+          set_last_cuda_error(e);
+          return VQ2_ERR_LAUNCH;
+        }
+      }
+      return moe_fused_ffn(f, val_dtype, st);
+    }
+  }
 
   // Only problems whose expert is in the pool are computed (remote experts of an expert-parallel
   // rank are -1): compact them so the GEMV grid covers real work only.
-  int s = run_compact(ids, P, num_experts, c_ids, c_map, c_cnt, st);
+  int s = ids_on_host ? run_compact(nullptr, P, num_experts, c_ids, c_map, c_cnt, st, ids, c_all)
+                      : run_compact(ids, P, num_experts, c_ids, c_map, c_cnt, st);
   if (s != VQ2_OK) return s;
+  if (ids_on_host) ids = c_all;
 
   GemvArgs a{};
   a.nprob = 0;
@@ -154,7 +194,8 @@ extern "C" int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T,
   int status = VQ2_OK;
   void* ws = vq2::noalloc_scratch(&status);
   if (ws == nullptr) return status;
+  // the static scratch starts zeroed and the fused kernel leaves its counters at zero
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
-                             scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream));
+                             scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream), false, true);
 }

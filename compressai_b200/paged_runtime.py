@@ -212,14 +212,21 @@ class PagedModelStore:
         return src, nbytes, slots, segs, int(nbytes.sum())
 
     def pager_stage(self, device, copy_stream):
-        """Device staging buffer for the coded records of one native step group (8 records),
-        one per copy stream (its copies and decodes are ordered on that stream)."""
+        """Staging of coded records for the native step, one per copy stream and shared by the
+        layers that page through it: a device buffer of two halves of 8 records, a decode
+        stream, the events ordering them and the host turn counter."""
         key = ("pager", str(device), copy_stream.cuda_stream)
-        buf = self._dev_stage.get(key)
-        if buf is None:
-            buf = torch.empty(8 * ((self.max_record_bytes + 255) // 256 * 256), dtype=torch.uint8, device=device)
-            self._dev_stage[key] = buf
-        return buf
+        st = self._dev_stage.get(key)
+        if st is None:
+            half = 8 * ((self.max_record_bytes + 255) // 256 * 256)
+            evs = [torch.cuda.Event() for _ in range(3)]
+            for ev in evs:  # the C side waits on them before their first record
+                ev.record(copy_stream)
+            st = {"buf": torch.empty(2 * half, dtype=torch.uint8, device=device),
+                  "decode_stream": torch.cuda.Stream(device), "ready": evs[0], "free0": evs[1], "free1": evs[2],
+                  "turn": np.zeros(1, dtype=np.int64)}
+            self._dev_stage[key] = st
+        return st
 
     def decode_status(self, device):
         """The device status word shared by every ANS decode of this store on ``device``."""
@@ -408,13 +415,15 @@ class PagedMoEExpert(nn.Module):
     # ---- host LRU (reference semantics) -----------------------------------------------------
     def _assign_slot(self, e_id):
         """Bookkeeping of _get_slot (vq2/paged_runtime.py:415-437) without the copy:
-        returns (slot, hit)."""
+        returns (slot, hit). The counters are updated through the instance dict: nn.Module's
+        __setattr__ costs microseconds per call on this per-expert path."""
+        d = self.__dict__
         self.activated_experts_set.add(e_id)
         if e_id in self.expert_to_slot:
-            self.hits += 1
+            d["hits"] += 1
             self.access_order.move_to_end(e_id)
             return self.expert_to_slot[e_id], True
-        self.misses += 1
+        d["misses"] += 1
         if self.free_slots:
             slot = self.free_slots.pop()
         else:
@@ -455,6 +464,7 @@ class PagedMoEExpert(nn.Module):
         coded = st.ans_coded
         stage = st.pager_stage(self.device, self.copy_stream) if coded else None
         status = st.decode_status(self.device) if coded else None
+        self._stage = stage  # keeps the shared staging alive with this layer
         r_in, r_mid = self.rot_2048, self.rot_512
         self._layer = _lib.PagedLayer(
             pool=self.pool.raw.data_ptr(), capacity=self.capacity, gu_rows=st.gu_rows, gu_cols=st.gu_cols,
@@ -462,8 +472,13 @@ class PagedMoEExpert(nn.Module):
             index_coding=1 if coded else 0, perm_in=r_in.perm.data_ptr(), sign_in=r_in.sign.data_ptr(),
             hb_in=r_in.hb, perm_mid=r_mid.perm.data_ptr(), sign_mid=r_mid.sign.data_ptr(), hb_mid=r_mid.hb,
             scale_in=float(r_in.scale), scale_mid=float(r_mid.scale),
-            stage=stage.data_ptr() if coded else None, stage_bytes=stage.numel() if coded else 0,
-            status=status.data_ptr() if coded else None, ids_host=self._ids_host.data_ptr(),
+            stage=stage["buf"].data_ptr() if coded else None, stage_bytes=stage["buf"].numel() if coded else 0,
+            status=status.data_ptr() if coded else None,
+            stage_turn=stage["turn"].ctypes.data if coded else None,
+            decode_stream=stage["decode_stream"].cuda_stream if coded else None,
+            stage_ready=stage["ready"].cuda_event if coded else None,
+            stage_free0=stage["free0"].cuda_event if coded else None,
+            stage_free1=stage["free1"].cuda_event if coded else None, ids_host=self._ids_host.data_ptr(),
             ids_dev=self._ids_dev.data_ptr(), ids_cap=cap, copy_stream=self.copy_stream.cuda_stream,
             copy_done=self._copy_done.cuda_event, compute_done=self._compute_done.cuda_event,
             ids_done=self._ids_done.cuda_event)
@@ -474,8 +489,8 @@ class PagedMoEExpert(nn.Module):
         T, K = len(slot_rows), len(slot_rows[0])
         layer = self._native_layer(T * K)
         need = _lib.load().vq2_moe_expert_ffn_workspace(T, K, self.store.gu_rows, self.store.dn_rows)
-        if self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        if self._ws.numel() < need:  # zeroed: the fused FFN keeps its counters in the first 1 KB
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         slots = np.asarray(slot_rows, dtype=np.int32).reshape(-1)
         n = len(misses)
         if n:

@@ -180,7 +180,7 @@ VQ2_API int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t top
 
 /*
  * Routed-expert FFN of one MoE layer for T tokens with top_k experts each (P = T * top_k
- * (token, expert) problems; three kernels on `stream`):
+ * (token, expert) problems; compaction + three kernels on `stream`):
  *   gu[p]  = GateUp_{ids[p]} . RHT_in(h[p / top_k])                  fp32 [P, gu_rows]
  *   yd[p]  = Down_{ids[p]} . RHT_mid(silu(gu[p, :I]) * gu[p, I:])     fp32 [P, dn_rows]
  *   out[t] = sum_j w[t, j] * yd[t * top_k + j]                        [T, H] in out_dtype
@@ -191,7 +191,8 @@ VQ2_API int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t top
  * scales [gu_rows], down indices int16 [dn_rows, dn_cols], down scales [dn_rows] (scales in
  * val_dtype), 16-byte aligned. RHT_in = (perm_in, sign_in, hb_in, scale_in), RHT_mid likewise
  * (as vq2_rht forward). workspace: device memory of >= vq2_moe_expert_ffn_workspace(T, top_k,
- * gu_rows, dn_rows) bytes, 256-byte aligned, holding gu and yd.
+ * gu_rows, dn_rows) bytes, 256-byte aligned, holding gu and yd (after a first 1 KB used by
+ * vq2_paged_moe_step's fused kernel).
  * Replaces: the compute of PagedMoEExpert.forward (vq2/paged_runtime.py:495-511, T > 1
  * :553-566) and PackedMoEExpertUniversal.forward (vq2/load_and_test_full_35b.py:53-95):
  * rot_2048.fwd, vq_moe_parallel_gate_up, SiLU*up, rot_512.fwd, vq_moe_parallel_down and the
@@ -300,16 +301,25 @@ VQ2_API int vq2_rans_decode_segments(const void* src, int64_t src_bytes,
  * on the host so hit/miss/slot sequences stay bit-exact):
  *   1. if n_miss > 0: copy_stream waits compute_done (earlier steps may still read the slots);
  *      record i (miss_bytes[i] bytes at host address miss_src[i], pinned for asynchrony) is
- *      copied to slot miss_slot[i] of the pool, or, with index_coding 1 (VQ2A-coded records), to
- *      the staging buffer, from which one decode launch per 8 records expands them into their
- *      slots following miss_seg (per record 4 segments of 5 int64: src_off, src_bytes, dst_off,
- *      n, kind, as vq2_rans_decode_segments); copy_done is recorded and `stream` waits for it;
- *   2. slots (host int32 [T * top_k]) go through ids_host (pinned; the call first waits on the
- *      host for ids_done, the previous upload) to ids_dev on `stream`;
+ *      copied to slot miss_slot[i] of the pool; copy_done is recorded and `stream` waits for it.
+ *      With index_coding 1 (VQ2A-coded records) groups of up to 8 records are copied into one
+ *      half of the staging buffer (halves taken in turn by *stage_turn, shared by the layers of
+ *      one copy stream; a half is reused after stage_free0/1), and decode_stream (after
+ *      stage_ready) expands each group in one launch into the slots following miss_seg (per
+ *      record 4 segments of 5 int64: src_off, src_bytes, dst_off, n, kind, as
+ *      vq2_rans_decode_segments); copy_done is then recorded on decode_stream;
+ *   2. slots (host int32 [T * top_k]): up to 64 travel in the first kernel's launch parameters;
+ *      more go through ids_host (pinned; the call first waits on the host for ids_done, the
+ *      previous upload) to ids_dev on `stream`;
  *   3. the routed-expert FFN (as vq2_moe_expert_ffn, on the pool with capacity rows) runs on
- *      `stream`, then compute_done is recorded.
+ *      `stream` -- for T * top_k <= 64 at the 35B-A3B expert shape as ONE fused persistent
+ *      kernel (gate_up, down and combine; work items handed out in dependency order, bounded
+ *      waits), which costs the host one launch instead of four -- then compute_done is recorded.
  * All events must have been recorded once before the first call. Steps of one layer use one
- * `stream`. Decode errors raise *status (see vq2_rans_decode).
+ * `stream`. The workspace (vq2_moe_expert_ffn_workspace bytes) must be zeroed before the first
+ * step and kept for this layer's steps: its first 1 KB holds counters of the fused FFN kernel,
+ * which leaves them at zero. Decode errors raise *status (see vq2_rans_decode), as does (code
+ * 0x100) a bounded wait of the fused FFN kernel that gave up.
  */
 typedef struct vq2_paged_layer {
   void* pool;                      /* device [capacity, record bytes] expert records */
@@ -324,8 +334,13 @@ typedef struct vq2_paged_layer {
   int64_t hb_mid;
   float scale_in, scale_mid;
   void* stage;                     /* device staging for coded records (index_coding 1) */
-  int64_t stage_bytes;
+  int64_t stage_bytes;             /* two halves of up to 8 records each */
   int32_t* status;                 /* device decode status word (index_coding 1) */
+  int64_t* stage_turn;             /* host counter shared with the other layers of copy_stream */
+  void* decode_stream;             /* cudaStream_t (index_coding 1) */
+  void* stage_ready;               /* cudaEvent_t (index_coding 1) */
+  void* stage_free0;               /* cudaEvent_t (index_coding 1) */
+  void* stage_free1;               /* cudaEvent_t (index_coding 1) */
   int32_t* ids_host;               /* pinned host int32 [ids_cap] */
   int32_t* ids_dev;                /* device int32 [ids_cap] */
   int64_t ids_cap;

@@ -133,12 +133,47 @@ def test_paged_experts_outputs_and_lru(cbs, tmp_path, mode, T, cap):
     store.close()
 
 
+@pytest.mark.parametrize("T", [1, 3, 9])
+def test_native_paged_step_matches_python_path_bitwise(cbs, tmp_path, T):
+    """A pinned-image store runs the native step (vq2_paged_moe_step: one call per step; for
+    T * 8 <= 64 the single-launch fused FFN kernel), an offset store the Python copy path with the
+    four-kernel FFN; per token both do the same arithmetic, so outputs, slot contents and LRU
+    sequences agree bit for bit (T = 9 exercises the native step's id upload path)."""
+    layers, E, cap = 2, 40, 12
+    path = str(tmp_path / "p.vq2m")
+    container.write_synthetic_vq2m(path, layers, E, seed=9)
+    native = paged_runtime.PagedModelStore.from_image(torch.from_numpy(np.fromfile(path, np.uint8)).pin_memory(),
+                                                      device=DEV)
+    python = paged_runtime.PagedModelStore(path, device=DEV)
+    cb = cb16_dev(cbs)
+    mods = {nm: [paged_runtime.PagedMoEExpert(ln, st, cb, capacity=cap, device=DEV) for ln in range(layers)]
+            for nm, st in (("native", native), ("python", python))}
+    assert all(m.native for m in mods["native"]) and not any(m.native for m in mods["python"])
+    rng = np.random.default_rng(T)
+    for step in range(4):
+        h = torch.from_numpy(rng.standard_normal((T, 2048)).astype(np.float16)).to(DEV)
+        for ln in range(layers):
+            ids = torch.from_numpy(np.stack([rng.choice(E, 8, replace=False) for _ in range(T)]))
+            w = torch.from_numpy(rng.random((T, 8)).astype(np.float32)).to(DEV)
+            y = {nm: ms[ln](h, ids, w) for nm, ms in mods.items()}
+            assert torch.equal(y["native"], y["python"]), (T, step, ln)
+            a, b = mods["native"][ln], mods["python"][ln]
+            assert (a.hits, a.misses, a.expert_to_slot) == (b.hits, b.misses, b.expert_to_slot)
+            for slot in a.expert_to_slot.values():
+                assert torch.equal(a.pool.raw[slot], b.pool.raw[slot])
+            h = y["native"]
+    assert native.bytes_paged == python.bytes_paged
+    native.close()
+    python.close()
+
+
 def test_expert_ffn_abi_workspace_and_errors(cbs):
     """vq2_moe_expert_ffn through the C-ABI: workspace sizing, too-small workspace refused,
     out-of-range ids contribute zero."""
     from compressai_b200 import _lib, vq
     lib = _lib.load()
-    assert lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048) == 8 * 1024 * 4 + 8 * 2048 * 4 + 256
+    # 1 KB of fused-kernel counters + fp32 gate_up and down outputs + the compaction lists
+    assert lib.vq2_moe_expert_ffn_workspace(1, 8, 1024, 2048) == 1024 + 8 * 1024 * 4 + 8 * 2048 * 4 + 256
     assert lib.vq2_moe_expert_ffn_workspace(0, 8, 1024, 2048) == -1
     seed, E = 21, 6
     pool = resident_pool(seed, E)
