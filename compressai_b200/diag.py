@@ -6,6 +6,11 @@
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix
   python -m compressai_b200.diag moe --T 1 --reps 3
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts
+  python -m compressai_b200.diag rans --n 16777216 --reps 2
+      `reps` GPU decodes of one VQ2A stream of n skewed index bytes, then `reps` decodes of one
+      ANS-coded expert record (vq2_rans_decode_segments)
+  python -m compressai_b200.diag paged --layers 2 --experts 64 --steps 8 --T 1 [--coding vq2a]
+      native paged MoE steps (vq2_paged_moe_step) over a pinned synthetic .vq2m image
 
 Each prints one JSON line with the measured device time per launch/layer.
 """
@@ -81,6 +86,66 @@ def cmd_moe(a):
                       "expert_GBs": round(nbytes / t / 1e9, 1), "tok_s": round(a.T / t, 1)}))
 
 
+def cmd_rans(a):
+    import numpy as np
+
+    from . import ans, container
+    dev = torch.device("cuda", 0)
+    x = np.minimum(np.abs(np.random.default_rng(a.seed).normal(0, 3000, a.n // 2)), 65535).astype(np.uint16)
+    enc = torch.from_numpy(ans.encode(x)).to(dev)
+    out = torch.empty(a.n, dtype=torch.uint8, device=dev)
+    status = ans.new_status(dev)
+    t = _time(lambda: ans.decode(enc, a.n, out, status), a.reps)
+    ans.check_status(status)
+    ok = bool(torch.equal(out.cpu(), torch.from_numpy(x.view(np.uint8))))
+    img, _ = container.synthetic_ans_vq2m_image(1, 2, seed=a.seed, distinct=2)
+    lay = container.parse_header(memoryview(img[:container.RESERVED_HEADER_BYTES]))
+    off, nb = lay.record(0, 1)
+    src = torch.from_numpy(img[off:off + nb].copy()).to(dev)
+    dst = torch.empty(lay.expert_bytes, dtype=torch.uint8, device=dev)
+    segs = lay.segments(0, 1)
+    tr = _time(lambda: ans.decode_segments(src, segs, dst, status), a.reps)
+    ans.check_status(status)
+    print(json.dumps({"rans_bytes": a.n, "encoded": enc.numel(), "us": round(t * 1e6, 2),
+                      "decoded_GBs": round(a.n / t / 1e9, 1), "bit_exact": ok, "record_bytes": nb,
+                      "record_us_eager": round(tr * 1e6, 2)}))
+
+
+def cmd_paged(a):
+    import time
+
+    import numpy as np
+
+    from . import container, paged_runtime
+    dev = torch.device("cuda", 0)
+    if a.coding == "raw":
+        img, _ = container.synthetic_vq2m_image(a.layers, a.experts, seed=a.seed)
+    else:
+        img, _ = container.synthetic_ans_vq2m_image(a.layers, a.experts, seed=a.seed, distinct=min(a.experts, 16))
+    store = paged_runtime.PagedModelStore.from_image(torch.from_numpy(img).pin_memory(), device=dev)
+    cb = _cbs(dev)["16"]
+    cs = torch.cuda.Stream(dev)
+    mods = [paged_runtime.PagedMoEExpert(ln, store, cb, capacity=a.capacity, device=dev, copy_stream=cs)
+            for ln in range(a.layers)]
+    rng = np.random.default_rng(a.seed)
+    trace = [[torch.from_numpy(np.stack([rng.choice(a.experts, 8, replace=False) for _ in range(a.T)]))
+              for _ in range(a.layers)] for _ in range(a.steps)]
+    w = torch.full((a.T, 8), 1.0 / 8, device=dev)
+    h = torch.randn(a.T, 2048, device=dev).half()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(a.steps):
+        for ln in range(a.layers):
+            h = mods[ln](h, trace[s][ln], w)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if store.ans_coded:
+        store.check_decode_status()
+    print(json.dumps({"paged_steps": a.steps, "layers": a.layers, "T": a.T, "coding": a.coding,
+                      "native": all(m.native for m in mods), "misses": sum(m.misses for m in mods),
+                      "ms_per_step": round(wall / a.steps * 1e3, 3), "finite": bool(torch.isfinite(h).all())}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -97,8 +162,20 @@ def main(argv=None):
     m.add_argument("--E", type=int, default=256)
     m.add_argument("--reps", type=int, default=3)
     m.add_argument("--seed", type=int, default=0)
+    r = sub.add_parser("rans")
+    r.add_argument("--n", type=int, default=1 << 24)
+    r.add_argument("--reps", type=int, default=2)
+    r.add_argument("--seed", type=int, default=0)
+    pg = sub.add_parser("paged")
+    pg.add_argument("--layers", type=int, default=2)
+    pg.add_argument("--experts", type=int, default=64)
+    pg.add_argument("--capacity", type=int, default=16)
+    pg.add_argument("--steps", type=int, default=8)
+    pg.add_argument("--T", type=int, default=1)
+    pg.add_argument("--coding", choices=("raw", "vq2a"), default="raw")
+    pg.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
-    {"gather": cmd_gather, "gemv": cmd_gemv, "moe": cmd_moe}[a.cmd](a)
+    {"gather": cmd_gather, "gemv": cmd_gemv, "moe": cmd_moe, "rans": cmd_rans, "paged": cmd_paged}[a.cmd](a)
 
 
 if __name__ == "__main__":
