@@ -91,9 +91,10 @@ __device__ void stage_activations(const ActSrc& a, int64_t xoff, int mcount, flo
         const int j = b * hb + t + T * i;
         const int64_t row = xoff + (int64_t)mi * a.x_row_stride;
         const int p = a.perm[j];
-        if (swiglu) {  // L2 loads: the gate|up rows may come from other CTAs of the same launch
+        if (swiglu) {  // plain loads: L1 lines are reused by the permuted reads of one row; rows
+                       // written by other CTAs of the same launch are read only after an acquire
           const float* g = static_cast<const float*>(a.x) + row;
-          val = silu_f(__ldcg(g + p)) * __ldcg(g + n + p);
+          val = silu_f(g[p]) * g[n + p];
         } else {
           val = load_act(a.x, a.x_dtype, row + p);
         }
