@@ -510,7 +510,7 @@ def run_sweep(dev, Ms=(1, 4, 16, 64), reps=10):
                 alg = gemv_bytes(rows, n, M, bits == 3)
                 out.append({"out": rows, "n": n, "bpw": bits, "M": M, "us": round(t * 1e6, 2),
                             "GBs": round(alg / t / 1e9, 1), "gathers_per_s": round(rows * n / 8 / t, 0),
-                            "path": "tensor cores (mma.sync)" if (M >= 8 or (M >= 2 and rows >= 16384))
+                            "path": "tensor cores (mma.sync)" if (M >= 4 or (M >= 2 and rows >= 16384))
                             else "CUDA cores"})
                 del gr
             del i0s, i1s

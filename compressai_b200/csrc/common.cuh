@@ -116,6 +116,32 @@ int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
 // selects the four-kernel path; both compute the same values).
 bool moe_fused_enabled();
 
+// Launch `kern` as clusters of `cluster_x` CTAs along x (plus the PDL attribute when enabled).
+template <typename... KArgs, typename... Args>
+int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x, cudaStream_t st,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = cluster_x;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return VQ2_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 

@@ -18,12 +18,20 @@
 //     accuracy of the oracle; each chunk (M tile x 128 x {hi, lo}) is streamed into a double
 //     buffer in shared memory with 16-byte cp.async copies while the previous chunk computes;
 //   * 3 bpw adds the residual codebook (shared memory) as a second A operand with its own MMAs,
-//     so the two codebooks are never summed in 16-bit.
+//     so the two codebooks are never summed in 16-bit;
+//   * split-K for matrices with too few 128-row items to fill the GPU: each item is a thread-block
+//     cluster of S CTAs (S <= 8), CTA rank r computing K chunks [r * chunks / S, (r+1) * chunks / S);
+//     the partial accumulators meet in distributed shared memory and rank 0 adds them in rank
+//     order (deterministic) before the epilogue.
 // Semantics: the batched form of reference vq2/kernels.py:32-78 (which serves M = 1 only;
 // vq2/runtime.py:105-110 dequantizes and calls F.linear for M > 1).
+#include <cooperative_groups.h>
+
 #include <atomic>
 
 #include "gemv.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace vq2 {
 
@@ -131,9 +139,20 @@ __global__ void __launch_bounds__(256, 2) vq_gemm_tc_kernel(const GemvArgs a) {
     cp_async_commit();
   };
 
-  const int64_t per = (items + gridDim.x - 1) / gridDim.x;
-  const int64_t i0 = (int64_t)blockIdx.x * per;
-  const int64_t i1 = min(items, i0 + per);
+  // Split-K launches (cluster of S CTAs per item) or persistent contiguous item ranges (S = 1).
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  int64_t i0, i1;
+  if (S > 1) {
+    i0 = (int64_t)blockIdx.x / S;
+    i1 = min(items, i0 + 1);
+  } else {
+    const int64_t per = (items + gridDim.x - 1) / gridDim.x;
+    i0 = (int64_t)blockIdx.x * per;
+    i1 = min(items, i0 + per);
+  }
+  const int c0 = (int)((int64_t)rank * chunks / S), c1 = (int)((int64_t)(rank + 1) * chunks / S);
   for (int64_t it = i0; it < i1; ++it) {
     const int mt = (int)(it / a.row_blocks);
     const int rbg = (int)(it - (int64_t)mt * a.row_blocks);
@@ -158,7 +177,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemm_tc_kernel(const GemvArgs a) {
     auto load_iv = [&](int c, uint4& iv, uint2& jv) {
       iv = make_uint4(0, 0, 0, 0);
       jv = make_uint2(0, 0);
-      if (lrow_ok && c < chunks) {
+      if (lrow_ok && c < c1) {
         const int gbase = c * 16 + 8 * (lane & 1);
         iv = ld_stream_u4(idx0 + (int64_t)lrow * ng + gbase, pol_s);
         if (RES) jv = ld_stream_u2(idx1 + (int64_t)lrow * ng + gbase, pol_s);
@@ -167,15 +186,16 @@ __global__ void __launch_bounds__(256, 2) vq_gemm_tc_kernel(const GemvArgs a) {
     uint4 iv, niv;
     uint2 jv, njv;
     __syncthreads();  // readers of both buffers (previous item) are done
-    stage(0, m0, mcount, 0);
-    load_iv(0, iv, jv);
-    for (int c = 0; c < chunks; ++c) {
-      if (c + 1 < chunks) stage((c + 1) & 1, m0, mcount, c + 1);
+    stage(0, m0, mcount, c0);
+    load_iv(c0, iv, jv);
+    for (int c = c0; c < c1; ++c) {
+      const int buf = (c - c0) & 1;
+      if (c + 1 < c1) stage(buf ^ 1, m0, mcount, c + 1);
       else cp_async_commit();  // keep one group per iteration so wait_group<1> covers chunk c
       load_iv(c + 1, niv, njv);
       cp_async_wait<1>();      // chunk c has landed
       __syncthreads();
-      const TV* xh = xs + (2 * (c & 1)) * XB;
+      const TV* xh = xs + (2 * buf) * XB;
       const TV* xl = xh + XB;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {  // 16 K per step: groups 2s and 2s+1 of the chunk
@@ -214,11 +234,32 @@ __global__ void __launch_bounds__(256, 2) vq_gemm_tc_kernel(const GemvArgs a) {
           }
         }
       }
-      __syncthreads();  // buffer c & 1 is free for chunk c + 2
+      __syncthreads();  // this buffer is free for chunk c + 2
       iv = niv;
       jv = njv;
     }
     cp_async_wait<0>();
+
+    if (S > 1) {  // split-K: partial sums through distributed shared memory, added in rank order
+      float* part = reinterpret_cast<float*>(smem_raw);  // the activation buffers are free now
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) part[(j * 4 + q) * 256 + threadIdx.x] = acc[j][q];
+      cluster.sync();
+      if (rank == 0) {
+        for (int r = 1; r < S; ++r) {
+          const float* rp = cluster.map_shared_rank(part, r);
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[j][q] += rp[(j * 4 + q) * 256 + threadIdx.x];
+        }
+      }
+      cluster.sync();  // the other ranks keep their shared memory until rank 0 has read it
+      if (rank != 0) continue;
+    }
 
     // epilogue: acc[j] = D[rows gid, gid+8][tokens 8j + 2tig, +1]
     const TV* sc = static_cast<const TV*>(a.p_scale[p]);
@@ -272,9 +313,17 @@ static int launch_tc(GemvArgs a, cudaStream_t st) {
     done.fetch_or(bit);
   }
   const int64_t cap = (int64_t)sm_count() * blocks_per_sm.load();
-  const int64_t grid = items < cap ? items : cap;
-  if (grid <= 0) return VQ2_OK;
-  return launch_kernel(kern, dim3((unsigned)grid), dim3(256), smem, st, a);
+  if (items <= 0) return VQ2_OK;
+  // Split-K when the items fill less than half the GPU: the largest power of two S <= 8 with
+  // items * S <= cap and at least two K chunks per CTA.
+  const int chunks = a.n / kTcKC;
+  int S = 1;
+  while (S < 8 && items * (2 * S) <= cap && chunks >= 2 * (2 * S)) S *= 2;
+  if (S == 1) {
+    const int64_t grid = items < cap ? items : cap;
+    return launch_kernel(kern, dim3((unsigned)grid), dim3(256), smem, st, a);
+  }
+  return launch_cluster(kern, dim3((unsigned)(items * S)), dim3(256), smem, S, st, a);
 }
 
 template <bool RES, typename TV>

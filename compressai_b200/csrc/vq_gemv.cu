@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 
 // ---- host dispatch ------------------------------------------------------------------------
 constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the SM's 256 KB stays L1
-constexpr int kTcMinRows = 8;           // activation rows from which the tensor-core path is used
+constexpr int kTcMinRows = 4;           // activation rows from which the tensor-core path is used
 constexpr int64_t kTcTallRows = 16384;  // ...or from 2 rows when the matrices have this many rows
 
 template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>

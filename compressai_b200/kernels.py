@@ -23,7 +23,7 @@ import torch
 from . import _lib
 
 HAVE_TRITON = _lib.available()   # name kept for importers: "fused GPU kernels available"
-TC_MIN_ROWS = 8                  # activation rows from which the tensor-core GEMV is used
+TC_MIN_ROWS = 4                  # activation rows from which the tensor-core GEMV is used
 HAVE_CUDA_KERNELS = HAVE_TRITON
 FUSED_KERNELS_ENABLED = True
 

@@ -109,7 +109,7 @@ VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, in
 
 /*
  * Workspace bytes vq2_gemv_multi / vq2_gemv use for M activation rows of length n (0 for one
- * row; -1 on bad sizes). With mode ROTATED, n % 128 == 0 and M >= 8 (or M >= 2 when the
+ * row; -1 on bad sizes). With mode ROTATED, n % 128 == 0 and M >= 4 (or M >= 2 when the
  * matrices total >= 16384 rows) the GEMV runs on the tensor cores (mma.sync m16n8k16 fed directly by the codebook gathers, activations split into
  * 16-bit hi + lo halves held in the workspace, 16-byte aligned); with no workspace, or one too
  * small, it runs on the CUDA cores with the same result.

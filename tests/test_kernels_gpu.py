@@ -331,6 +331,21 @@ def test_tensor_core_batched_gemv(cbs, M, bits, cbdt):
     assert rel_err(y, ref) < 3e-5
 
 
+@pytest.mark.parametrize("out,n,M", [(2048, 6144, 16), (9000, 1024, 24), (40000, 2048, 8), (130, 256, 64)])
+def test_tensor_core_split_k_shapes(cbs, out, n, M):
+    """Split-K over thread-block clusters (items that fill less than half the GPU: S = 8, 4, 1,
+    and K too short to split) agrees with the fp64 oracle to fp32 accuracy."""
+    idx, scale = synth.random_matrix(out + n, out, n)
+    cbd = dev_cbs(cbs)
+    sc = torch.from_numpy(scale).to(DEV)
+    x = np.random.default_rng(out).standard_normal((M, n)).astype(np.float32)
+    y = kernels.vq_gemv(torch.from_numpy(x).to(DEV), torch.from_numpy(idx[0]).to(DEV), cbd["16"], sc,
+                        out_dtype=torch.float32).cpu().numpy()
+    cb_np = cbd["16"].float().cpu().numpy()
+    ref = np.stack([O.vq_gemv_legacy(x[m], idx[0], cb_np, scale.astype(np.float32), 1.0) for m in range(M)])
+    assert rel_err(y, ref) < 3e-5
+
+
 def test_tensor_core_path_without_workspace_falls_back_exactly(cbs):
     """vq2_gemv with M >= 8 but no workspace runs the CUDA-core kernel: same result."""
     from compressai_b200 import _lib
