@@ -50,6 +50,10 @@ SIGNATURES = {
     "vq2_rans_encode": [_p, _i64, _p, _i64, _p],
     "vq2_rans_decode": [_p, _i64, _i64, _p, _i64, _p, _p],
     "vq2_rans_decode_segments": [_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p],
+    "vq2_lru_state_ints": [_i64, _i64],
+    "vq2_lru_step": [_p, _p, _i64, _p, _p, _p],
+    "vq2_fetch_records": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _p],
+    "vq2_host_device_pointer": [_p, _p],
     "vq2_paged_moe_step": [_p, _p, _i32, _i64, _i64, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i32, _p],
 }
 
@@ -89,7 +93,7 @@ def load():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
             fn.restype = (ctypes.c_char_p if name == "vq2_status_string" else
-                          ctypes.c_int64 if name.endswith(("_workspace", "_bound")) else ctypes.c_int)
+                          ctypes.c_int64 if name.endswith(("_workspace", "_bound", "_ints")) else ctypes.c_int)
         if lib.vq2_abi_version() != ABI_VERSION:
             raise VQ2Error(f"ABI version mismatch: library {lib.vq2_abi_version()}, python {ABI_VERSION}")
         _lib = lib

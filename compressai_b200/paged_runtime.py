@@ -575,3 +575,94 @@ class PagedMoEExpert(nn.Module):
             self._join_loads(stream)
         self._run(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T])
         return out
+
+
+class DeviceResidentPagedMoE:
+    """Device-resident paged MoE decode (T = 1) over a pinned ``.vq2m`` image: per layer step,
+    ``vq2_lru_step`` (the reference ``_get_slot`` LRU, vq2/paged_runtime.py:415-437, as a GPU
+    kernel), ``vq2_fetch_records`` (missed records read by the SMs from the pinned image,
+    zero-copy) and the routed-expert FFN on the slots -- no host synchronisation, so the steps of
+    all layers (with the router) can be captured in one CUDA graph. This removes the per-layer
+    ``.tolist()`` read-back of reference ``PagedMoEExpert.forward`` (:443). Hit/miss/slot
+    sequences are bit-exact with the reference LRU; capacity must be at least top_k."""
+
+    def __init__(self, store, cb16, capacity=39, device=DEVICE, top_k=8):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DeviceResidentPagedMoE runs on CUDA only")
+        if not store.pinned_image() or store.ans_coded:
+            raise ValueError("device-resident paging needs a raw .vq2m held in a pinned host image")
+        if capacity < top_k:
+            raise ValueError("capacity must be >= top_k (a step must not evict its own experts)")
+        lib = _lib.load()
+        dptr = ctypes.c_void_p()
+        _lib.check(lib.vq2_host_device_pointer(store.image.data_ptr(), ctypes.byref(dptr)), "vq2_host_device_pointer")
+        self.image_dev = dptr.value
+        self.store, self.cb16, self.capacity, self.top_k = store, cb16, capacity, top_k
+        L, E = store.num_layers, store.num_experts
+        self.num_layers, self.num_experts = L, E
+        self.pools = [moe.ExpertRecordPool(capacity, self.device, store.gu_rows, store.gu_cols, store.dn_rows,
+                                           store.dn_cols) for _ in range(L)]
+        self.state = torch.from_numpy(np.stack([self.initial_lru_state(E, capacity)] * L)).to(self.device)
+        base = store.layout
+        self.rec_off = torch.tensor([[base.record(ln, e)[0] for e in range(E)] for ln in range(L)], dtype=torch.int64,
+                                    device=self.device)
+        self.slots = torch.empty(L, top_k, dtype=torch.int32, device=self.device)
+        self.miss = torch.zeros(L, 1 + 2 * top_k, dtype=torch.int32, device=self.device)
+        self.ws_bytes = lib.vq2_moe_expert_ffn_workspace(1, top_k, store.gu_rows, store.dn_rows)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.device)
+        self.rot_in = vq.get_rot("moe_expert_2048", store.gu_cols * 8, self.device)
+        self.rot_mid = vq.get_rot("moe_expert_512", store.gu_rows // 2, self.device)
+
+    @staticmethod
+    def initial_lru_state(num_experts, capacity):
+        """The int32 LRU state of vq2_lru_step for an empty pool: no experts, list(range(cap))
+        as the free-slot stack (reference PagedMoEExpert.__init__, vq2/paged_runtime.py:344-348)."""
+        nst = _lib.load().vq2_lru_state_ints(num_experts, capacity)
+        st = np.full(nst, -1, dtype=np.int32)
+        st[2] = capacity
+        st[3:5] = 0
+        st[5] = capacity
+        st[6] = num_experts
+        st[7] = 0
+        st[8 + 3 * num_experts:] = np.arange(capacity, dtype=np.int32)
+        return st
+
+    def layer(self, ln, hidden, ids, weights, out=None):
+        """One layer for one token: hidden [1, H], ids int32 [top_k] and weights fp32 [1, top_k]
+        on the device (router output). Returns [1, H] in hidden's dtype (or fills ``out``)."""
+        lib = _lib.load()
+        st = _lib.stream_ptr(self.device)
+        K = self.top_k
+        if ids.dtype != torch.int32 or ids.numel() != K or not ids.is_cuda:
+            raise ValueError("ids must be an int32 CUDA tensor of top_k entries")
+        h = hidden.reshape(1, -1)
+        if out is None:
+            out = torch.empty_like(h)
+        pool = self.pools[ln]
+        _lib.check(lib.vq2_lru_step(_lib.ptr(self.state[ln]), _lib.ptr(ids), K, _lib.ptr(self.slots[ln]),
+                                    _lib.ptr(self.miss[ln]), st), "vq2_lru_step")
+        _lib.check(lib.vq2_fetch_records(self.image_dev, _lib.ptr(self.rec_off[ln]), pool.record_bytes,
+                                         _lib.ptr(pool.raw), self.capacity, _lib.ptr(self.miss[ln]), K,
+                                         self.num_experts, st), "vq2_fetch_records")
+        ri, rm = self.rot_in, self.rot_mid
+        _lib.call("vq2_moe_expert_ffn", _lib.ptr(h), _lib.dtype_code(h), 1, K, _lib.ptr(self.slots[ln]),
+                  _lib.ptr(weights), _lib.ptr(pool.raw), self.capacity, self.store.gu_rows, self.store.gu_cols,
+                  self.store.dn_rows, self.store.dn_cols, _lib.ptr(self.cb16), _lib.dtype_code(self.cb16),
+                  _lib.ptr(ri.perm), _lib.ptr(ri.sign), ri.hb, float(ri.scale), _lib.ptr(rm.perm),
+                  _lib.ptr(rm.sign), rm.hb, float(rm.scale), _lib.ptr(self.ws), self.ws_bytes, _lib.ptr(out),
+                  _lib.dtype_code(out), st)
+        return out
+
+    def lru_view(self, ln):
+        """Host copy of one layer's LRU: (hits, misses, expert_to_slot dict, access order list,
+        error flag) -- for checking against the reference sequence."""
+        s = self.state[ln].cpu().numpy()
+        E = self.num_experts
+        e2s = s[8:8 + E]
+        nxt = s[8 + 2 * E:8 + 3 * E]
+        order, x = [], int(s[0])
+        while x >= 0 and len(order) <= E:
+            order.append(x)
+            x = int(nxt[x])
+        return int(s[3]), int(s[4]), {int(e): int(e2s[e]) for e in np.nonzero(e2s >= 0)[0]}, order, int(s[7])

@@ -356,6 +356,34 @@ VQ2_API int vq2_paged_moe_step(const vq2_paged_layer* layer, const void* h, int 
                                const int32_t* miss_slot, const int64_t* miss_seg, void* workspace,
                                int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
+/*
+ * ---- Device-resident paging (T = 1 decode without host round trips) ----
+ * The LRU decision of PagedMoEExpert._get_slot (vq2/paged_runtime.py:415-437) as a GPU kernel
+ * and a fetch of missed records from the pinned host image by the SMs (zero-copy), so router ->
+ * LRU -> fetch -> expert FFN of every layer can run in one CUDA graph.
+ *
+ * LRU state of one layer: int32 [vq2_lru_state_ints(E, cap)] = {head, tail, free count, hits,
+ * misses, cap, E, error}, expert->slot [E] (-1 absent), prev [E], next [E], free-slot stack [cap]
+ * (range(cap), top at the end). vq2_lru_step processes ids[0..K) in order (hit: move to most
+ * recent; miss: pop a free slot, else evict the least recent), writes slots[K] and the miss
+ * list miss = {count, expert[K], slot[K]} (int32 [1 + 2K]); it sets the error flag if a slot
+ * needed earlier in the same step would be reused (capacity < K) -- bit-exact with the
+ * reference for every step it accepts.
+ */
+VQ2_API int64_t vq2_lru_state_ints(int64_t num_experts, int64_t capacity);
+VQ2_API int vq2_lru_step(int32_t* state, const int32_t* ids, int64_t K, int32_t* slots,
+                         int32_t* miss, void* stream);
+/*
+ * Copy the records of a miss list into their pool slots: record e of the layer is rec_bytes at
+ * image_dev + rec_off[e] (device int64 [num_experts]); image_dev is the device address of a
+ * page-locked host image (vq2_host_device_pointer); rec_bytes % 16 == 0, 16-byte alignment.
+ */
+VQ2_API int vq2_fetch_records(const void* image_dev, const int64_t* rec_off, int64_t rec_bytes,
+                              void* pool, int64_t capacity, const int32_t* miss, int64_t K,
+                              int64_t num_experts, void* stream);
+/* Device address of page-locked host memory (VQ2_ERR_ARG if it is not mapped). */
+VQ2_API int vq2_host_device_pointer(const void* host, void** device_ptr);
+
 #ifdef __cplusplus
 }
 #endif
