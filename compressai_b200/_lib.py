@@ -50,6 +50,8 @@ SIGNATURES = {
     "vq2_rans_encode": [_p, _i64, _p, _i64, _p],
     "vq2_rans_decode": [_p, _i64, _i64, _p, _i64, _p, _p],
     "vq2_rans_decode_segments": [_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p],
+    "vq2_moe_expert_ffn_res": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _p,
+                               _i64, _f32, _p, _p, _i64, _f32, _p, _p, _i64, _p, _i32, _p],
     "vq2_lru_state_ints": [_i64, _i64],
     "vq2_lru_step": [_p, _p, _i64, _p, _p, _p],
     "vq2_fetch_records": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _p],

@@ -38,8 +38,11 @@ RESERVED_HEADER_BYTES = 2 * 1024 * 1024
 DEFAULT_DIMS = dict(gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64)
 
 
-def record_bytes(gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64):
-    return gu_rows * gu_cols * 2 + gu_rows * 2 + dn_rows * dn_cols * 2 + dn_rows * 2
+def record_bytes(gu_rows=1024, gu_cols=256, dn_rows=2048, dn_cols=64, bits=2):
+    """Bytes of one expert record: 792,576 at 2 bpw, 1,185,792 for a promoted 3 bpw expert
+    (each index entry is idx0 int16 followed by idx1 uint8)."""
+    w = 3 if bits == 3 else 2
+    return gu_rows * gu_cols * w + gu_rows * 2 + dn_rows * dn_cols * w + dn_rows * 2
 
 
 class Vq2mLayout:
@@ -89,6 +92,10 @@ class Vq2mLayout:
         k = 0 if self.ans_coded else 1
         return [(0, sg, 0, n_gi, k), (os_ - og, ss, n_gi, n_gs, 1), (od - og, sd, n_gi + n_gs, n_di, k),
                 (ods - og, sds, n_gi + n_gs + n_di, n_ds, 1)]
+
+    def expert_mode(self, layer, expert):
+        """3 for a promoted 3 bpw expert (meta expert_modes["L:E"] == 3), else 2."""
+        return 3 if self.meta.get("expert_modes", {}).get(f"{layer}:{expert}") == 3 else 2
 
     def record(self, layer, expert):
         """(offset, nbytes) of the contiguous record of one expert; raises if the four tensors
@@ -178,14 +185,39 @@ def write_vq2m(path, num_layers, num_experts, expert_fn, dims=None, meta_extra=N
     as VQ2A rANS streams (host encoder of the C-ABI library). Returns the file size."""
     dims = dict(DEFAULT_DIMS, **(dims or {}))
     if index_coding == "raw":
-        table, meta, end = _table_and_meta(num_layers, num_experts, dims, meta_extra)
+        # experts returned as 6-tuples (idx0, idx1, scale per matrix) are promoted 3 bpw experts:
+        # index entries idx0 || idx1 and meta expert_modes["L:E"] = 3
+        _, meta, _ = _table_and_meta(num_layers, num_experts, dims, meta_extra)
+        table = [[None] * num_experts for _ in range(num_layers)]
+        modes = {}
+        off = RESERVED_HEADER_BYTES
         with open(path, "wb") as f:
-            f.write(_header_bytes(num_layers, num_experts, table, meta))
+            f.write(b"\x00" * RESERVED_HEADER_BYTES)
             for ln in range(num_layers):
                 for e in range(num_experts):
-                    for a in _typed(expert_fn(ln, e)):
+                    parts = expert_fn(ln, e)
+                    if len(parts) == 6:
+                        gi0, gi1, gs, di0, di1, ds = parts
+                        ent = [np.concatenate([np.ascontiguousarray(gi0, np.int16).view(np.uint8).reshape(-1),
+                                               np.ascontiguousarray(gi1, np.uint8).reshape(-1)]),
+                               np.ascontiguousarray(gs, np.float16).view(np.uint8).reshape(-1),
+                               np.concatenate([np.ascontiguousarray(di0, np.int16).view(np.uint8).reshape(-1),
+                                               np.ascontiguousarray(di1, np.uint8).reshape(-1)]),
+                               np.ascontiguousarray(ds, np.float16).view(np.uint8).reshape(-1)]
+                        modes[f"{ln}:{e}"] = 3
+                    else:
+                        ent = [a.view(np.uint8).reshape(-1) for a in _typed(parts)]
+                    row = []
+                    for a in ent:
+                        row += [off, a.size]
                         f.write(a.tobytes())
-        return end
+                        off += a.size
+                    table[ln][e] = tuple(row)
+            if modes:
+                meta = dict(meta, expert_modes=modes)
+            f.seek(0)
+            f.write(_header_bytes(num_layers, num_experts, table, meta))
+        return off
     if index_coding != "vq2a":
         raise ValueError(f"unknown index_coding {index_coding!r}")
     from . import ans

@@ -28,7 +28,8 @@ struct GemvArgs {
   const int32_t* prob_count;  // device problem count (<= K) or null: problems [count, K) are skipped
   const int32_t* prob_map;    // [K] original problem index of each (compacted) problem, or null
   int64_t num_experts;
-  int64_t idx_e_stride;   // out * ng
+  int64_t idx_e_stride;   // out * ng (int16 elements between experts' idx0)
+  int64_t idx1_e_stride;  // bytes between experts' idx1 (3 bpw expert pools)
   int64_t scale_e_stride; // out
   int64_t y_k_stride;     // elements between problems k
   // multi-matrix problems (nprob > 0): problem p has its own weights/outputs, one shared x
@@ -89,7 +90,8 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
                    float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host = false,
-                   bool counters_zeroed = false, int32_t* err = nullptr, bool prefer_fused = false);
+                   bool counters_zeroed = false, int32_t* err = nullptr, bool prefer_fused = false,
+                   const void* cb1 = nullptr, const float* add = nullptr);
 
 // Fused single-launch expert FFN for T * top_k <= 64 (moe_fused.cu).
 struct MoeFusedArgs {

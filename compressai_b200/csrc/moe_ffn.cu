@@ -10,16 +10,22 @@
 
 namespace vq2 {
 
+// Byte offsets within one expert record. 2 bpw (.vq2m payload): gu idx0 | gu scale | dn idx0 |
+// dn scale. 3 bpw (promoted experts, reference tools/build_mixed_b2_container.py:50-80): each
+// index entry is idx0 (int16) followed by idx1 (uint8): gu idx0 | gu idx1 | gu scale | dn idx0 |
+// dn idx1 | dn scale (1,185,792 bytes at the 35B-A3B shape).
 struct RecordLayout {
-  int64_t gu_idx, gu_scale, dn_idx, dn_scale, bytes;  // byte offsets within one expert record
+  int64_t gu_idx, gu_idx1, gu_scale, dn_idx, dn_idx1, dn_scale, bytes;
 };
 
-static RecordLayout record_layout(int64_t gr, int64_t gc, int64_t dr, int64_t dc) {
+static RecordLayout record_layout(int64_t gr, int64_t gc, int64_t dr, int64_t dc, bool res = false) {
   RecordLayout r;
   r.gu_idx = 0;
-  r.gu_scale = gr * gc * 2;
+  r.gu_idx1 = gr * gc * 2;
+  r.gu_scale = r.gu_idx1 + (res ? gr * gc : 0);
   r.dn_idx = r.gu_scale + gr * 2;
-  r.dn_scale = r.dn_idx + dr * dc * 2;
+  r.dn_idx1 = r.dn_idx + dr * dc * 2;
+  r.dn_scale = r.dn_idx1 + (res ? dr * dc : 0);
   r.bytes = r.dn_scale + dr * 2;
   return r;
 }
@@ -42,7 +48,7 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
                    float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host,
-                   bool counters_zeroed, int32_t* err, bool prefer_fused) {
+                   bool counters_zeroed, int32_t* err, bool prefer_fused, const void* cb1, const float* add) {
   if (!h || !ids || !w || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid || !ws || !out)
     return VQ2_ERR_ARG;
   if (T <= 0 || top_k <= 0 || top_k > 64 || num_experts <= 0) return VQ2_ERR_SHAPE;
@@ -51,9 +57,10 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   if (dn_cols * 8 != gu_rows / 2 || dn_rows != gu_cols * 8) return VQ2_ERR_SHAPE;  // SwiGLU width / hidden size
   if (h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
   if (out_dtype != VQ2_F32 && out_dtype != VQ2_F16 && out_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
-  const RecordLayout L = record_layout(gu_rows, gu_cols, dn_rows, dn_cols);
-  if (L.bytes % 16 != 0 || L.dn_idx % 16 != 0) return VQ2_ERR_ALIGN;
-  if (!aligned(pool, 16) || !aligned(cb0, 16) || !aligned(ws, 256)) return VQ2_ERR_ALIGN;
+  const bool res = cb1 != nullptr;
+  const RecordLayout L = record_layout(gu_rows, gu_cols, dn_rows, dn_cols, res);
+  if (L.bytes % 16 != 0 || L.dn_idx % 16 != 0 || L.gu_idx1 % 8 != 0 || L.dn_idx1 % 8 != 0) return VQ2_ERR_ALIGN;
+  if (!aligned(pool, 16) || !aligned(cb0, 16) || !aligned(ws, 256) || (res && !aligned(cb1, 16))) return VQ2_ERR_ALIGN;
   const int64_t P = T * top_k;
   if (P > 65536) return VQ2_ERR_SHAPE;
   const int64_t H = gu_cols * 8, I = gu_rows / 2;
@@ -71,7 +78,7 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   // the host): one fused launch (moe_fused.cu) instead of four. Inside a CUDA graph the four
   // kernels are faster on the GPU (40 vs 47 us per 35B layer at T = 1, top-8), so the generic
   // entry points keep them.
-  if (prefer_fused && P <= kIdsByValue && moe_fused_enabled()) {
+  if (prefer_fused && !res && !add && P <= kIdsByValue && moe_fused_enabled()) {
     MoeFusedArgs f{};
     f.h = h; f.h_dtype = h_dtype; f.T = (int)T; f.K = (int)top_k; f.P = (int)P;
     f.ids = ids_on_host ? nullptr : ids;
@@ -106,22 +113,24 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   a.nprob = 0;
   a.x = h; a.x_dtype = h_dtype; a.x_mode = VQ2_ACT_RHT; a.x_row_stride = 0; a.x_k_stride = H; a.x_k_div = top_k;
   a.perm = perm_in; a.sign = sign_in; a.hb = (int)hb_in; a.rot_scale = scale_in; a.M = 1;
-  a.idx0 = reinterpret_cast<const int16_t*>(base + L.gu_idx); a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr;
+  a.idx0 = reinterpret_cast<const int16_t*>(base + L.gu_idx); a.cb0 = cb0;
+  a.idx1 = res ? reinterpret_cast<const uint8_t*>(base + L.gu_idx1) : nullptr; a.cb1 = res ? cb1 : nullptr;
   a.scale = base + L.gu_scale; a.y = gu; a.y_dtype = VQ2_F32; a.y_row_stride = 0; a.y_k_stride = gu_rows;
   a.e_ids = c_ids; a.prob_count = c_cnt; a.prob_map = c_map;
-  a.num_experts = num_experts; a.idx_e_stride = L.bytes / 2; a.scale_e_stride = L.bytes / 2;
+  a.num_experts = num_experts; a.idx_e_stride = L.bytes / 2; a.idx1_e_stride = L.bytes; a.scale_e_stride = L.bytes / 2;
   a.out = (int)gu_rows; a.n = (int)H; a.rs = 1.f; a.K = (int)P;
-  s = run_gemv(a, gu_rows * P, false, val_dtype, st);
+  s = run_gemv(a, gu_rows * P, res, val_dtype, st);
   if (s != VQ2_OK) return s;
 
   GemvArgs b = a;
   b.x = gu; b.x_dtype = VQ2_F32; b.x_mode = VQ2_ACT_SWIGLU_RHT; b.x_k_stride = gu_rows; b.x_k_div = 1;
   b.perm = perm_mid; b.sign = sign_mid; b.hb = (int)hb_mid; b.rot_scale = scale_mid;
   b.idx0 = reinterpret_cast<const int16_t*>(base + L.dn_idx); b.scale = base + L.dn_scale;
+  b.idx1 = res ? reinterpret_cast<const uint8_t*>(base + L.dn_idx1) : nullptr;
   b.y = yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
-  s = run_gemv(b, dn_rows * P, false, val_dtype, st);
+  s = run_gemv(b, dn_rows * P, res, val_dtype, st);
   if (s != VQ2_OK) return s;
-  return run_combine(yd, w, T, (int)top_k, H, nullptr, out, out_dtype, st, ids, num_experts);
+  return run_combine(yd, w, T, (int)top_k, H, add, out, out_dtype, st, ids, num_experts);
 }
 
 }  // namespace vq2
@@ -142,6 +151,23 @@ extern "C" int vq2_moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
                              scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vq2_moe_expert_ffn_res(const void* h, int h_dtype, int64_t T, int64_t top_k, const int32_t* ids,
+                                      const float* w, const void* pool, int64_t num_experts, int64_t gu_rows,
+                                      int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0,
+                                      const void* cb1, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
+                                      int64_t hb_in, float scale_in, const int32_t* perm_mid,
+                                      const int8_t* sign_mid, int64_t hb_mid, float scale_mid, const float* add,
+                                      void* workspace, int64_t workspace_bytes, void* out, int out_dtype,
+                                      void* stream) {
+  if (T <= 0 || top_k <= 0 || gu_rows <= 0 || dn_rows <= 0) return VQ2_ERR_SHAPE;
+  if (!cb1) return VQ2_ERR_ARG;
+  if (workspace_bytes < vq2::moe_ffn_workspace(T * top_k, gu_rows, dn_rows)) return VQ2_ERR_ARG;
+  return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
+                             cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
+                             scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream), false, false,
+                             nullptr, false, cb1, add);
 }
 
 // ---- allocation-free variant -----------------------------------------------------------------

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
       }
       w.e = e;
       w.i0 = a.idx0 + e * a.idx_e_stride;
-      w.i1 = RES ? a.idx1 + e * a.idx_e_stride : nullptr;
+      w.i1 = RES ? a.idx1 + e * a.idx1_e_stride : nullptr;
     }
     return w;
   };
@@ -477,7 +477,8 @@ extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_
   a.x_k_div = x_k_div; a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale; a.M = 1;
   a.idx0 = idx; a.idx1 = nullptr; a.cb0 = cb0; a.cb1 = nullptr; a.scale = scale;
   a.y = y; a.y_dtype = y_dtype; a.y_row_stride = 0; a.y_k_stride = out;
-  a.e_ids = e_ids; a.num_experts = num_experts; a.idx_e_stride = idx_e_stride; a.scale_e_stride = scale_e_stride;
+  a.e_ids = e_ids; a.num_experts = num_experts; a.idx_e_stride = idx_e_stride; a.idx1_e_stride = idx_e_stride;
+  a.scale_e_stride = scale_e_stride;
   a.out = (int)out; a.n = (int)(ng * 8); a.rs = rs; a.K = (int)K;
   return run_gemv(a, out * K, false, val_dtype, static_cast<cudaStream_t>(stream));
 }

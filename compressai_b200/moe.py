@@ -58,6 +58,48 @@ class ExpertRecordPool:
         self.dn_scale[e].copy_(torch.as_tensor(dn_scale).to(torch.float16))
 
 
+class Expert3Pool:
+    """Resident pool of promoted 3 bpw expert records (reference expert_modes == 3; record =
+    gu idx0 int16 | gu idx1 uint8 | gu scale fp16 | dn idx0 int16 | dn idx1 uint8 | dn scale fp16,
+    1,185,792 B at the 35B-A3B shape, tools/build_mixed_b2_container.py:50-80)."""
+
+    def __init__(self, E, device, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_cols=DN_COLS):
+        self.dims = (gu_rows, gu_cols, dn_rows, dn_cols)
+        self.E = E
+        self.record_bytes = 3 * gu_rows * gu_cols + 2 * gu_rows + 3 * dn_rows * dn_cols + 2 * dn_rows
+        self.raw = torch.zeros(max(E, 1), self.record_bytes, dtype=torch.uint8, device=device)
+
+    def set_record(self, e, rec):
+        """Copy one stored 3 bpw record (host bytes, in container order) into row e."""
+        self.raw[e].copy_(torch.as_tensor(rec).reshape(-1))
+
+
+def expert_ffn_res(hidden, ids, weights, pool3, cb16, cb8, rot_in, rot_mid, top_k, add=None, out=None,
+                   out_dtype=None):
+    """expert_ffn over a pool of 3 bpw expert records (vq2_moe_expert_ffn_res): ids index rows of
+    ``pool3`` (-1 = not in this pool); ``add`` (fp32 [T, H]) is added before the output cast."""
+    _lib.require_cuda(hidden, ids, weights, cb16, cb8)
+    T, H = hidden.shape
+    gr, gc, dr, dc = pool3.dims
+    h = hidden.contiguous()
+    ids = ids.contiguous()
+    w = weights.float().contiguous()
+    out_dtype = out_dtype or hidden.dtype
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=h.device)
+    addc = add.float().contiguous() if add is not None else None
+    lib = _lib.load()
+    ws_bytes = lib.vq2_moe_expert_ffn_workspace(T, top_k, gr, dr)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=h.device)
+    _lib.call("vq2_moe_expert_ffn_res", _lib.ptr(h), _lib.dtype_code(h), T, top_k, _lib.ptr(ids), _lib.ptr(w),
+              _lib.ptr(pool3.raw), pool3.E, gr, gc, dr, dc, _lib.ptr(cb16), _lib.ptr(cb8), _lib.dtype_code(cb16),
+              _lib.ptr(rot_in.perm), _lib.ptr(rot_in.sign), rot_in.hb, float(rot_in.scale), _lib.ptr(rot_mid.perm),
+              _lib.ptr(rot_mid.sign), rot_mid.hb, float(rot_mid.scale),
+              _lib.ptr(addc) if addc is not None else None, _lib.ptr(ws), ws_bytes, _lib.ptr(out),
+              _lib.dtype_code(out), _lib.stream_ptr(h.device))
+    return out
+
+
 def route(logits, top_k=8, hidden=None, shared_gate=None):
     """Router on device logits fp32 [T, E] -> (ids int32 [T, top_k], w fp32 [T, top_k]
     [, shared_w fp32 [T]]); the math of Qwen3_5MoeTopKRouter (softmax, topk, renormalise) and

@@ -370,7 +370,7 @@ class PagedMoEExpert(nn.Module):
     topk_weights [T, k]) -> [T, H] in the hidden dtype. topk_idx on the host avoids the
     device-to-host read of the ids (the reference always reads them back, :443)."""
 
-    def __init__(self, layer_idx, store, cb16, capacity=96, device=DEVICE, copy_stream=None):
+    def __init__(self, layer_idx, store, cb16, capacity=96, device=DEVICE, copy_stream=None, cb8=None):
         super().__init__()
         self.layer_idx = layer_idx
         self.store = store
@@ -379,9 +379,23 @@ class PagedMoEExpert(nn.Module):
         self.device = torch.device(device)
         self.hidden_dim = store.gu_cols * 8
         self.intermediate_dim = store.gu_rows // 2
-        modes = store.meta.get("expert_modes", {})
-        if any(modes.get(f"{layer_idx}:{e}") == 3 for e in range(store.num_experts)):
-            raise NotImplementedError("3-bit promoted experts (expert_modes) are not supported by the paged pool")
+        # Promoted 3 bpw experts (expert_modes == 3) stay resident and bypass the LRU, as in the
+        # reference (vq2/paged_runtime.py:357-389, 446-460); here they stay in VQ form (no dense
+        # bf16 weights) and run through the residual-codebook expert FFN.
+        self.promoted = [e for e in range(store.num_experts) if store.layout.expert_mode(layer_idx, e) == 3]
+        self._promoted_row = {e: i for i, e in enumerate(self.promoted)}
+        self.pool3, self.cb8 = None, cb8
+        if self.promoted:
+            if cb8 is None:
+                raise ValueError(f"layer {layer_idx} has promoted 3-bit experts: pass cb8 (the '16_8' codebook)")
+            self.pool3 = moe.Expert3Pool(len(self.promoted), self.device, store.gu_rows, store.gu_cols,
+                                         store.dn_rows, store.dn_cols)
+            for e, row in self._promoted_row.items():
+                rec = store.read_record(layer_idx, e)
+                if rec.size != self.pool3.record_bytes:
+                    raise ValueError(f"promoted expert ({layer_idx}, {e}) record has {rec.size} bytes, "
+                                     f"expected {self.pool3.record_bytes}")
+                self.pool3.set_record(row, torch.from_numpy(rec))
         self.pool = moe.ExpertRecordPool(capacity, self.device, store.gu_rows, store.gu_cols, store.dn_rows,
                                          store.dn_cols)
         # reference attribute names, as views into the record pool
@@ -484,8 +498,21 @@ class PagedMoEExpert(nn.Module):
             ids_done=self._ids_done.cuda_event)
         return self._layer
 
-    def _step(self, h, slot_rows, w, out, misses, stream):
-        """Load ``misses`` and run the experts of tokens h on ``slot_rows`` in one native call."""
+    def _promoted(self, h, rows3, w, partial, out):
+        """Add the promoted experts (pool3 rows ``rows3``, -1 elsewhere) to the fp32 partial of
+        the paged experts, writing ``out``."""
+        ids3 = torch.as_tensor(rows3, dtype=torch.int32).reshape(-1).pin_memory().to(self.device, non_blocking=True)
+        moe.expert_ffn_res(h, ids3, w, self.pool3, self.cb16, self.cb8, self.rot_2048, self.rot_512, w.shape[1],
+                           add=partial, out=out)
+
+    def _step(self, h, slot_rows, w, out, misses, stream, rows3=None):
+        """Load ``misses`` and run the experts of tokens h on ``slot_rows`` in one native call
+        (plus the promoted experts of ``rows3``)."""
+        if rows3 is not None and any(r >= 0 for row in rows3 for r in row):
+            partial = torch.empty(out.shape, dtype=torch.float32, device=self.device)
+            self._step(h, slot_rows, w, partial, misses, stream)
+            self._promoted(h, rows3, w, partial, out)
+            return
         T, K = len(slot_rows), len(slot_rows[0])
         layer = self._native_layer(T * K)
         need = _lib.load().vq2_moe_expert_ffn_workspace(T, K, self.store.gu_rows, self.store.dn_rows)
@@ -506,21 +533,29 @@ class PagedMoEExpert(nn.Module):
 
     def _forward_native(self, h, ids_list, w, out, stream):
         T = h.shape[0]
-        seg_start, seg_slots, slot_rows, misses = 0, set(), [], []
+        seg_start, seg_slots, slot_rows, rows3, misses = 0, set(), [], [], []
+        promoted = self._promoted_row
         for t in range(T):
-            row = []
+            row, row3 = [], []
             for e in ids_list[t]:
-                slot, hit = self._assign_slot(int(e))
+                e = int(e)
+                if e in promoted:  # resident 3 bpw expert: not paged, not counted by the LRU
+                    row.append(-1)
+                    row3.append(promoted[e])
+                    continue
+                row3.append(-1)
+                slot, hit = self._assign_slot(e)
                 if not hit and slot in seg_slots:
                     # the slot is still to be read by earlier tokens of this batch: run them first
-                    self._step(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t], misses, stream)
-                    seg_start, seg_slots, slot_rows, misses = t, set(), [], []
+                    self._step(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t], misses, stream, rows3)
+                    seg_start, seg_slots, slot_rows, rows3, misses = t, set(), [], [], []
                 if not hit:
-                    misses.append((int(e), slot))
+                    misses.append((e, slot))
                 row.append(slot)
             slot_rows.append(row)
+            rows3.append(row3)
             seg_slots.update(row)
-        self._step(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T], misses, stream)
+        self._step(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T], misses, stream, rows3)
         return out
 
     def _join_loads(self, stream):
@@ -528,11 +563,17 @@ class PagedMoEExpert(nn.Module):
             stream.wait_stream(s)
 
     # ---- compute ----------------------------------------------------------------------------
-    def _run(self, h, slots, w, out):
-        """Expert FFN of tokens h [t, H] on pool slots [t, k] with weights [t, k] into out."""
+    def _run(self, h, slots, w, out, rows3=None):
+        """Expert FFN of tokens h [t, H] on pool slots [t, k] with weights [t, k] into out (plus
+        the promoted experts of ``rows3``)."""
         stream = torch.cuda.current_stream(self.device)
         ids = torch.as_tensor(slots, dtype=torch.int32).reshape(-1).pin_memory().to(self.device, non_blocking=True)
-        moe.expert_ffn(h, ids, w, self.pool, self.cb16, self.rot_2048, self.rot_512, w.shape[1], out=out)
+        if rows3 is not None and any(r >= 0 for row in rows3 for r in row):
+            partial = moe.expert_ffn(h, ids, w, self.pool, self.cb16, self.rot_2048, self.rot_512, w.shape[1],
+                                     out_dtype=torch.float32)
+            self._promoted(h, rows3, w, partial, out)
+        else:
+            moe.expert_ffn(h, ids, w, self.pool, self.cb16, self.rot_2048, self.rot_512, w.shape[1], out=out)
         self._compute_done.record(stream)
 
     def forward(self, hidden_states, topk_idx, topk_weights):
@@ -553,27 +594,35 @@ class PagedMoEExpert(nn.Module):
         if self.native:
             return self._forward_native(h, ids_list, w, out, stream)
 
-        seg_start, seg_slots, slot_rows = 0, set(), []
+        seg_start, seg_slots, slot_rows, rows3 = 0, set(), [], []
         loads_in_seg = False
+        promoted = self._promoted_row
         for t in range(T):
-            row = []
+            row, row3 = [], []
             for e in ids_list[t]:
-                slot, hit = self._assign_slot(int(e))
+                e = int(e)
+                if e in promoted:  # resident 3 bpw expert: not paged, not counted by the LRU
+                    row.append(-1)
+                    row3.append(promoted[e])
+                    continue
+                row3.append(-1)
+                slot, hit = self._assign_slot(e)
                 if not hit and slot in seg_slots:
                     # the slot is still to be read by earlier tokens of this batch: run them first
                     if loads_in_seg:
                         self._join_loads(stream)
-                    self._run(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t])
-                    seg_start, seg_slots, slot_rows, loads_in_seg = t, set(), [], False
+                    self._run(h[seg_start:t], slot_rows, w[seg_start:t], out[seg_start:t], rows3)
+                    seg_start, seg_slots, slot_rows, rows3, loads_in_seg = t, set(), [], [], False
                 if not hit:
-                    self._load(int(e), slot)
+                    self._load(e, slot)
                     loads_in_seg = True
                 row.append(slot)
             slot_rows.append(row)
+            rows3.append(row3)
             seg_slots.update(row)
         if loads_in_seg:
             self._join_loads(stream)
-        self._run(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T])
+        self._run(h[seg_start:T], slot_rows, w[seg_start:T], out[seg_start:T], rows3)
         return out
 
 
@@ -594,6 +643,8 @@ class DeviceResidentPagedMoE:
             raise ValueError("device-resident paging needs a raw .vq2m held in a pinned host image")
         if capacity < top_k:
             raise ValueError("capacity must be >= top_k (a step must not evict its own experts)")
+        if store.meta.get("expert_modes"):
+            raise ValueError("device-resident paging does not serve promoted 3-bit experts; use PagedMoEExpert")
         lib = _lib.load()
         dptr = ctypes.c_void_p()
         _lib.check(lib.vq2_host_device_pointer(store.image.data_ptr(), ctypes.byref(dptr)), "vq2_host_device_pointer")

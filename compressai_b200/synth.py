@@ -27,6 +27,15 @@ def synth_expert(seed, e, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_
     return gu_idx, gu_sc, dn_idx, dn_sc
 
 
+def synth_expert_3bit(seed, e, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_cols=DN_COLS):
+    """A promoted 3 bpw expert (reference tools/build_mixed_b2_container.py:50-80): (gu_idx0 int16,
+    gu_idx1 uint8, gu_scale fp16, dn_idx0 int16, dn_idx1 uint8, dn_scale fp16), seeded."""
+    gi, gs, di, ds = synth_expert(seed, e, gu_rows, gu_cols, dn_rows, dn_cols)
+    rng = np.random.default_rng([int(seed), int(e), 0x3B])
+    return (gi, rng.integers(0, 256, size=gi.shape, dtype=np.uint8), gs, di,
+            rng.integers(0, 256, size=di.shape, dtype=np.uint8), ds)
+
+
 def synth_expert_skewed(seed, e, gu_rows=GU_ROWS, gu_cols=GU_COLS, dn_rows=DN_ROWS, dn_cols=DN_COLS,
                         sigma=3000.0):
     """As synth_expert, but indices |N(0, sigma)| (clipped to 65535): a codebook whose rows are

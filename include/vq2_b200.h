@@ -207,6 +207,25 @@ VQ2_API int vq2_moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t to
                                int64_t hb_mid, float scale_mid, void* workspace,
                                int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
+/*
+ * vq2_moe_expert_ffn over a pool of 3 bpw expert records (promoted "anchor" experts,
+ * expert_modes["L:E"] == 3 in the .vq2m meta): each index entry is idx0 int16 [rows, cols]
+ * followed by idx1 uint8 [rows, cols] (gate_up idx0 | idx1 | scales | down idx0 | idx1 | scales,
+ * 1,185,792 bytes at the 35B-A3B shape), decoded as cb0[idx0] + cb1[idx1] (cb1: [256, 8]). add:
+ * optional fp32 [T, H] added to the routing-weighted sum before the output conversion (the
+ * regular experts' partial). Replaces the dense-bf16 promoted-expert path of reference
+ * PagedMoEExpert (vq2/paged_runtime.py:357-389, 446-460) without dequantizing the weights.
+ */
+VQ2_API int vq2_moe_expert_ffn_res(const void* h, int h_dtype, int64_t T, int64_t top_k,
+                                   const int32_t* ids, const float* w, const void* pool,
+                                   int64_t num_experts, int64_t gu_rows, int64_t gu_cols,
+                                   int64_t dn_rows, int64_t dn_cols, const void* cb0,
+                                   const void* cb1, int val_dtype, const int32_t* perm_in,
+                                   const int8_t* sign_in, int64_t hb_in, float scale_in,
+                                   const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
+                                   float scale_mid, const float* add, void* workspace,
+                                   int64_t workspace_bytes, void* out, int out_dtype, void* stream);
+
 /* Workspace bytes vq2_moe_expert_ffn needs for T tokens x top_k experts (-1 on bad sizes). */
 VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows,
                                              int64_t dn_rows);

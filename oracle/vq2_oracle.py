@@ -163,13 +163,16 @@ def silu(v):
     return v / (1.0 + np.exp(-v))
 
 
-def moe_layer_ref(h, ids, w, experts, cb16, rot2048, rot512, shared=None, shared_w=None):
+def moe_layer_ref(h, ids, w, experts, cb16, rot2048, rot512, shared=None, shared_w=None, cb8=None):
     """One MoE layer for T tokens, fp64: per token, per selected expert, gate_up -> silu(gate)*up
     -> RHT512 -> down, then the routing-weighted sum -- PagedMoEExpert.forward,
     vq2/paged_runtime.py:491-511 (T=1) and :553-566 (T>1), with the CPU expert kernels
     (:19-41) and Rot.fwd (vq.py:78-82). ``experts(e)`` returns (gu_idx, gu_scale, dn_idx,
-    dn_scale). ``shared`` (same tuple) with per-token weight ``shared_w`` adds the always-on
-    shared expert as Qwen3_5MoeSparseMoeBlock.forward does (modeling_qwen3_5_moe.py:781-791)."""
+    dn_scale), or for a promoted 3 bpw expert (gu_idx0, gu_idx1, gu_scale, dn_idx0, dn_idx1,
+    dn_scale) decoded as cb16[idx0] + cb8[idx1] (reference PagedMoEExpert promoted path,
+    vq2/paged_runtime.py:357-389, 446-460, here without the bf16 rounding of its dense weights).
+    ``shared`` (same tuple) with per-token weight ``shared_w`` adds the always-on shared expert as
+    Qwen3_5MoeSparseMoeBlock.forward does (modeling_qwen3_5_moe.py:781-791)."""
     h = np.asarray(h, dtype=np.float64)
     T = h.shape[0]
     out = np.zeros((T, h.shape[1]))
@@ -178,12 +181,16 @@ def moe_layer_ref(h, ids, w, experts, cb16, rot2048, rot512, shared=None, shared
         plist = [(experts(int(e)), float(wk)) for e, wk in zip(ids[t], w[t])]
         if shared is not None:
             plist.append((shared, float(shared_w[t])))
-        for (gu_i, gu_s, dn_i, dn_s), wk in plist:
-            y_gu = vq_gemv_legacy(xr, gu_i, cb16, gu_s, 1.0)
+        for ex, wk in plist:
+            if len(ex) == 6:
+                gu_i, gu_i1, gu_s, dn_i, dn_i1, dn_s = ex
+            else:
+                (gu_i, gu_s, dn_i, dn_s), gu_i1, dn_i1 = ex, None, None
+            y_gu = vq_gemv_legacy(xr, gu_i, cb16, gu_s, 1.0, gu_i1, cb8)
             half = y_gu.shape[0] // 2
             act = silu(y_gu[:half]) * y_gu[half:]
             act_r = rht_fwd(act, *rot512)
-            out[t] += wk * vq_gemv_legacy(act_r, dn_i, cb16, dn_s, 1.0)
+            out[t] += wk * vq_gemv_legacy(act_r, dn_i, cb16, dn_s, 1.0, dn_i1, cb8)
     return out
 
 

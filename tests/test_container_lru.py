@@ -105,3 +105,35 @@ def test_cpu_forward_is_refused():
     m = _lru_module(4)
     with pytest.raises(ValueError, match="CUDA"):
         m(torch.zeros(1, 64), torch.zeros(1, 8, dtype=torch.long), torch.zeros(1, 8))
+
+
+def test_promoted_3bit_experts_in_container(tmp_path):
+    """Promoted 3 bpw experts (6-tuples) are written as idx0 || idx1 entries with
+    expert_modes["L:E"] = 3 and 1,185,792-byte records at the 35B shape; the LRU of a CPU-side
+    PagedMoEExpert never sees them (reference vq2/paged_runtime.py:446-460)."""
+    promoted = {(0, 3), (1, 0), (1, 4)}
+    fn = lambda ln, e: (synth.synth_expert_3bit(ln, e, **DIMS) if (ln, e) in promoted
+                        else synth.synth_expert(ln, e, **DIMS))
+    path = str(tmp_path / "m.vq2m")
+    container.write_vq2m(path, 2, 6, fn, dims=DIMS)
+    st = paged_runtime.PagedModelStore(path, device="cpu")
+    lay = st.layout
+    assert lay.meta["expert_modes"] == {f"{ln}:{e}": 3 for ln, e in promoted}
+    for ln in range(2):
+        for e in range(6):
+            bits = 3 if (ln, e) in promoted else 2
+            assert lay.expert_mode(ln, e) == bits
+            assert lay.record(ln, e)[1] == container.record_bytes(bits=bits, **DIMS)
+            rec = st.read_record(ln, e)
+            parts = fn(ln, e)
+            want = np.concatenate([np.ascontiguousarray(a).view(np.uint8).reshape(-1) for a in parts]) if bits == 2 \
+                else np.concatenate([np.ascontiguousarray(a).view(np.uint8).reshape(-1) for a in
+                                     (parts[0], parts[1], parts[2], parts[3], parts[4], parts[5])])
+            assert np.array_equal(rec, want)
+    assert container.record_bytes(bits=3) == 1185792
+    m = paged_runtime.PagedMoEExpert(1, st, torch.zeros(65536, 8, dtype=torch.float16), capacity=3, device="cpu",
+                                     cb8=torch.zeros(256, 8, dtype=torch.float16))
+    assert m.promoted == [0, 4] and m.pool3.record_bytes == container.record_bytes(bits=3, **DIMS)
+    with pytest.raises(ValueError):   # promoted experts need the residual codebook
+        paged_runtime.PagedMoEExpert(1, st, torch.zeros(65536, 8, dtype=torch.float16), capacity=3, device="cpu")
+    st.close()
