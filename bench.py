@@ -317,8 +317,9 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
     """Decode step of a 40-layer stack of MoE blocks (256 routed experts + 1 shared, top-8,
     SwiGLU 2048->512->2048 at 2 bpw, all resident): router kernel + expert FFN per layer on
     device logits. N = 1: MoEBlock in a CUDA graph. N > 1: expert parallel -- each rank holds
-    256/N experts of every layer (+ the shared expert on rank 0), replicated router, one NCCL
-    all_reduce of the fp32 partial per layer. Expert bytes per layer = (distinct experts + shared)
+    256/N experts of every layer (+ the shared expert on rank 0), replicated router, the rank sum
+    done by the combine kernel over NVLink peer memory (NCCL all_reduce when symmetric memory is
+    unavailable). Expert bytes per layer = (distinct experts + shared)
     x 792,576 B, all ranks together."""
     from compressai_b200 import ep, moe, synth, vq
     L, E = args.moe_layers, 256
@@ -330,6 +331,12 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
     n_local = (hi - lo) + (1 if rank == 0 else 0)
     r_in, r_mid = vq.get_rot("moe_expert_2048", HIDDEN, dev), vq.get_rot("moe_expert_512", 512, dev)
     blocks, logits = [], []
+    peer_ctx = None
+    if world > 1:  # one symmetric buffer for the rank sums of all layers (see ep.py)
+        try:
+            peer_ctx = ep.PeerReduceContext(None, dev, max_tokens=T, hidden=HIDDEN)
+        except Exception:
+            peer_ctx = None
     for _ in range(L):
         pool = moe.ExpertRecordPool(n_local if world > 1 else E + 1, dev)
         w16 = pool.raw.view(torch.int16)
@@ -338,7 +345,9 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
         pool.dn_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.dn_scale.shape, generator=g, device=dev)))
         gate = 0.02 * torch.randn(HIDDEN, generator=gl, device=dev)
         if world > 1:
-            blocks.append(ep.ExpertParallelMoEBlock(pool, cb, E, r_in, r_mid, shared_gate=gate))
+            blocks.append(ep.ExpertParallelMoEBlock(pool, cb, E, r_in, r_mid, shared_gate=gate,
+                                                    reduce="peer" if peer_ctx is not None else "nccl",
+                                                    peer_ctx=peer_ctx, max_tokens=T))
         else:
             blocks.append(moe.MoEBlock(moe.PackedMoEExpertUniversal(pool, cb, dev, shared=True), shared_gate=gate))
         logits.append(torch.randn(T, E, generator=gl, device=dev))
@@ -394,6 +403,11 @@ def run_moe(args, dev, dist, world, T, steps, warmup):
            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world, "unit": "GB/s",
                         "frac": round(ach / (peak * world), 4)},
            "launches_per_step": 4 * L, "graph": graphed, "finite": bool(torch.isfinite(out.float()).all())}
+    if world > 1:
+        res["rank_sum"] = ("combine kernel over NVLink peer memory" if blocks[0].reduce_kind == "peer"
+                           else "NCCL all_reduce")
+        if peer_ctx is not None:
+            peer_ctx.check()
     del gr, blocks
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

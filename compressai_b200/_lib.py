@@ -52,6 +52,9 @@ SIGNATURES = {
     "vq2_rans_decode_segments": [_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p],
     "vq2_moe_expert_ffn_res": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _p,
                                _i64, _f32, _p, _p, _i64, _f32, _p, _p, _i64, _p, _i32, _p],
+    "vq2_moe_peer_buffer_bytes": [_i64, _i64, _i64],
+    "vq2_moe_expert_ffn_ep": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
+                              _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _p, _i32, _p],
     "vq2_lru_state_ints": [_i64, _i64],
     "vq2_lru_step": [_p, _p, _i64, _p, _p, _p],
     "vq2_fetch_records": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _p],
@@ -95,7 +98,7 @@ def load():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
             fn.restype = (ctypes.c_char_p if name == "vq2_status_string" else
-                          ctypes.c_int64 if name.endswith(("_workspace", "_bound", "_ints")) else ctypes.c_int)
+                          ctypes.c_int64 if name.endswith(("_workspace", "_bound", "_ints", "_bytes")) else ctypes.c_int)
         if lib.vq2_abi_version() != ABI_VERSION:
             raise VQ2Error(f"ABI version mismatch: library {lib.vq2_abi_version()}, python {ABI_VERSION}")
         _lib = lib

@@ -82,6 +82,19 @@ struct IdsByValue {
 int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
                 int32_t* out_count, cudaStream_t st, const int32_t* host_ids = nullptr, int32_t* ids_copy = nullptr);
 
+// Cross-GPU reduction of the expert-parallel combine over peer memory (moe_ep.cu).
+constexpr int kPeerMaxBlocks = 128;  // CTAs (output ranges) of the peer combine, at most
+struct PeerReduce {
+  uint8_t* const* peers;  // device array [world] of the symmetric buffers' base addresses
+  int rank, world;
+  int64_t part_off;       // bytes: flags region (world x kPeerMaxBlocks uint32) padded
+  int64_t part_bytes;     // bytes of one (parity, rank) slot (>= T x H fp32)
+  int32_t* epochs;        // local device state {sequence number, finished CTAs}, zero at first use
+  int32_t* err;           // optional status word (timeouts)
+};
+int run_combine_peer(const float* y, const float* w, int64_t T, int top_k, int64_t H, const int32_t* ids,
+                     int64_t num_experts, const PeerReduce& pr, void* out, int out_dtype, cudaStream_t st);
+
 // Routed-expert FFN of one MoE layer (moe_ffn.cu): compaction, gate_up GEMV (input RHT),
 // down GEMV (SwiGLU + RHT), combine; `ws` holds moe_ffn_workspace(T * top_k, ...) bytes.
 int64_t moe_ffn_workspace(int64_t P, int64_t gu_rows, int64_t dn_rows);
@@ -91,7 +104,7 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
                    float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host = false,
                    bool counters_zeroed = false, int32_t* err = nullptr, bool prefer_fused = false,
-                   const void* cb1 = nullptr, const float* add = nullptr);
+                   const void* cb1 = nullptr, const float* add = nullptr, const PeerReduce* peer = nullptr);
 
 // Fused single-launch expert FFN for T * top_k <= 64 (moe_fused.cu).
 struct MoeFusedArgs {

@@ -48,7 +48,8 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
                    int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
                    float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host,
-                   bool counters_zeroed, int32_t* err, bool prefer_fused, const void* cb1, const float* add) {
+                   bool counters_zeroed, int32_t* err, bool prefer_fused, const void* cb1, const float* add,
+                   const PeerReduce* peer) {
   if (!h || !ids || !w || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid || !ws || !out)
     return VQ2_ERR_ARG;
   if (T <= 0 || top_k <= 0 || top_k > 64 || num_experts <= 0) return VQ2_ERR_SHAPE;
@@ -78,7 +79,7 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   // the host): one fused launch (moe_fused.cu) instead of four. Inside a CUDA graph the four
   // kernels are faster on the GPU (40 vs 47 us per 35B layer at T = 1, top-8), so the generic
   // entry points keep them.
-  if (prefer_fused && !res && !add && P <= kIdsByValue && moe_fused_enabled()) {
+  if (prefer_fused && !res && !add && !peer && P <= kIdsByValue && moe_fused_enabled()) {
     MoeFusedArgs f{};
     f.h = h; f.h_dtype = h_dtype; f.T = (int)T; f.K = (int)top_k; f.P = (int)P;
     f.ids = ids_on_host ? nullptr : ids;
@@ -130,6 +131,10 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   b.y = yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
   s = run_gemv(b, dn_rows * P, res, val_dtype, st);
   if (s != VQ2_OK) return s;
+  if (peer) {  // expert parallel: combine + sum over ranks in one kernel over peer memory
+    if (add) return VQ2_ERR_ARG;
+    return run_combine_peer(yd, w, T, (int)top_k, H, ids, num_experts, *peer, out, out_dtype, st);
+  }
   return run_combine(yd, w, T, (int)top_k, H, add, out, out_dtype, st, ids, num_experts);
 }
 

@@ -10,15 +10,52 @@ Per layer and batch of T tokens:
 2. local problems: id - r*E/N where the expert is local, -1 (zero contribution) elsewhere;
    the shared expert (when present) is one more problem on rank 0 only;
 3. expert FFN over the local problems into an fp32 partial [T, H] (vq2_moe_expert_ffn);
-4. one all_reduce(SUM) of the partial over the group; every rank ends with the full output.
+4. the sum over ranks. Default (``reduce="peer"``): the combine kernel itself sums the ranks'
+   partials over NVLink peer memory (vq2_moe_expert_ffn_ep: each CTA publishes its column slice
+   of the partial into a symmetric buffer, signals the peers, waits for theirs and adds all
+   slices in rank order) -- one kernel instead of combine + NCCL all_reduce + cast, graph
+   capturable, identical output on every rank. ``reduce="nccl"``: fp32 partial then one NCCL
+   all_reduce(SUM) (the baseline, also used when symmetric memory is unavailable).
 
-At T = 1 the whole exchange is one all_reduce of 8 KB per layer (the hidden state is already
-replicated, so no dispatch collective is needed); the reference has no multi-GPU path at all.
+At T = 1 the whole exchange is 8 KB per rank per layer (the hidden state is already replicated,
+so no dispatch collective is needed); the reference has no multi-GPU path at all.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from . import moe
+from . import _lib, moe
+
+
+class PeerReduceContext:
+    """Symmetric buffer (torch symmetric memory, peer-mapped on every rank of ``group``) plus the
+    local epochs and status word of vq2_moe_expert_ffn_ep; one per (group, device), shared by
+    all layers (their calls are ordered on one stream)."""
+
+    def __init__(self, group, device, max_tokens, hidden):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_tokens, self.hidden = max_tokens, hidden
+        lib = _lib.load()
+        nbytes = lib.vq2_moe_peer_buffer_bytes(max_tokens, hidden, self.world)
+        if nbytes < 0:
+            raise ValueError("bad peer buffer size")
+        name = group.group_name if group is not None else dist.group.WORLD.group_name
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, name)
+        self.peers_dev = self.handle.buffer_ptrs_dev
+        self.epochs = torch.zeros(2, dtype=torch.int32, device=device)   # sequence number, finished CTAs
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every rank's flags are zero before any rank writes into them
+
+    def check(self):
+        """Raise if a wait for a peer gave up."""
+        if int(self.err.item()):
+            raise RuntimeError(f"peer reduction timed out (status {int(self.err.item()):#x})")
 
 
 def partition(num_experts, world, rank):
@@ -48,7 +85,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     it is a parameter so the host logic can be exercised on CPU ranks with a stand-in."""
 
     def __init__(self, pool, cb16, num_experts, rot_in, rot_mid, group=None, shared_gate=None, top_k=8,
-                 ffn=None, router=None):
+                 ffn=None, router=None, reduce="peer", peer_ctx=None, max_tokens=64):
         super().__init__()
         self.group = group
         self.world = dist.get_world_size(group)
@@ -61,6 +98,13 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self.shared_row = (self.hi - self.lo) if (shared_gate is not None and self.rank == 0) else None
         self.ffn = ffn or self._cuda_ffn
         self.router = router or moe.route
+        self.peer = None
+        if reduce == "peer" and ffn is None and self.world > 1 and pool.raw.is_cuda:
+            try:
+                self.peer = peer_ctx or PeerReduceContext(group, pool.raw.device, max_tokens, pool.dims[1] * 8)
+            except Exception as exc:  # no symmetric memory on this system: NCCL all_reduce
+                self.peer_error = repr(exc)
+        self.reduce_kind = "peer" if self.peer is not None else "nccl"
 
     def _cuda_ffn(self, h, ids, w, k):
         return moe.expert_ffn(h, ids.reshape(-1), w, self.pool, self.cb16, self.rot_in, self.rot_mid, k,
@@ -73,6 +117,25 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         else:
             (ids, w), sw = self.router(router_logits, self.top_k), None
         loc, lw = local_problems(ids, w, self.lo, self.hi, self.shared_row, sw)
+        if self.peer is not None and T <= self.peer.max_tokens:
+            return self._peer_ffn(hidden_states.reshape(T, -1).contiguous(), loc, lw, loc.shape[1])
         part = self.ffn(hidden_states.reshape(T, -1), loc, lw, loc.shape[1])
         dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
         return part.to(hidden_states.dtype)
+
+    def _peer_ffn(self, h, loc, lw, k):
+        T = h.shape[0]
+        gr, gc, dr, dc = self.pool.dims
+        lib = _lib.load()
+        ws_bytes = lib.vq2_moe_expert_ffn_workspace(T, k, gr, dr)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=h.device)
+        out = torch.empty(T, gc * 8, dtype=h.dtype, device=h.device)
+        pc = self.peer
+        ri, rm = self.rot_in, self.rot_mid
+        _lib.call("vq2_moe_expert_ffn_ep", _lib.ptr(h), _lib.dtype_code(h), T, k, _lib.ptr(loc), _lib.ptr(lw),
+                  _lib.ptr(self.pool.raw), self.pool.E, gr, gc, dr, dc, _lib.ptr(self.cb16), _lib.dtype_code(self.cb16),
+                  _lib.ptr(ri.perm), _lib.ptr(ri.sign), ri.hb, float(ri.scale), _lib.ptr(rm.perm), _lib.ptr(rm.sign),
+                  rm.hb, float(rm.scale), _lib.ptr(ws), ws_bytes, ctypes.c_void_p(pc.peers_dev), pc.rank, pc.world,
+                  pc.max_tokens, _lib.ptr(pc.epochs), _lib.ptr(pc.err), _lib.ptr(out), _lib.dtype_code(out),
+                  _lib.stream_ptr(h.device))
+        return out

@@ -226,6 +226,28 @@ VQ2_API int vq2_moe_expert_ffn_res(const void* h, int h_dtype, int64_t T, int64_
                                    float scale_mid, const float* add, void* workspace,
                                    int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
+/*
+ * Expert-parallel vq2_moe_expert_ffn whose combine also sums over the ranks of a group, in one
+ * kernel over NVLink peer memory (instead of combine -> NCCL all_reduce -> cast). ids: this
+ * rank's local pool rows (-1 for experts of other ranks). peers_dev: device array of `world`
+ * addresses of identical symmetric buffers (one per rank, peer-mapped, vq2_moe_peer_buffer_bytes
+ * bytes, zeroed before first use); epochs: local device uint32 [2] (sequence number, finished
+ * CTAs), zeroed before first use.
+ * Every rank must make the same sequence of calls (T <= max_tokens); a wait for a peer that
+ * gives up (about a second) raises *err (code 0x200). The output is identical on every rank.
+ */
+VQ2_API int64_t vq2_moe_peer_buffer_bytes(int64_t max_tokens, int64_t hidden, int64_t world);
+VQ2_API int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int64_t top_k,
+                                  const int32_t* ids, const float* w, const void* pool,
+                                  int64_t num_experts, int64_t gu_rows, int64_t gu_cols,
+                                  int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
+                                  const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in,
+                                  float scale_in, const int32_t* perm_mid, const int8_t* sign_mid,
+                                  int64_t hb_mid, float scale_mid, void* workspace,
+                                  int64_t workspace_bytes, void* const* peers_dev, int rank,
+                                  int world, int64_t max_tokens, uint32_t* epochs, int32_t* err,
+                                  void* out, int out_dtype, void* stream);
+
 /* Workspace bytes vq2_moe_expert_ffn needs for T tokens x top_k experts (-1 on bad sizes). */
 VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows,
                                              int64_t dn_rows);

@@ -1,5 +1,7 @@
-"""Expert parallelism on 2 GPUs (NCCL): the EP block's output equals a single-GPU MoE block
-holding all experts. Skipped with fewer than 2 GPUs."""
+"""Expert parallelism on 2 GPUs: the EP block's output (rank sum over NVLink peer memory inside the
+combine kernel, and the NCCL all_reduce baseline) equals a single-GPU MoE block holding all
+experts, identically on both ranks, also when the layer stack runs from a CUDA graph. Skipped
+with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -45,13 +47,41 @@ def _worker(rank, world, port, results):
             loc.raw[hi - lo].copy_(full.raw[E])
         gate = torch.from_numpy((0.05 * np.random.default_rng(1).standard_normal(2048)).astype(np.float32)).to(dev)
         r_in, r_mid = vq.get_rot("moe_expert_2048", 2048, dev), vq.get_rot("moe_expert_512", 512, dev)
-        blk = ep.ExpertParallelMoEBlock(loc, cb, E, r_in, r_mid, shared_gate=gate)
+        blk = ep.ExpertParallelMoEBlock(loc, cb, E, r_in, r_mid, shared_gate=gate)            # peer reduce
+        nccl = ep.ExpertParallelMoEBlock(loc, cb, E, r_in, r_mid, shared_gate=gate, reduce="nccl")
+        assert blk.reduce_kind == "peer", getattr(blk, "peer_error", "")
         ref_blk = moe.MoEBlock(moe.PackedMoEExpertUniversal(full, cb, dev, shared=True), shared_gate=gate)
-        h = torch.from_numpy(np.random.default_rng(2).standard_normal((T, 2048)).astype(np.float16)).to(dev)
-        lg = torch.from_numpy(np.random.default_rng(3).standard_normal((T, E)).astype(np.float32)).to(dev)
-        y = blk(h, lg).float().cpu().numpy()
-        ref = ref_blk(h, lg).float().cpu().numpy()
-        results[rank] = (float(np.abs(y - ref).max() / np.abs(ref).max()), y)
+        out = {}
+        for t_ in (T, 1):
+            h = torch.from_numpy(np.random.default_rng(2 + t_).standard_normal((t_, 2048)).astype(np.float16)).to(dev)
+            lg = torch.from_numpy(np.random.default_rng(3 + t_).standard_normal((t_, E)).astype(np.float32)).to(dev)
+            ref = ref_blk(h, lg).float().cpu().numpy()
+            y = blk(h, lg).float().cpu().numpy()
+            yn = nccl(h, lg).float().cpu().numpy()
+            out[t_] = (float(np.abs(y - ref).max() / np.abs(ref).max()),
+                       float(np.abs(yn - ref).max() / np.abs(ref).max()), y)
+        # several layers in one CUDA graph (no NCCL inside): replays equal the eager chain
+        h = torch.from_numpy(np.random.default_rng(9).standard_normal((1, 2048)).astype(np.float16)).to(dev)
+        lgs = [torch.from_numpy(np.random.default_rng(10 + i).standard_normal((1, E)).astype(np.float32)).to(dev)
+               for i in range(3)]
+        eager = h
+        for lg in lgs:
+            eager = blk(eager, lg)
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                x = h
+                for lg in lgs:
+                    x = blk(x, lg)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        graph_equal = bool(torch.equal(x, eager))
+        blk.peer.check()
+        del g
+        results[rank] = (out, graph_equal)
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
@@ -65,6 +95,9 @@ def test_expert_parallel_two_gpus_matches_single_gpu():
     results = mgr.dict()
     mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
-        err, _ = results[r]
-        assert err < 2e-3, (r, err)   # fp16 outputs of two fp32 sums in different orders
-    assert np.array_equal(results[0][1], results[1][1])
+        out, graph_equal = results[r]
+        for t_, (err_peer, err_nccl, _) in out.items():
+            assert err_peer < 2e-3 and err_nccl < 2e-3, (r, t_, err_peer, err_nccl)  # fp16 outputs
+        assert graph_equal, r
+    for t_ in results[0][0]:
+        assert np.array_equal(results[0][0][t_][2], results[1][0][t_][2])   # identical on both ranks
