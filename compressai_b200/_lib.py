@@ -35,6 +35,8 @@ SIGNATURES = {
     "vq2_gemv_multi": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _i64, _p, _p, _p, _p, _p, _p, _i32, _p,
                        _i32, _i64, _i64, _f32, _p, _i64, _p],
     "vq2_gemv_workspace": [_i64, _i64],
+    "vq2_gemv_argmax": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _p, _p, _p, _p, _i32, _i64, _i64, _f32, _p,
+                        _i32, _i64, _p, _p],
     "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p, _i64, _p],
     "vq2_moe_gemv": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i32,
                      _p, _i32, _i64, _i64, _f32, _p],

@@ -45,6 +45,8 @@ struct GemvArgs {
   const void* cb1;        // [256, 8] val or null
   int y_dtype;
   int64_t y_row_stride;   // elements between output rows m
+  unsigned long long* argmax;  // greedy argmax per activation row m (multi mode, CUDA cores), or null
+  bool no_y;                   // argmax only: outputs are not written
   int out;                // rows (expert-indexed mode)
   int n;
   float rs;

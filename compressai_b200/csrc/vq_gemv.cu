@@ -29,6 +29,15 @@
 
 namespace vq2 {
 
+// Order-preserving 64-bit key of (value, row) for a greedy argmax by atomicMax: the float's bits
+// flipped so that unsigned order is numeric order, then the row complemented so that ties go to
+// the smaller row (torch.argmax's choice). NaN-free inputs assumed; 0 means "none".
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(row));
+}
+
 template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
 __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   static_assert(!XREG || (LPR == 32 && MT == 1), "register activations need one 256-group chunk, M tile 1");
@@ -223,6 +232,11 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
         for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
           for (int off = LPR / 2; off > 0; off >>= 1) acc[rw][mi] += __shfl_xor_sync(0xffffffffu, acc[rw][mi], off);
+      // greedy argmax (one matrix): per activation row, the warp's best (value, row) key, one atomic
+      // per warp
+      unsigned long long best[MT];
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) best[mi] = 0ull;
       if (li == 0) {
         const TV* sc = multi ? static_cast<const TV*>(a.p_scale[cur.k])
                              : static_cast<const TV*>(a.scale) + cur.e * a.scale_e_stride;
@@ -238,12 +252,29 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
               if (mi < mcount) {
                 const int64_t o = yk + (int64_t)(m0 + mi) * a.y_row_stride + r;
                 const float v = acc[rw][mi] * s;
+                if (a.argmax) {  // global row of the concatenated outputs: problem offset + r
+                  const unsigned long long key = argmax_key(v, r);
+                  best[mi] = key > best[mi] ? key : best[mi];
+                }
+                if (a.no_y) continue;
                 if (a.y_dtype == VQ2_F16) static_cast<__half*>(ybase)[o] = __float2half_rn(v);
                 else if (a.y_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(ybase)[o] = __float2bfloat16_rn(v);
                 else static_cast<float*>(ybase)[o] = v;
               }
             }
           }
+        }
+      }
+      if (a.argmax) {
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+          unsigned long long b = best[mi];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long q = __shfl_xor_sync(0xffffffffu, b, off);
+            b = q > b ? q : b;
+          }
+          if (lane == 0 && mi < mcount && b) atomicMax(a.argmax + m0 + mi, b);
         }
       }
     }
@@ -376,7 +407,7 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
   // Tensor cores from 8 activation rows, or from 2 when the matrices are tall enough to fill
   // the GPU with 128-row items (measured: lm_head at M = 4 is faster there than on CUDA cores).
   const bool tc = a.M >= kTcMinRows || (a.M >= 2 && total_rows >= kTcTallRows);
-  if (tc && a.nprob > 0 && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
+  if (tc && a.nprob > 0 && !a.argmax && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
     const int r = run_gemm_tc(a, res, val_dtype, ws, st);  // batched: decode into tensor-core MMAs
     if (r != -1) return r;
   }
@@ -481,4 +512,29 @@ extern "C" int vq2_moe_gemv(const void* x, int x_dtype, int x_mode, int64_t x_k_
   a.scale_e_stride = scale_e_stride;
   a.out = (int)out; a.n = (int)(ng * 8); a.rs = rs; a.K = (int)K;
   return run_gemv(a, out * K, false, val_dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vq2_gemv_argmax(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,
+                               const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
+                               const int16_t* idx0, const uint8_t* idx1, const void* cb0, const void* cb1,
+                               const void* scale, int val_dtype, int64_t out, int64_t n, float rs, void* y,
+                               int y_dtype, int64_t y_row_stride, unsigned long long* best, void* stream) {
+  using namespace vq2;
+  if (!x || !idx0 || !scale || !cb0 || !best) return VQ2_ERR_ARG;
+  if (!dtype_ok(x_dtype) || (y && !dtype_ok(y_dtype))) return VQ2_ERR_DTYPE;
+  if (M <= 0 || M > 64 || n <= 0 || n % 64 != 0 || out <= 0 || out > INT32_MAX) return VQ2_ERR_SHAPE;
+  if (x_row_stride < (x_mode == VQ2_ACT_SWIGLU_RHT ? 2 * n : n) || (y && M > 1 && y_row_stride < out))
+    return VQ2_ERR_SHAPE;
+  if (!aligned(cb0, 16) || !aligned(idx0, 16) || (idx1 && !aligned(idx1, 8)) || (cb1 && !aligned(cb1, 16)))
+    return VQ2_ERR_ALIGN;
+  if ((idx1 != nullptr) != (cb1 != nullptr)) return VQ2_ERR_ARG;
+  GemvArgs a{};
+  a.nprob = 1;
+  a.p_idx0[0] = idx0; a.p_idx1[0] = idx1; a.p_scale[0] = scale; a.p_y[0] = y; a.p_out[0] = (int)out;
+  a.x = x; a.x_dtype = x_dtype; a.x_mode = x_mode; a.x_row_stride = x_row_stride; a.x_k_stride = 0; a.x_k_div = 1;
+  a.perm = perm; a.sign = sign; a.hb = (int)hb; a.rot_scale = rot_scale;
+  a.M = (int)M; a.cb0 = cb0; a.cb1 = cb1; a.y_dtype = y ? y_dtype : VQ2_F32; a.y_row_stride = y_row_stride;
+  a.n = (int)n; a.rs = rs; a.K = 1; a.out = (int)out;
+  a.argmax = best; a.no_y = (y == nullptr);
+  return run_gemv(a, out, idx1 != nullptr, val_dtype, static_cast<cudaStream_t>(stream), nullptr, 0);
 }

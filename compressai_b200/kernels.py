@@ -104,6 +104,34 @@ def _ids32(ids):
     return ids.contiguous()
 
 
+def gemv_argmax(x, mat, cb0, cb1=None, rot=None, mode=None, rs=1.0, y=None):
+    """Greedy argmax over the rows of one VQ matrix, fused into its GEMV (vq2_gemv_argmax):
+    returns int64 [M] row indices (ties to the smaller row); with ``y`` (a [M, out] tensor) the
+    logits are written too. M <= 64."""
+    i0, i1, sc = mat
+    _lib.require_cuda(x, i0, i1, sc, cb0, cb1)
+    if mode is None:
+        mode = _lib.VQ2_ACT_RHT if rot is not None else _lib.VQ2_ACT_ROTATED
+    out, ng = i0.shape
+    n = ng * 8
+    xin = 2 * n if mode == _lib.VQ2_ACT_SWIGLU_RHT else n
+    x2 = x.reshape(-1, xin).contiguous()
+    M = x2.shape[0]
+    _check_vals(cb0, cb1 if i1 is not None else None, sc)
+    i0, i1, sc = _c(i0), _c(i1), _c(sc)   # held for the call: a temporary's memory could be reused
+    best = torch.zeros(M, dtype=torch.int64, device=x.device)
+    if y is not None and (y.shape[-1] != out or not y.is_contiguous()):
+        raise ValueError("y must be contiguous [M, out]")
+    _lib.call("vq2_gemv_argmax", _lib.ptr(x2), _lib.dtype_code(x2), int(mode), M, x2.stride(0),
+              _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
+              int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0,
+              _lib.ptr(i0), _lib.ptr(i1) if i1 is not None else None, _lib.ptr(cb0),
+              _lib.ptr(cb1) if i1 is not None else None, _lib.ptr(sc), _lib.dtype_code(cb0), out, n,
+              float(rs), _lib.ptr(y) if y is not None else None, _lib.dtype_code(y) if y is not None else 0, out,
+              _lib.ptr(best), _lib.stream_ptr(x.device))
+    return 0xFFFFFFFF - (best & 0xFFFFFFFF)
+
+
 def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=None, ys=None, y_row_stride=None):
     """P <= 8 VQ matrices sharing one activation in ONE launch.
 

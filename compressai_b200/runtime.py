@@ -119,6 +119,12 @@ class PackedLinear(nn.Module):
         out_dtype = x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float16
         return kernels.gemv_multi(x, [self.mat()], cb0, cb1, rot=self.rot, out_dtype=out_dtype)[0]
 
+    def greedy(self, x, logits=None):
+        """argmax over this layer's outputs for each row of x, fused into the GEMV (no logits
+        round trip unless ``logits`` [M, out] is given to be filled): int64 [M]."""
+        cb0, cb1 = self.codebooks()
+        return kernels.gemv_argmax(x, self.mat(), cb0, cb1, rot=self.rot, y=logits)
+
     def nbytes(self):
         return sum(b.numel() * b.element_size() for b in self.buffers())
 
@@ -205,6 +211,11 @@ class PackedLMHead(nn.Module):
 
     def forward(self, x):
         return self.lin(x)
+
+    def greedy(self, x, logits=None):
+        """Next-token ids (greedy) from hidden states x [M, H]: the VQ GEMV with the argmax in
+        its epilogue (vq2_gemv_argmax)."""
+        return self.lin.greedy(x, logits)
 
 
 # --------------------------------------------------------------------------------------------

@@ -130,6 +130,23 @@ VQ2_API int vq2_gemv(const void* xr, int x_dtype, int64_t M, int64_t x_row_strid
                      void* stream);
 
 /*
+ * Greedy argmax fused into the VQ GEMV of one matrix (the lm_head): as vq2_gemv_multi with P = 1
+ * (any x_mode), and best[m] = max over rows r of key(y[m, r], r), an order-preserving 64-bit key
+ * (high 32 bits: the fp32 value's bits, flipped so unsigned order is numeric order; low 32 bits:
+ * 0xffffffff - r, so ties go to the smaller row, as torch.argmax). best: device uint64 [M], zeroed
+ * by the caller before the call (the kernel only raises it); the token of row m is
+ * 0xffffffff - (best[m] & 0xffffffff). y may be NULL (argmax only; no logits written). M <= 64,
+ * CUDA-core path. Replaces: the lm_head GEMV + torch argmax of the decode loop (LEGION greedy
+ * decoding, legion/engine.py:288-303), with no [M, vocab] logits round trip when y is NULL.
+ */
+VQ2_API int vq2_gemv_argmax(const void* x, int x_dtype, int x_mode, int64_t M, int64_t x_row_stride,
+                            const int32_t* perm, const int8_t* sign, int64_t hb, float rot_scale,
+                            const int16_t* idx0, const uint8_t* idx1, const void* cb0,
+                            const void* cb1, const void* scale, int val_dtype, int64_t out,
+                            int64_t n, float rs, void* y, int y_dtype, int64_t y_row_stride,
+                            unsigned long long* best, void* stream);
+
+/*
  * Expert-indexed VQ GEMV over K problems (2 bpw):
  *   xr_k = act(x + (k / x_k_div) * x_k_stride)        (per x_mode, as in vq2_gemv_multi)
  *   y[k, r] = rs * scale[e_k, r] * sum_g dot(cb0[idx[e_k, r, g]], xr_k[8g:8g+8]),  e_k = e_ids[k]

@@ -360,3 +360,36 @@ def test_tensor_core_path_without_workspace_falls_back_exactly(cbs):
               _lib.ptr(sc), _lib.VQ2_F16, _lib.ptr(y_cc), _lib.VQ2_F32, 256, 256, 2048, 1.0, None, 0,
               _lib.stream_ptr(DEV))
     assert rel_err(y_cc.cpu().numpy(), y_tc.cpu().numpy()) < 3e-5
+
+
+@pytest.mark.parametrize("M,bits,ties", [(1, (16,), False), (3, (16, 8), False), (2, (16,), True)])
+def test_lm_head_fused_greedy_argmax(cbs, M, bits, ties):
+    """vq2_gemv_argmax: the argmax of each activation row equals torch.argmax of the GEMV's own
+    logits (ties to the smaller row), with and without the logits written."""
+    from compressai_b200 import runtime
+    out, n = 20000, 2048
+    idx, scale = synth.random_matrix(M + 50, out, n, bits)
+    if ties:   # three identical rows with a large scale: equal maximal logits at 123, 7000, 19999
+        idx = [a.copy() for a in idx]
+        for a in idx:
+            a[7000] = a[123]
+            a[19999] = a[123]
+        scale = scale.copy()
+        scale[[123, 7000, 19999]] = 100.0
+    cbd = dev_cbs(cbs)
+    lin = runtime.PackedLinear((out, n), bits, "lm_head_t", [torch.from_numpy(a) for a in idx],
+                               torch.from_numpy(scale), cbd, DEV)
+    x = torch.randn(M, n, device=DEV).half()
+    logits = lin(x).float()
+    if ties:   # make row 123's logit positive for every activation row, so its twins tie at the max
+        x = torch.where((logits[:, 123] < 0)[:, None], -x, x)
+        logits = lin(x).float()
+    got = lin.greedy(x)
+    y = torch.empty(M, out, device=DEV, dtype=torch.float32)
+    got2 = lin.greedy(x, logits=y)
+    # the fused kernel's own fp32 logits decide; lin(x) may run on tensor cores (another sum order)
+    assert torch.equal(got, torch.argmax(y, dim=-1)) and torch.equal(got2, got)
+    assert (y - logits).abs().max() <= 1e-3 * logits.abs().max()
+    assert torch.equal(got, torch.argmax(logits, dim=-1))
+    if ties:
+        assert (got == 123).all()
