@@ -57,16 +57,181 @@ __device__ __forceinline__ void fwht8(float v[8]) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
+// Shared-memory ("fast") staging, used by the GEMV kernels: the rotation table is loaded into
+// shared memory before the dependency wait (it is constant), the activation rows are read after
+// it with independent coalesced loads (one memory round trip) into `raw`, and the permuted reads
+// of the transform come from shared memory. When the transform is one pass (MT * n <= 2048:
+// every raw value is read before the pass writes the tile) `raw` aliases the tile; otherwise it
+// is a separate [MT][n] buffer. The old form (every permuted element read from global memory)
+// remains for the shapes whose buffers do not fit and for the fused MoE kernel.
+constexpr int kFastStageFloats = 12288;
+// Dynamic shared memory of a GEMV CTA at most (the kernels' MaxDynamicSharedMemorySize): an
+// activation tile of up to 80 KB, the transform scratch and the residual codebook.
+constexpr int kGemvSmemCap = 80 * 1024 + kScratchFloats * 4 + 4096;
+__host__ __device__ constexpr bool stage_in_place(int mt, int n) { return mt * n <= 2048; }
+__host__ __device__ constexpr int fast_extra_floats(int mt, int n) {
+  return (stage_in_place(mt, n) ? 0 : mt * n) + (n + 1) / 2;  // raw rows (unless in place) + table
+}
+__host__ __device__ constexpr bool fast_stage(int mt, int n) {
+  return n <= 32768 && (stage_in_place(mt, n) || (mt + 1) * n <= kFastStageFloats) &&
+         (mt * xs_len(n) + kScratchFloats + 1024 + fast_extra_floats(mt, n)) * 4 <= kGemvSmemCap;
+}
+// Extra shared-memory floats of fast staging in mode `mode` (ROTATED needs none: it copies
+// straight into the tile; the table has 16-bit entries).
+__host__ __device__ constexpr int fast_stage_floats(int mt, int n, int mode) {
+  return mode != VQ2_ACT_ROTATED && fast_stage(mt, n) ? fast_extra_floats(mt, n) : 0;
+}
+
+// Rotation table for fast staging: perm (< 2^15) with the sign in bit 15. All threads of the CTA
+// call it; a barrier must follow before the table is read.
+__device__ __forceinline__ void stage_perm(const ActSrc& a, uint16_t* ps) {
+  if (a.x_mode == VQ2_ACT_ROTATED) return;
+  const int n = a.n, nt = blockDim.x;
+  if ((reinterpret_cast<uintptr_t>(a.perm) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.sign) & 3) == 0 &&
+      n <= 8 * 4 * nt) {  // all loads issued before any store: one round trip
+    const int4* p4 = reinterpret_cast<const int4*>(a.perm);
+    const uint32_t* s4 = reinterpret_cast<const uint32_t*>(a.sign);
+    int4 pv[8];
+    uint32_t sv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int v = k * nt + threadIdx.x;
+      if (4 * v < n) {
+        pv[k] = p4[v];
+        sv[k] = s4[v];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int v = k * nt + threadIdx.x;
+      if (4 * v < n) {
+        const int4 q = pv[k];
+        const uint32_t sg = sv[k];  // four int8 signs; bit 7 of a byte is set when negative
+        const uint32_t lo = (q.x | (sg & 0x80u) << 8) | (q.y | (sg & 0x8000u)) << 16;
+        const uint32_t hi = (q.z | (sg & 0x800000u) >> 8) | (q.w | (sg & 0x80000000u) >> 16) << 16;
+        *reinterpret_cast<uint2*>(ps + 4 * v) = make_uint2(lo, hi);
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < n; i += nt) ps[i] = static_cast<uint16_t>(a.perm[i] | (a.sign[i] < 0 ? 0x8000 : 0));
+}
+
+constexpr int kLoadsInFlight = 2;  // 16-byte loads per thread per round (x2 for SwiGLU rows)
+
+__device__ __forceinline__ int stage_pos(int j, bool padded) { return padded ? xs_pos(j >> 3, j & 7) : j; }
+
+// Coalesced loads of `cnt` consecutive activations from element `off` of x into dst (padded
+// tile positions or linear): value x[off + j], or silu(x[off + j]) * x[off + n + j] for SwiGLU
+// rows (fp32 [gate | up]). All loads of a round are issued before its stores.
+__device__ __forceinline__ void load_row(const ActSrc& a, int64_t off, int cnt, bool swiglu, float* dst,
+                                         bool padded) {
+  const int nt = blockDim.x;
+  const bool f32 = swiglu || a.x_dtype == VQ2_F32;
+  const uintptr_t addr = f32 ? reinterpret_cast<uintptr_t>(static_cast<const float*>(a.x) + off)
+                             : reinterpret_cast<uintptr_t>(static_cast<const __half*>(a.x) + off);
+  const bool vec = (addr & 15) == 0 && (!swiglu || (a.n & 3) == 0);
+  if (vec && f32) {
+    const float4* g = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + off);
+    const int nv = cnt >> 2;
+    for (int v0 = 0; v0 < nv; v0 += nt * kLoadsInFlight) {
+      float4 gv[kLoadsInFlight], uv[kLoadsInFlight];
+#pragma unroll
+      for (int k = 0; k < kLoadsInFlight; ++k) {
+        const int v = v0 + k * nt + threadIdx.x;
+        if (v < nv) {
+          gv[k] = g[v];
+          if (swiglu) uv[k] = g[v + (a.n >> 2)];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kLoadsInFlight; ++k) {
+        const int v = v0 + k * nt + threadIdx.x;
+        if (v < nv) {
+          float4 r = gv[k];
+          if (swiglu) {
+            r.x = silu_f(r.x) * uv[k].x; r.y = silu_f(r.y) * uv[k].y;
+            r.z = silu_f(r.z) * uv[k].z; r.w = silu_f(r.w) * uv[k].w;
+          }
+          *reinterpret_cast<float4*>(dst + stage_pos(4 * v, padded)) = r;
+        }
+      }
+    }
+    return;
+  }
+  if (vec) {  // 16-bit: 8 values per 16-byte load
+    const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + off);
+    const int nv = cnt >> 3;
+    for (int v0 = 0; v0 < nv; v0 += nt * kLoadsInFlight) {
+      uint4 w[kLoadsInFlight];
+#pragma unroll
+      for (int k = 0; k < kLoadsInFlight; ++k) {
+        const int v = v0 + k * nt + threadIdx.x;
+        if (v < nv) w[k] = g[v];
+      }
+#pragma unroll
+      for (int k = 0; k < kLoadsInFlight; ++k) {
+        const int v = v0 + k * nt + threadIdx.x;
+        if (v < nv) {
+          float f[8];
+          if (a.x_dtype == VQ2_F16) decode8<__half>(w[k], f);
+          else decode8<__nv_bfloat16>(w[k], f);
+          float* d = dst + stage_pos(8 * v, padded);
+          *reinterpret_cast<float4*>(d) = make_float4(f[0], f[1], f[2], f[3]);
+          *reinterpret_cast<float4*>(d + 4) = make_float4(f[4], f[5], f[6], f[7]);
+        }
+      }
+    }
+    return;
+  }
+  for (int j0 = 0; j0 < cnt; j0 += nt * 8) {  // unaligned rows: scalar loads, 8 in flight
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + k * nt + threadIdx.x;
+      v[k] = 0.f;
+      if (j < cnt) {
+        if (swiglu) {
+          const float* g = static_cast<const float*>(a.x) + off;
+          v[k] = silu_f(g[j]) * g[a.n + j];
+        } else {
+          v[k] = load_act(a.x, a.x_dtype, off + j);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + k * nt + threadIdx.x;
+      if (j < cnt) dst[stage_pos(j, padded)] = v[k];
+    }
+  }
+}
+
 // Stage MT activation rows (starting at element offset xoff) into the padded fp32 tile xs.
 // Mode ROTATED copies; modes RHT / SWIGLU_RHT apply the forward randomized Hadamard transform
 // (perm gather, sign, blocked Sylvester Hadamard, rot_scale) with the whole CTA: a segment of
 // hb elements belongs to T = hb/8 threads (8 values each): 3 butterfly stages in registers,
 // one transpose through `scratch`, 3 more in registers, the rest with warp shuffles (the same
-// scheme as the standalone vq2_rht kernel). Must be called by all 256 threads.
+// scheme as the standalone vq2_rht kernel). With `raw` the rows are staged the fast way
+// (fast_stage above; `ps` is the table from stage_perm). Must be called by all 256 threads.
 template <int MT>
-__device__ void stage_activations(const ActSrc& a, int64_t xoff, int mcount, float* xs, int xl, float* scratch) {
+__device__ __forceinline__ void stage_activations(const ActSrc& a, int64_t xoff, int mcount, float* xs, int xl,
+                                                  float* scratch, float* raw = nullptr,
+                                                  const uint16_t* ps = nullptr) {
   const int n = a.n;
-  if (a.x_mode == VQ2_ACT_ROTATED) {
+  const bool swiglu = (a.x_mode == VQ2_ACT_SWIGLU_RHT), rotated = (a.x_mode == VQ2_ACT_ROTATED);
+  if (raw != nullptr) {
+#pragma unroll 1
+    for (int mi = 0; mi < MT; ++mi) {
+      if (mi < mcount) {
+        load_row(a, xoff + (int64_t)mi * a.x_row_stride, n, swiglu, rotated ? xs + mi * xl : raw + mi * n, rotated);
+      } else if (rotated) {  // the transform reads no rows past mcount
+        for (int j = threadIdx.x; j < n; j += blockDim.x) xs[mi * xl + stage_pos(j, true)] = 0.f;
+      }
+    }
+    if (rotated) return;
+    __syncthreads();
+  } else if (rotated) {
     for (int i = threadIdx.x; i < MT * n; i += blockDim.x) {
       const int mi = i / n, j = i - mi * n;
       const float v = mi < mcount ? load_act(a.x, a.x_dtype, xoff + (int64_t)mi * a.x_row_stride + j) : 0.f;
@@ -77,30 +242,38 @@ __device__ void stage_activations(const ActSrc& a, int64_t xoff, int mcount, flo
   const int hb = a.hb, T = hb >> 3, SEG = 256 / T, nb = n / hb;
   const int s = threadIdx.x / T, t = threadIdx.x % T;
   const int segs = MT * nb;
-  const bool swiglu = (a.x_mode == VQ2_ACT_SWIGLU_RHT);
   float* sc = scratch + s * (hb + (hb >> 5));
   for (int s0 = 0; s0 < segs; s0 += SEG) {
     const int gs = s0 + s;
     const int mi = gs / nb, b = gs - mi * nb;
     const bool active = gs < segs && mi < mcount;
     float v[8];
+    if (raw != nullptr) {  // uniform branch, outside the unrolled loads
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float val = 0.f;
-      if (active) {
-        const int j = b * hb + t + T * i;
-        const int64_t row = xoff + (int64_t)mi * a.x_row_stride;
-        const int p = a.perm[j];
-        if (swiglu) {  // plain loads: L1 lines are reused by the permuted reads of one row; rows
-                       // written by other CTAs of the same launch are read only after an acquire
-          const float* g = static_cast<const float*>(a.x) + row;
-          val = silu_f(g[p]) * g[n + p];
-        } else {
-          val = load_act(a.x, a.x_dtype, row + p);
-        }
-        val *= static_cast<float>(a.sign[j]);
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t q = ps[b * hb + t + T * i];
+        const float r = active ? raw[mi * n + (q & 0x7fffu)] : 0.f;
+        v[i] = (q & 0x8000u) ? -r : r;
       }
-      v[i] = val;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float val = 0.f;
+        if (active) {
+          const int j = b * hb + t + T * i;
+          const int64_t row = xoff + (int64_t)mi * a.x_row_stride;
+          const int p = a.perm[j];
+          if (swiglu) {  // plain loads: L1 lines are reused by the permuted reads of one row; rows
+                         // written by other CTAs of the same launch are read only after an acquire
+            const float* g = static_cast<const float*>(a.x) + row;
+            val = silu_f(g[p]) * g[n + p];
+          } else {
+            val = load_act(a.x, a.x_dtype, row + p);
+          }
+          val *= static_cast<float>(a.sign[j]);
+        }
+        v[i] = val;
+      }
     }
     fwht8(v);
 #pragma unroll
@@ -133,6 +306,5 @@ __device__ void stage_activations(const ActSrc& a, int64_t xoff, int mcount, flo
     __syncthreads();
   }
 }
-
 
 }  // namespace vq2

@@ -38,6 +38,19 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
   return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(row));
 }
 
+// Activation staging as a real call: it runs once per activation tile, and keeping its code out
+// of the main loop leaves that loop's register allocation (gathers in flight) to itself.
+template <int MT>
+__device__ __noinline__ void stage_tile(const ActSrc a, int64_t xoff, int mcount, float* xs, int xl, float* scratch,
+                                        float* raw, const uint16_t* ps) {
+  stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
+}
+
+// Variants that stage the fast way: all but the 3 bpw two-row register variant, whose
+// registers are taken by its two rows of residual indices.
+template <int RW, bool RES, bool XREG>
+constexpr bool variant_fast_stage() { return !(RES && XREG && RW == 2); }
+
 template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
 __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   static_assert(!XREG || (LPR == 32 && MT == 1), "register activations need one 256-group chunk, M tile 1");
@@ -49,6 +62,18 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   float* xs = smem;                                            // [MT][xl] activation tile
   float* scratch = smem + MT * xl;                             // RHT transpose scratch (2112 floats)
   uint4* cb1s = reinterpret_cast<uint4*>(scratch + kScratchFloats);  // [256] when RES
+  // Fast staging (gemv_dev.cuh): raw activation rows (or the tile itself) and the rotation
+  // table after the residual codebook; recomputed where used, so no registers stay tied up
+  // across the main loop.
+  auto fast_raw = [&]() -> float* {
+    if (!variant_fast_stage<RW, RES, XREG>() || !fast_stage(MT, a.n)) return nullptr;
+    if (a.x_mode == VQ2_ACT_ROTATED || stage_in_place(MT, a.n)) return smem;
+    return smem + MT * xs_len(a.n) + kScratchFloats + (RES ? 4 * 256 : 0);
+  };
+  auto fast_ps = [&]() -> uint16_t* {
+    return reinterpret_cast<uint16_t*>(smem + MT * xs_len(a.n) + kScratchFloats + (RES ? 4 * 256 : 0) +
+                                       (stage_in_place(MT, a.n) ? 0 : MT * a.n));
+  };
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane / LPR, li = lane % LPR;
@@ -98,14 +123,20 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     }
     return w;
   };
-  auto load_idx = [&](const Item& w, int c, uint4 (&iv)[RW], uint2 (&jv)[RW]) {
+  // Index vectors of chunk c of item w; with the last chunk, the rows' scales too (lane li == 0
+  // only), so the epilogue waits on no memory round trip of its own.
+  auto load_idx = [&](const Item& w, int c, uint4 (&iv)[RW], uint2 (&jv)[RW], float (&sv)[RW]) {
     const int g0 = (c * LPR + li) * 8;
+    const TV* sc = multi ? static_cast<const TV*>(a.p_scale[w.k])
+                         : static_cast<const TV*>(a.scale) + w.e * a.scale_e_stride;
 #pragma unroll
     for (int rw = 0; rw < RW; ++rw) {
       const int r = w.rb * RPC + warp * RPW + rw * RPL + sub;
+      sv[rw] = 0.f;
       if (w.valid && r < w.out) {
         iv[rw] = ld_stream_u4(w.i0 + (int64_t)r * ng + g0, pol_s);
         if (RES) jv[rw] = ld_stream_u2(w.i1 + (int64_t)r * ng + g0, pol_s);
+        if (li == 0 && c == chunks - 1) sv[rw] = to_f32<TV>(sc[r]) * a.rs;
       } else {
         iv[rw] = make_uint4(0, 0, 0, 0);
         if (RES) jv[rw] = make_uint2(0, 0);
@@ -121,11 +152,14 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   int chunk = 0;
   uint4 iv[RW];
   uint2 jv[RW];
+  float sv[RW];
   Item cur;
   if (weights_known && item < item_end) {  // constant weights: safe before the dependency wait
     cur = decode(item);
-    load_idx(cur, 0, iv, jv);
+    load_idx(cur, 0, iv, jv, sv);
   }
+  if (variant_fast_stage<RW, RES, XREG>() && fast_stage_floats(MT, n, a.x_mode) > 0)
+    stage_perm(act_src(a), fast_ps());  // constant too; the staging barrier follows
   pdl_wait();
   if (!multi && a.prob_count) {  // device-side problem count (compacted problem lists)
     const int kc = min(a.K, max(0, *a.prob_count));
@@ -136,7 +170,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   }
   if (!weights_known && item < item_end) {
     cur = decode(item);
-    load_idx(cur, 0, iv, jv);
+    load_idx(cur, 0, iv, jv, sv);
   }
   if (RES) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) cb1s[i] = static_cast<const uint4*>(a.cb1)[i];
@@ -153,7 +187,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     const int64_t xoff = (int64_t)m0 * a.x_row_stride + (multi ? 0 : (int64_t)(cur.o / a.x_k_div) * a.x_k_stride);
     if (xoff != cur_xoff) {  // uniform over the CTA
       __syncthreads();
-      stage_activations<MT>(act_src(a), xoff, mcount, xs, xl, scratch);
+      stage_tile<MT>(act_src(a), xoff, mcount, xs, xl, scratch, fast_raw(), fast_ps());
       __syncthreads();
       if constexpr (XREG) {  // this lane's 8 groups -> registers (conflict-free: lanes 68 floats apart)
 #pragma unroll
@@ -173,10 +207,11 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     if (nchunk == chunks) { nchunk = 0; nitem = item + 1; }
     uint4 nv[RW];
     uint2 njv[RW];
+    float nsv[RW] = {};
     Item nxt = cur;
     if (nitem < item_end) {
       if (nitem != item) nxt = decode(nitem);
-      load_idx(nxt, nchunk, nv, njv);
+      load_idx(nxt, nchunk, nv, njv, nsv);
     }
 
     if (chunk == 0) {
@@ -238,15 +273,13 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
 #pragma unroll
       for (int mi = 0; mi < MT; ++mi) best[mi] = 0ull;
       if (li == 0) {
-        const TV* sc = multi ? static_cast<const TV*>(a.p_scale[cur.k])
-                             : static_cast<const TV*>(a.scale) + cur.e * a.scale_e_stride;
         void* ybase = multi ? a.p_y[cur.k] : a.y;
         const int64_t yk = multi ? 0 : (int64_t)cur.o * a.y_k_stride;
 #pragma unroll
         for (int rw = 0; rw < RW; ++rw) {
           const int r = cur.rb * RPC + warp * RPW + rw * RPL + sub;
           if (r < cur.out) {
-            const float s = cur.valid ? to_f32<TV>(sc[r]) * a.rs : 0.f;
+            const float s = sv[rw];
 #pragma unroll
             for (int mi = 0; mi < MT; ++mi) {
               if (mi < mcount) {
@@ -285,6 +318,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     for (int rw = 0; rw < RW; ++rw) {
       iv[rw] = nv[rw];
       if (RES) jv[rw] = njv[rw];
+      sv[rw] = nsv[rw];
     }
   }
 }
@@ -312,7 +346,10 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
     a.row_blocks = (a.out + RPC - 1) / RPC;
     items = (int64_t)a.row_blocks * a.K * a.mtiles;
   }
-  const size_t smem = ((size_t)MT * xs_len(a.n) + kScratchFloats) * sizeof(float) + (RES ? 256 * sizeof(uint4) : 0);
+  const size_t smem = ((size_t)MT * xs_len(a.n) + kScratchFloats +
+                       (variant_fast_stage<RW, RES, XREG>() ? fast_stage_floats(MT, a.n, a.x_mode) : 0)) *
+                          sizeof(float) +
+                      (RES ? 256 * sizeof(uint4) : 0);
   auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV>;
   // Per-device one-time attributes: dynamic shared memory opt-in and, for the small-tile
   // variants, a small shared-memory carveout so most of the SM's 256 KB serves as L1.
@@ -323,7 +360,7 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (!(done.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kMaxXsBytes + kScratchFloats * 4 + 4096);
+                                         kGemvSmemCap);
     if (e == cudaSuccess && XREG) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 20);
     if (e != cudaSuccess) { set_last_cuda_error(e); return VQ2_ERR_LAUNCH; }
     int nb = 0;
