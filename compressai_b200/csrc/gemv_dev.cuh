@@ -62,19 +62,23 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g))
 // it with independent coalesced loads (one memory round trip) into `raw`, and the permuted reads
 // of the transform come from shared memory. When the transform is one pass (MT * n <= 2048:
 // every raw value is read before the pass writes the tile) `raw` aliases the tile; otherwise it
-// is a separate [MT][n] buffer. The old form (every permuted element read from global memory)
+// is a separate buffer of fast_raw_rows rows (all MT while MT + 1 rows fit kFastStageFloats,
+// else one row per round). The old form (every permuted element read from global memory)
 // remains for the shapes whose buffers do not fit and for the fused MoE kernel.
 constexpr int kFastStageFloats = 12288;
 // Dynamic shared memory of a GEMV CTA at most (the kernels' MaxDynamicSharedMemorySize): an
-// activation tile of up to 80 KB, the transform scratch and the residual codebook.
-constexpr int kGemvSmemCap = 80 * 1024 + kScratchFloats * 4 + 4096;
+// activation tile of up to 80 KB, the transform scratch, the residual codebook and the fast
+// staging buffers. Two CTAs of that size still share one SM.
+constexpr int kGemvSmemCap = 112 * 1024;
 __host__ __device__ constexpr bool stage_in_place(int mt, int n) { return mt * n <= 2048; }
+__host__ __device__ constexpr int fast_raw_rows(int mt, int n) {
+  return stage_in_place(mt, n) || (mt + 1) * n <= kFastStageFloats ? mt : 1;
+}
 __host__ __device__ constexpr int fast_extra_floats(int mt, int n) {
-  return (stage_in_place(mt, n) ? 0 : mt * n) + (n + 1) / 2;  // raw rows (unless in place) + table
+  return (stage_in_place(mt, n) ? 0 : fast_raw_rows(mt, n) * n) + (n + 1) / 2;  // raw rows + table
 }
 __host__ __device__ constexpr bool fast_stage(int mt, int n) {
-  return n <= 32768 && (stage_in_place(mt, n) || (mt + 1) * n <= kFastStageFloats) &&
-         (mt * xs_len(n) + kScratchFloats + 1024 + fast_extra_floats(mt, n)) * 4 <= kGemvSmemCap;
+  return n <= 32768 && (mt * xs_len(n) + kScratchFloats + 1024 + fast_extra_floats(mt, n)) * 4 <= kGemvSmemCap;
 }
 // Extra shared-memory floats of fast staging in mode `mode` (ROTATED needs none: it copies
 // straight into the tile; the table has 16-bit entries).
@@ -220,6 +224,15 @@ __device__ __forceinline__ void stage_activations(const ActSrc& a, int64_t xoff,
                                                   const uint16_t* ps = nullptr) {
   const int n = a.n;
   const bool swiglu = (a.x_mode == VQ2_ACT_SWIGLU_RHT), rotated = (a.x_mode == VQ2_ACT_ROTATED);
+  if constexpr (MT > 1) {  // one raw row per round: stage each row as its own one-row tile
+    if (raw != nullptr && !rotated && fast_raw_rows(MT, n) == 1) {
+#pragma unroll 1
+      for (int mi = 0; mi < MT; ++mi)
+        stage_activations<1>(a, xoff + (int64_t)mi * a.x_row_stride, mi < mcount ? 1 : 0, xs + mi * xl, xl,
+                             scratch, raw, ps);
+      return;
+    }
+  }
   if (raw != nullptr) {
 #pragma unroll 1
     for (int mi = 0; mi < MT; ++mi) {

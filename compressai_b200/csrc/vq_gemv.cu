@@ -38,12 +38,20 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
   return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(row));
 }
 
-// Activation staging as a real call: it runs once per activation tile, and keeping its code out
-// of the main loop leaves that loop's register allocation (gathers in flight) to itself.
+// Activation staging. For M tile 1 it is a real call: it runs once per activation tile, and
+// keeping its code out of the main loop leaves that loop's register allocation (gathers in
+// flight) to itself. Larger M tiles inline it (as a call, its callee-saved registers made the
+// permuted global loads of the old staging form spill and serialise).
 template <int MT>
-__device__ __noinline__ void stage_tile(const ActSrc a, int64_t xoff, int mcount, float* xs, int xl, float* scratch,
-                                        float* raw, const uint16_t* ps) {
+__device__ __noinline__ void stage_tile_call(const ActSrc a, int64_t xoff, int mcount, float* xs, int xl,
+                                             float* scratch, float* raw, const uint16_t* ps) {
   stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
+}
+template <int MT>
+__device__ __forceinline__ void stage_tile(const ActSrc& a, int64_t xoff, int mcount, float* xs, int xl,
+                                           float* scratch, float* raw, const uint16_t* ps) {
+  if constexpr (MT == 1) stage_tile_call<1>(a, xoff, mcount, xs, xl, scratch, raw, ps);
+  else stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
 }
 
 // Variants that stage the fast way: all but the 3 bpw two-row register variant, whose
@@ -72,7 +80,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   };
   auto fast_ps = [&]() -> uint16_t* {
     return reinterpret_cast<uint16_t*>(smem + MT * xs_len(a.n) + kScratchFloats + (RES ? 4 * 256 : 0) +
-                                       (stage_in_place(MT, a.n) ? 0 : MT * a.n));
+                                       (stage_in_place(MT, a.n) ? 0 : fast_raw_rows(MT, a.n) * a.n));
   };
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
