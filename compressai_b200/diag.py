@@ -2,8 +2,10 @@
 
   python -m compressai_b200.diag gather
       random codebook-row gather rates (global / shared / cluster-shared memory)
-  python -m compressai_b200.diag gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3
-      `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix
+  python -m compressai_b200.diag gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3 [--swiglu]
+      `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
+      with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
+      prologue (the MLP down projection)
   python -m compressai_b200.diag moe --T 1 --reps 3
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts
   python -m compressai_b200.diag rans --n 16777216 --reps 2
@@ -59,9 +61,18 @@ def cmd_gemv(a):
     idx, scale = synth.random_matrix(a.seed, a.out, a.n, bits)
     lin = runtime.PackedLinear((a.out, a.n), bits, "diag", [torch.from_numpy(i) for i in idx],
                                torch.from_numpy(scale), cbs, dev)
-    x = torch.randn(a.M, a.n, device=dev).half()
-    t = _time(lambda: lin(x), a.reps)
-    nbytes = a.out * a.n // 8 * (2 if a.bpw == 2 else 3) + 2 * a.out + 2 * a.M * (a.n + a.out)
+    if a.swiglu:
+        from . import _lib
+        x = torch.randn(a.M, 2 * a.n, device=dev)
+        cb0, cb1 = lin.codebooks()
+        t = _time(lambda: kernels.gemv_multi(x, [lin.mat()], cb0, cb1, rot=lin.rot, mode=_lib.VQ2_ACT_SWIGLU_RHT,
+                                             out_dtype=torch.float16), a.reps)
+        xbytes = 4 * a.M * 2 * a.n
+    else:
+        x = torch.randn(a.M, a.n, device=dev).half()
+        t = _time(lambda: lin(x), a.reps)
+        xbytes = 2 * a.M * a.n
+    nbytes = a.out * a.n // 8 * (2 if a.bpw == 2 else 3) + 2 * a.out + xbytes + 2 * a.M * a.out
     print(json.dumps({"gemv": [a.out, a.n, a.M, a.bpw], "us": round(t * 1e6, 2), "GBs": round(nbytes / t / 1e9, 1)}))
 
 
@@ -157,6 +168,7 @@ def main(argv=None):
     g.add_argument("--bpw", type=int, default=2, choices=(2, 3))
     g.add_argument("--reps", type=int, default=3)
     g.add_argument("--seed", type=int, default=0)
+    g.add_argument("--swiglu", action="store_true")
     m = sub.add_parser("moe")
     m.add_argument("--T", type=int, default=1)
     m.add_argument("--E", type=int, default=256)
