@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, in
   const int64_t m = active ? gs / nb : 0;
   const int64_t base = active ? (gs % nb) * HBK : 0;
   const int64_t xrow = m * x_row_stride;
+  pdl_wait();  // x may be the previous kernel's output (the tables are constant but few)
 
   float v[8];
 #pragma unroll
@@ -122,12 +123,11 @@ static int launch_rht(const void* x, int64_t xs, int64_t M, int64_t n, int log_h
   const dim3 grid(static_cast<unsigned>(blocks));
   switch (log_hb) {
 #define VQ2_RHT_CASE(L) \
-  case L: rht_kernel<L, MODE, TX><<<grid, 256, 0, st>>>(x, xs, M, n, perm, sign, scale, xr, xrs); break;
+  case L: return launch_kernel(rht_kernel<L, MODE, TX>, grid, dim3(256), 0, st, x, xs, M, n, perm, sign, scale, xr, xrs);
     VQ2_RHT_CASE(6) VQ2_RHT_CASE(7) VQ2_RHT_CASE(8) VQ2_RHT_CASE(9) VQ2_RHT_CASE(10) VQ2_RHT_CASE(11)
 #undef VQ2_RHT_CASE
     default: return VQ2_ERR_SHAPE;
   }
-  return launch_status();
 }
 
 static int log2_hb(int64_t n, int64_t hb) {

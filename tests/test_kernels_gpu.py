@@ -393,3 +393,30 @@ def test_lm_head_fused_greedy_argmax(cbs, M, bits, ties):
     assert torch.equal(got, torch.argmax(logits, dim=-1))
     if ties:
         assert (got == 123).all()
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+@pytest.mark.parametrize("n", [2048, 6144])
+@pytest.mark.parametrize("M", [1, 2, 3])
+def test_fused_staging_bitwise_equals_separate_transform(cbs, M, n, swiglu):
+    """The GEMV prologue's staging (rotation table in shared memory, coalesced row loads, one raw
+    row per round for M tiles that do not fit) gives the same bits as the standalone transform
+    kernel followed by a GEMV on the pre-rotated rows: both compute the same fp32 values in the
+    same order."""
+    from compressai_b200 import _lib
+    out = 1000
+    idx, scale = synth.random_matrix(7 + M, out, n, (16,))
+    cbd = dev_cbs(cbs)
+    mat = (torch.from_numpy(idx[0]).to(DEV), None, torch.from_numpy(scale).to(DEV, cbd["16"].dtype))
+    rot = vq.get_rot("mlp_down" if n == 6144 else "dense_q", n, DEV)
+    if swiglu:
+        x = torch.randn(M, 2 * n, device=DEV)
+        xr = kernels.swiglu_rht(x, rot)
+        mode = _lib.VQ2_ACT_SWIGLU_RHT
+    else:
+        x = torch.randn(M, n, device=DEV).half()
+        xr = rot.fwd_f32(x)
+        mode = _lib.VQ2_ACT_RHT
+    y_fused = kernels.gemv_multi(x, [mat], cbd["16"], None, rot=rot, mode=mode, out_dtype=torch.float32)[0]
+    y_split = kernels.gemv_multi(xr, [mat], cbd["16"], None, mode=_lib.VQ2_ACT_ROTATED, out_dtype=torch.float32)[0]
+    assert torch.equal(y_fused, y_split)
