@@ -152,11 +152,27 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
     }
   };
 
+  // This CTA's contiguous item range. With two CTAs per SM (the grid is the SMs x 2), CTAs b and
+  // b + G/2 split one SM-sized share of the items between them, so per-SM totals differ by at
+  // most one item (a CTA-level floor/ceil split alone can still give some SMs two large ranges);
+  // otherwise a plain floor/ceil split.
+  auto cta_items = [&](int64_t items, int64_t& lo, int64_t& hi) {
+    const int64_t G = gridDim.x, b = blockIdx.x;
+    if (G % 2 == 0) {
+      const int64_t half = G / 2, pr = b % half;
+      const int64_t p0 = pr * items / half, p1 = (pr + 1) * items / half, mid = p0 + (p1 - p0 + 1) / 2;
+      lo = b < half ? p0 : mid;
+      hi = b < half ? mid : p1;
+    } else {
+      lo = b * items / G;
+      hi = (b + 1) * items / G;
+    }
+  };
+
   // Items are known before the dependency wait unless the problem count lives on the device.
   const int64_t items_max = multi ? (int64_t)a.row_blocks * a.mtiles : (int64_t)a.row_blocks * a.K * a.mtiles;
-  int64_t per = (items_max + gridDim.x - 1) / gridDim.x;
-  int64_t item = (int64_t)blockIdx.x * per;
-  int64_t item_end = min(items_max, item + per);
+  int64_t item, item_end;
+  cta_items(items_max, item, item_end);
   int chunk = 0;
   uint4 iv[RW];
   uint2 jv[RW];
@@ -172,9 +188,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   if (!multi && a.prob_count) {  // device-side problem count (compacted problem lists)
     const int kc = min(a.K, max(0, *a.prob_count));
     const int64_t items = (int64_t)a.row_blocks * kc * a.mtiles;
-    per = (items + gridDim.x - 1) / gridDim.x;
-    item = (int64_t)blockIdx.x * per;
-    item_end = min(items, item + per);
+    cta_items(items, item, item_end);
   }
   if (!weights_known && item < item_end) {
     cur = decode(item);
