@@ -65,6 +65,11 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
 int run_gemm_tc(const GemvArgs& a, bool res, int val_dtype, void* ws, cudaStream_t st);
 // Workspace bytes of the tensor-core path: the 16-bit hi/lo split of the [M, n] activations.
 int64_t gemm_tc_workspace(int64_t M, int64_t n);
+// Forward RHT (or SwiGLU + RHT) of M rows into the hi / lo operand halves of the tensor-core
+// GEMV (rht.cu).
+int rht_split(const void* x, int x_dtype, int x_mode, int64_t x_row_stride, int64_t M, int64_t n, int64_t hb,
+              const int32_t* perm, const int8_t* sign, float scale, void* xh, void* xl, int val_dtype,
+              cudaStream_t st);
 
 // Launch the routing-weighted combine out[t] = sum_j w[t, j] y[t*top_k + j] (+ add[t]) (moe.cu);
 // with ids != null, rows whose id is outside [0, num_experts) are skipped.

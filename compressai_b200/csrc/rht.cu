@@ -10,10 +10,14 @@
 //      shuffles (T/16 <= 16, so partners are always in the same warp).
 // Forward: gather x[perm[j]] * sign[j] on load, contiguous store. Inverse: contiguous load,
 // multiply by sign[j] and scatter to perm[j] on store.
+// Forward results are fp32, or (for the tensor-core GEMV's A/B operand) split into a 16-bit
+// high half and the 16-bit rounding of the remainder, as that GEMV's split_hilo kernel does.
 // Semantics: Rot.fwd / Rot.inv in reference vq2/vq.py:66-87 (perm gather, sign, blocked
 // Sylvester Hadamard, hb^-0.5), FastRot in vq2/runtime.py:57-63 (out_scale = 1), and the
 // SwiGLU + rot_512.fwd of PagedMoEExpert.forward, vq2/paged_runtime.py:501-504.
-#include "common.cuh"
+#include <type_traits>
+
+#include "gemv.cuh"
 
 namespace vq2 {
 
@@ -40,11 +44,15 @@ __device__ __forceinline__ float ldx(const void* x, int64_t i) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
-template <int LOG_HB, int MODE, typename TX>
+// TO = float: fp32 result in xr. TO = __half / __nv_bfloat16 (forward modes only): the result w
+// stored as hi = TO(w) in xr and lo = TO(w - float(hi)) in xl, both [M, n] with row stride
+// xr_row_stride.
+template <int LOG_HB, int MODE, typename TX, typename TO = float>
 __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, int64_t x_row_stride, int64_t M,
                                                   int64_t n, const int32_t* __restrict__ perm,
                                                   const int8_t* __restrict__ sign, float out_scale,
-                                                  float* __restrict__ xr, int64_t xr_row_stride) {
+                                                  void* __restrict__ xr_, int64_t xr_row_stride,
+                                                  void* __restrict__ xl_ = nullptr) {
   constexpr int HBK = 1 << LOG_HB;
   constexpr int T = HBK / 8;    // threads per segment
   constexpr int SEG = 256 / T;  // segments per CTA
@@ -96,8 +104,30 @@ __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, in
     }
   }
   if (!active) return;
-  float* o = xr + m * xr_row_stride;
   const int64_t j0 = base + 8 * t;
+  if constexpr (!std::is_same<TO, float>::value) {  // hi / lo split for the tensor-core GEMV
+    TO hi[8], lo[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float w = v[i] * out_scale;
+      hi[i] = from_f32<TO>(w);
+      lo[i] = from_f32<TO>(w - to_f32<TO>(hi[i]));
+    }
+    TO* oh = static_cast<TO*>(xr_) + m * xr_row_stride + j0;
+    TO* ol = static_cast<TO*>(xl_) + m * xr_row_stride + j0;
+    if (aligned(oh, 16) && aligned(ol, 16)) {
+      *reinterpret_cast<uint4*>(oh) = *reinterpret_cast<const uint4*>(hi);
+      *reinterpret_cast<uint4*>(ol) = *reinterpret_cast<const uint4*>(lo);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        oh[i] = hi[i];
+        ol[i] = lo[i];
+      }
+    }
+    return;
+  }
+  float* o = static_cast<float*>(xr_) + m * xr_row_stride;
   if (MODE == kInverse) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[perm[j0 + i]] = v[i] * out_scale * static_cast<float>(sign[j0 + i]);
@@ -112,9 +142,9 @@ __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, in
   }
 }
 
-template <int MODE, typename TX>
+template <int MODE, typename TX, typename TO = float>
 static int launch_rht(const void* x, int64_t xs, int64_t M, int64_t n, int log_hb, const int32_t* perm,
-                      const int8_t* sign, float scale, float* xr, int64_t xrs, cudaStream_t st) {
+                      const int8_t* sign, float scale, void* xr, int64_t xrs, cudaStream_t st, void* xl = nullptr) {
   const int T = (1 << log_hb) / 8;
   const int seg = 256 / T;
   const int64_t segs = M * (n >> log_hb);
@@ -123,7 +153,7 @@ static int launch_rht(const void* x, int64_t xs, int64_t M, int64_t n, int log_h
   const dim3 grid(static_cast<unsigned>(blocks));
   switch (log_hb) {
 #define VQ2_RHT_CASE(L) \
-  case L: return launch_kernel(rht_kernel<L, MODE, TX>, grid, dim3(256), 0, st, x, xs, M, n, perm, sign, scale, xr, xrs);
+  case L: return launch_kernel(rht_kernel<L, MODE, TX, TO>, grid, dim3(256), 0, st, x, xs, M, n, perm, sign, scale, xr, xrs, xl);
     VQ2_RHT_CASE(6) VQ2_RHT_CASE(7) VQ2_RHT_CASE(8) VQ2_RHT_CASE(9) VQ2_RHT_CASE(10) VQ2_RHT_CASE(11)
 #undef VQ2_RHT_CASE
     default: return VQ2_ERR_SHAPE;
@@ -135,6 +165,33 @@ static int log2_hb(int64_t n, int64_t hb) {
   int l = 0;
   while ((int64_t(1) << l) < hb) ++l;
   return l;
+}
+
+// Forward RHT (x_mode RHT: x in x_dtype) or SwiGLU + RHT (x_mode SWIGLU_RHT: fp32 [gate | up])
+// of M rows, written as the hi / lo operand halves of the tensor-core GEMV (xh, xl: [M, n] in
+// val_dtype). One launch instead of a transform followed by the split.
+int rht_split(const void* x, int x_dtype, int x_mode, int64_t x_row_stride, int64_t M, int64_t n, int64_t hb,
+              const int32_t* perm, const int8_t* sign, float scale, void* xh, void* xl, int val_dtype,
+              cudaStream_t st) {
+  const int l = log2_hb(n, hb);
+  if (l < 0 || M <= 0) return VQ2_ERR_SHAPE;
+  if (x_mode == VQ2_ACT_SWIGLU_RHT) {
+    if (x_dtype != VQ2_F32) return VQ2_ERR_DTYPE;
+    return val_dtype == VQ2_F16 ? launch_rht<kSwiGLU, float, __half>(x, x_row_stride, M, n, l, perm, sign, scale, xh, n, st, xl)
+                                : launch_rht<kSwiGLU, float, __nv_bfloat16>(x, x_row_stride, M, n, l, perm, sign, scale, xh, n, st, xl);
+  }
+  if (x_mode != VQ2_ACT_RHT) return VQ2_ERR_ARG;
+#define VQ2_RHT_SPLIT(TXT)                                                                                     \
+  return val_dtype == VQ2_F16                                                                                  \
+             ? launch_rht<kForward, TXT, __half>(x, x_row_stride, M, n, l, perm, sign, scale, xh, n, st, xl)   \
+             : launch_rht<kForward, TXT, __nv_bfloat16>(x, x_row_stride, M, n, l, perm, sign, scale, xh, n, st, xl);
+  switch (x_dtype) {
+    case VQ2_F32: VQ2_RHT_SPLIT(float)
+    case VQ2_F16: VQ2_RHT_SPLIT(__half)
+    case VQ2_BF16: VQ2_RHT_SPLIT(__nv_bfloat16)
+    default: return VQ2_ERR_DTYPE;
+  }
+#undef VQ2_RHT_SPLIT
 }
 
 }  // namespace vq2

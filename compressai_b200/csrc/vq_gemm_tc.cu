@@ -346,16 +346,30 @@ static int run_split(const GemvArgs& a, void* ws, cudaStream_t st) {
 
 int64_t gemm_tc_workspace(int64_t M, int64_t n) { return 2 * M * n * 2; }
 
-// Tensor-core path for multi-matrix problems on pre-rotated activations with n % 128 == 0;
-// `ws` holds gemm_tc_workspace(M, n) bytes for the split operand. Returns -1 when the problem
-// is not eligible (the caller then uses the CUDA-core kernel).
+// Tensor-core path for multi-matrix problems with n % 128 == 0; `ws` holds
+// gemm_tc_workspace(M, n) bytes for the split operand. Pre-rotated activations are split by
+// split_hilo_kernel; modes RHT / SWIGLU_RHT are transformed and split in one launch
+// (rht_split). Returns -1 when the problem is not eligible (the caller then uses the CUDA-core
+// kernel).
 int run_gemm_tc(const GemvArgs& a0, bool res, int val_dtype, void* ws, cudaStream_t st) {
-  if (a0.nprob <= 0 || a0.x_mode != VQ2_ACT_ROTATED || a0.n % kTcKC != 0 || ws == nullptr) return -1;
+  if (a0.nprob <= 0 || a0.n % kTcKC != 0 || ws == nullptr) return -1;
   if (!aligned(ws, 16)) return VQ2_ERR_ALIGN;
   GemvArgs a = a0;
   a.x = ws;
   a.x_row_stride = a.n;
+  a.x_mode = VQ2_ACT_ROTATED;
   int s;
+  if (a0.x_mode != VQ2_ACT_ROTATED) {
+    const int64_t total = (int64_t)a0.M * a0.n;
+    void* xl = static_cast<char*>(ws) + total * 2;
+    if ((s = rht_split(a0.x, a0.x_dtype, a0.x_mode, a0.x_row_stride, a0.M, a0.n, a0.hb, a0.perm, a0.sign,
+                       a0.rot_scale, ws, xl, val_dtype, st)) != VQ2_OK)
+      return s;
+    if (val_dtype == VQ2_F16) return res ? launch_tc_nt<true, __half>(a, st) : launch_tc_nt<false, __half>(a, st);
+    if (val_dtype == VQ2_BF16)
+      return res ? launch_tc_nt<true, __nv_bfloat16>(a, st) : launch_tc_nt<false, __nv_bfloat16>(a, st);
+    return VQ2_ERR_DTYPE;
+  }
   if (val_dtype == VQ2_F16) {
     if ((s = run_split<__half>(a0, ws, st)) != VQ2_OK) return s;
     return res ? launch_tc_nt<true, __half>(a, st) : launch_tc_nt<false, __half>(a, st);

@@ -155,11 +155,6 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     M = x2.shape[0]
-    tall = sum(m[0].shape[0] for m in mats) >= 16384
-    if (M >= TC_MIN_ROWS or (M >= 2 and tall)) and mode != _lib.VQ2_ACT_ROTATED and n % 128 == 0:
-        # batched: rotate once with the standalone kernel, then the tensor-core GEMV
-        x2 = swiglu_rht(x2, rot) if mode == _lib.VQ2_ACT_SWIGLU_RHT else rot.fwd_f32(x2)
-        mode = _lib.VQ2_ACT_ROTATED
     res = mats[0][1] is not None
     _check_vals(cb0, cb1 if res else None, *[m[2] for m in mats])
     i0s, i1s, scs, outs = [], [], [], []
@@ -184,7 +179,7 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
         if y.numel() < o or (M > 1 and (y.dim() < 2 or y.shape[-2] < M)):
             raise ValueError("output too small")
     P = len(mats)
-    ws = _workspace(M, n, x.device) if mode == _lib.VQ2_ACT_ROTATED else None
+    ws = _workspace(M, n, x.device)   # batched (tensor-core) path: the transformed, split operand
     _lib.call("vq2_gemv_multi", _lib.ptr(x2), _lib.dtype_code(x2), int(mode), M, x2.stride(0),
               _lib.ptr(rot.perm) if rot is not None else None, _lib.ptr(rot.sign) if rot is not None else None,
               int(rot.hb) if rot is not None else 0, float(rot.scale) if rot is not None else 1.0, P,

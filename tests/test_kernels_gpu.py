@@ -397,12 +397,13 @@ def test_lm_head_fused_greedy_argmax(cbs, M, bits, ties):
 
 @pytest.mark.parametrize("swiglu", [False, True])
 @pytest.mark.parametrize("n", [2048, 6144])
-@pytest.mark.parametrize("M", [1, 2, 3])
+@pytest.mark.parametrize("M", [1, 2, 3, 8, 16])
 def test_fused_staging_bitwise_equals_separate_transform(cbs, M, n, swiglu):
-    """The GEMV prologue's staging (rotation table in shared memory, coalesced row loads, one raw
-    row per round for M tiles that do not fit) gives the same bits as the standalone transform
-    kernel followed by a GEMV on the pre-rotated rows: both compute the same fp32 values in the
-    same order."""
+    """The fused transform gives the same bits as the standalone transform kernel followed by a
+    GEMV on the pre-rotated rows: both compute the same fp32 values in the same order. M <= 3:
+    the CUDA-core prologue's staging (rotation table in shared memory, coalesced row loads, one
+    raw row per round for M tiles that do not fit). M >= 4: the tensor-core path's transform +
+    hi/lo split in one launch against the transform followed by the split kernel."""
     from compressai_b200 import _lib
     out = 1000
     idx, scale = synth.random_matrix(7 + M, out, n, (16,))
