@@ -383,7 +383,11 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
   if (!(done.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kGemvSmemCap);
-    if (e == cudaSuccess && XREG) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 20);
+    if (e == cudaSuccess && XREG) {  // small carveout (most of the SM's memory as L1), room for 2 CTAs
+      const int cta = ((xs_len(2048) + kScratchFloats + fast_extra_floats(1, 2048)) * 4 + (RES ? 4096 : 0)) + 1024;
+      const int pct = (2 * cta * 100 + 228 * 1024 - 1) / (228 * 1024);
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct > 20 ? pct : 20);
+    }
     if (e != cudaSuccess) { set_last_cuda_error(e); return VQ2_ERR_LAUNCH; }
     int nb = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, smem);
