@@ -35,6 +35,7 @@ SIGNATURES = {
     "vq2_gemv_multi": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _i64, _p, _p, _p, _p, _p, _p, _i32, _p,
                        _i32, _i64, _i64, _f32, _p, _i64, _p],
     "vq2_gemv_workspace": [_i64, _i64],
+    "vq2_tc_status": [_i32],
     "vq2_gemv_argmax": [_p, _i32, _i32, _i64, _i64, _p, _p, _i64, _f32, _p, _p, _p, _p, _p, _i32, _i64, _i64, _f32, _p,
                         _i32, _i64, _p, _p],
     "vq2_gemv": [_p, _i32, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i32, _i64, _i64, _i64, _f32, _p, _i64, _p],
@@ -57,6 +58,11 @@ SIGNATURES = {
     "vq2_moe_peer_buffer_bytes": [_i64, _i64, _i64],
     "vq2_moe_expert_ffn_ep": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
                               _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _p, _i32, _p],
+    "vq2_moe_layer_workspace": [_i64, _i64, _i32, _i64, _i64, _i64],
+    "vq2_moe_layer": [_p, _i32, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p, _i64, _i64, _i64, _i64, _i64,
+                      _p, _i32, _p, _p, _i64, _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _p],
+    "vq2_moe_layer_ep": [_p, _i32, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32,
+                         _p, _p, _i64, _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _p, _i32, _p],
     "vq2_lru_state_ints": [_i64, _i64],
     "vq2_lru_step": [_p, _p, _i64, _p, _p, _p],
     "vq2_fetch_records": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _p],

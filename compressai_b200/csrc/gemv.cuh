@@ -47,6 +47,15 @@ struct GemvArgs {
   int64_t y_row_stride;   // elements between output rows m
   unsigned long long* argmax;  // greedy argmax per activation row m (multi mode, CUDA cores), or null
   bool no_y;                   // argmax only: outputs are not written
+  // fused routing-weighted combine (expert-indexed mode; comb_w null: off): when the last of
+  // token t's problems has written a row block, the CTA that wrote it sums the token's problems
+  // there in problem order, out[t, r] = sum_c w[map[c]] * y[map[c], r], into comb_out
+  const float* comb_w;        // [T * comb_ks] weights by original problem index
+  const int32_t* comb_tstart; // [T] first compacted problem of token t
+  const int32_t* comb_tcnt;   // [T] compacted problems of token t
+  int32_t* comb_ctr;          // [T * row_blocks] arrival counters, zero at launch
+  void* comb_out;             // [T, out] in comb_dtype
+  int comb_dtype, comb_ks;
   int out;                // rows (expert-indexed mode)
   int n;
   float rs;
@@ -65,6 +74,13 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
 int run_gemm_tc(const GemvArgs& a, bool res, int val_dtype, void* ws, cudaStream_t st);
 // Workspace bytes of the tensor-core path: the 16-bit hi/lo split of the [M, n] activations.
 int64_t gemm_tc_workspace(int64_t M, int64_t n);
+// The 16-bit operand halves of the tensor-core paths from a's activations (vq_gemm_tc.cu): hi =
+// round(x), lo = round(x - hi), each [M, n]; the RHT (or SwiGLU + RHT) is applied on the way
+// when a.x_mode asks for it. xl null: hi only.
+int tc_operands(const GemvArgs& a, void* xh, void* xl, int val_dtype, cudaStream_t st);
+// Tensor-core path on tcgen05 / TMEM / TMA (vq_gemm_umma.cu) for multi-matrix problems with
+// enough 128-row tiles to fill the GPU; returns -1 when not eligible.
+int run_gemm_umma(const GemvArgs& a, bool res, int val_dtype, void* ws, int64_t ws_bytes, cudaStream_t st);
 // Forward RHT (or SwiGLU + RHT) of M rows into the hi / lo operand halves of the tensor-core
 // GEMV (rht.cu).
 int rht_split(const void* x, int x_dtype, int x_mode, int64_t x_row_stride, int64_t M, int64_t n, int64_t hb,
@@ -89,6 +105,37 @@ struct IdsByValue {
 int run_compact(const int32_t* ids, int64_t P, int64_t num_experts, int32_t* out_ids, int32_t* out_map,
                 int32_t* out_count, cudaStream_t st, const int32_t* host_ids = nullptr, int32_t* ids_copy = nullptr);
 
+// Router of one MoE layer (moe.cu): one CTA for all T tokens; see moe_route_kernel.
+struct RouteArgs {
+  const float* logits;
+  int T, E, K;
+  const void* h;
+  int h_dtype, H;
+  const float* gate;     // shared-expert gate [H] fp32, or null
+  int32_t* ids;          // [T, ks]
+  float* w;              // [T, ks]
+  int ks;                // K (+1 in layer mode with a shared expert)
+  float* shared_w;       // legacy mode: [T] sigmoid gate, or null
+  bool layer;            // layer mode (local ids, shared column, RHT, compaction)
+  int lo, hi, shared_row, rank, world;
+  const int32_t* perm;
+  const int8_t* sign;
+  int hb;
+  float rot_scale;
+  float* xrot;           // [T, H] fp32
+  int32_t* c_ids;        // [T*ks] compacted pool rows
+  int32_t* c_map;        // [T*ks] original problem index of each
+  int32_t* c_cnt;        // [1]
+  int32_t* tstart;       // [T] first compacted problem of token t
+  int32_t* tcnt;         // [T] compacted problems of token t
+  int32_t* zero;         // int32 words cleared for later kernels (combine counters), or null
+  int64_t zero_n;
+  void* out;             // layer mode: [T, H] rows of tokens without local problems are zeroed, or null
+  int out_dtype;
+};
+
+int run_route(const RouteArgs& r, cudaStream_t st);
+
 // Cross-GPU reduction of the expert-parallel combine over peer memory (moe_ep.cu).
 constexpr int kPeerMaxBlocks = 128;  // CTAs (output ranges) of the peer combine, at most
 struct PeerReduce {
@@ -112,6 +159,16 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
                    float scale_mid, void* ws, void* out, int out_dtype, cudaStream_t st, bool ids_on_host = false,
                    bool counters_zeroed = false, int32_t* err = nullptr, bool prefer_fused = false,
                    const void* cb1 = nullptr, const float* add = nullptr, const PeerReduce* peer = nullptr);
+
+// One MoE layer from router logits (moe_ffn.cu): route kernel, gate_up GEMV, down GEMV with the
+// combine in its epilogue (or the peer combine when `peer` is given).
+int64_t moe_layer_workspace(int64_t T, int64_t ks, int64_t H, int64_t gu_rows, int64_t dn_rows);
+int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E, int64_t K,
+              const float* shared_gate, int64_t lo, int64_t hi, int rank, int world, const void* pool,
+              int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0,
+              int val_dtype, const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in,
+              const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid, void* ws,
+              int64_t ws_bytes, void* out, int out_dtype, cudaStream_t st, const PeerReduce* peer);
 
 // Fused single-launch expert FFN for T * top_k <= 64 (moe_fused.cu).
 struct MoeFusedArgs {

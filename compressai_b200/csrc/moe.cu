@@ -1,75 +1,225 @@
 // MoE helper kernels: router (softmax top-k) and routing-weighted combine of expert outputs.
 #include <cfloat>
 
-#include "gemv.cuh"
+#include "gemv_dev.cuh"
 
 namespace vq2 {
 
-// Router, one warp per token: softmax over E logits, top-k, renormalised weights -- the math of
-// transformers Qwen3_5MoeTopKRouter.forward (softmax fp32 -> topk -> /= sum). Selection runs on
-// the logits (softmax is monotonic) with ties to the lower expert id; the renormalised weight
-// of a selected expert is exp(l_i - l_max) / sum_selected exp(l_j - l_max) because the full
-// softmax denominator cancels. Optionally the shared expert's weight sigmoid(h . g).
-constexpr int kMaxRouteE = 1024;
+// Router of one MoE layer, ONE CTA of 1024 threads for all T tokens (decode sizes): the math of
+// transformers Qwen3_5MoeTopKRouter.forward (softmax fp32 -> topk -> /= sum of the selected) and
+// of the shared expert's sigmoid(h . shared_gate) in Qwen3_5MoeSparseMoeBlock.forward.
+//   * Selection by rank counting: each of the TPT threads of a token holds one logit and counts
+//     the logits that beat it (greater, or equal with a lower expert id); ranks < K are the
+//     top-k in descending order with ties to the lower id, as the reference's argmax order.
+//     Softmax is monotonic, so this selects on the logits themselves.
+//   * Weights: exp(l_k - l_max) / sum over the selected of exp(l_j - l_max), summed in rank
+//     order by every selected thread alike (deterministic). The full softmax denominator
+//     cancels, so this is the reference's renormalised softmax up to fp32 rounding (~1e-7).
+//   * Layer mode (RouteArgs.xrot set): the expert ids are mapped to rows of this rank's pool
+//     (lo <= e < hi -> e - lo, else -1), the shared expert becomes problem column K (pool row
+//     shared_row, computed on rank t % world), the input RHT of every token's hidden state is
+//     written once for all CTAs of the gate_up GEMV, and the problems are compacted in order
+//     (ids, map, count, per-token start and count) for the GEMVs that follow.
+constexpr int kRouteThreads = 1024;
 
-__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, int64_t T, int E, int K,
-                                                        int32_t* __restrict__ ids, float* __restrict__ w,
-                                                        const void* h, int h_dtype, const float* __restrict__ g,
-                                                        int64_t H, float* __restrict__ shared_w) {
-  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  pdl_wait();
-  if (t >= T) return;
-  constexpr int PER = kMaxRouteE / 32;
-  float v[PER];
-  const float* lg = logits + t * E;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = i * 32 + lane;
-    v[i] = e < E ? lg[e] : -FLT_MAX;
-  }
-  uint32_t taken = 0;  // bit i: element i*32+lane selected
-  float sel_v[32];
-  int sel_e[32];
-  for (int k = 0; k < K; ++k) {
-    float bv = -FLT_MAX;
-    int be = INT32_MAX;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && !((taken >> i) & 1u) && (v[i] > bv || (v[i] == bv && e < be))) { bv = v[i]; be = e; }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-    }
-    if (be != INT32_MAX && (be & 31) == lane) taken |= 1u << (be >> 5);
-    sel_v[k] = bv;
-    sel_e[k] = be;
-  }
-  if (lane == 0) {
-    const float mx = sel_v[0];
-    float sum = 0.f;
-    for (int k = 0; k < K; ++k) sum += __expf(sel_v[k] - mx);
-    for (int k = 0; k < K; ++k) {
-      ids[t * K + k] = sel_e[k];
-      w[t * K + k] = __expf(sel_v[k] - mx) / sum;
-    }
-  }
-  if (g != nullptr) {
+template <int TPT>
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RouteArgs r) {
+  constexpr int TPR = kRouteThreads / TPT;  // tokens per round
+  __shared__ float sl[TPR][TPT];
+  __shared__ int sel_e[TPR][32];
+  __shared__ float sel_v[TPR][32];
+  __shared__ float red[kRouteThreads / 32];
+  __shared__ float rht_sc[8 * (kRouteThreads + kRouteThreads / 32)];  // (1024 / (hb / 8)) x (hb + hb / 32)
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int slot = tid / TPT, i = tid % TPT;
+  pdl_trigger();  // the GEMV that follows may start its own preamble
+  pdl_wait();      // logits, hidden state and the workspace belong to earlier kernels until here
+  for (int64_t z = tid; r.zero && z < r.zero_n; z += kRouteThreads) r.zero[z] = 0;
+
+  for (int t0 = 0; t0 < r.T; t0 += TPR) {
+    const int t = t0 + slot;
+    const bool tok = t < r.T;
+    // ---- logits, shared-gate partial dot product (loads of both issued before use)
+    const float l = (tok && i < r.E) ? r.logits[(int64_t)t * r.E + i] : -FLT_MAX;
     float d = 0.f;
-    for (int64_t i = lane; i < H; i += 32) {
-      float hv;
-      if (h_dtype == VQ2_F32) hv = static_cast<const float*>(h)[t * H + i];
-      else if (h_dtype == VQ2_F16) hv = __half2float(static_cast<const __half*>(h)[t * H + i]);
-      else hv = __bfloat162float(static_cast<const __nv_bfloat16*>(h)[t * H + i]);
-      d = fmaf(hv, g[i], d);
+    if (r.gate != nullptr && tok) {
+      for (int k = i; k < r.H; k += TPT) {
+        const int64_t o = (int64_t)t * r.H + k;
+        const float hv = r.h_dtype == VQ2_F32 ? static_cast<const float*>(r.h)[o]
+                         : r.h_dtype == VQ2_F16 ? __half2float(static_cast<const __half*>(r.h)[o])
+                                                : __bfloat162float(static_cast<const __nv_bfloat16*>(r.h)[o]);
+        d = fmaf(hv, r.gate[k], d);
+      }
     }
+    sl[slot][i] = l;
+    if (r.gate != nullptr) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-    if (lane == 0) shared_w[t] = 1.f / (1.f + __expf(-d));
+      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      if (lane == 0) red[warp] = d;
+    }
+    __syncthreads();
+    // ---- rank of this logit among its token's E logits
+    if (tok && i < r.E) {
+      int rank = 0;
+      const float* row = sl[slot];
+#pragma unroll 8
+      for (int j = 0; j < r.E; ++j) {
+        const float o = row[j];
+        rank += (o > l || (o == l && j < i)) ? 1 : 0;
+      }
+      if (rank < r.K) {
+        sel_e[slot][rank] = i;
+        sel_v[slot][rank] = l;
+      }
+    }
+    __syncthreads();
+    if (tok && i < r.K) {
+      const float mx = sel_v[slot][0];
+      float sum = 0.f;
+      for (int k = 0; k < r.K; ++k) sum += expf(sel_v[slot][k] - mx);
+      const int e = sel_e[slot][i];
+      const int64_t o = (int64_t)t * r.ks + i;
+      r.ids[o] = r.layer ? ((e >= r.lo && e < r.hi) ? e - r.lo : -1) : e;
+      r.w[o] = expf(sel_v[slot][i] - mx) / sum;
+    }
+    if (r.gate != nullptr && tok && i == 0) {
+      float dd = 0.f;
+      for (int wv = 0; wv < TPT / 32; ++wv) dd += red[slot * (TPT / 32) + wv];
+      const float sw = 1.f / (1.f + expf(-dd));
+      if (r.layer) {
+        r.ids[(int64_t)t * r.ks + r.K] = (t % r.world == r.rank) ? r.shared_row : -1;
+        r.w[(int64_t)t * r.ks + r.K] = sw;
+      } else if (r.shared_w) {
+        r.shared_w[t] = sw;
+      }
+    }
+    __syncthreads();
+  }
+  if (!r.layer) return;
+
+  // ---- forward RHT of every token's hidden state, fp32 [T, H]: segments of hb elements, each
+  // handled by hb / 8 threads (8 values each): 3 butterfly stages in registers, a transpose
+  // through shared memory, 3 more in registers, the rest by warp shuffles
+  {
+    const int TS = r.hb >> 3, SPR = kRouteThreads / TS, nb = r.H / r.hb;
+    const int sg = tid / TS, ts = tid % TS;
+    float* sc = rht_sc + sg * (r.hb + (r.hb >> 5));
+    for (int s0 = 0; s0 < r.T * nb; s0 += SPR) {
+      const int gs = s0 + sg;
+      const bool act = sg < SPR && gs < r.T * nb;
+      const int t = act ? gs / nb : 0, b = act ? gs % nb : 0;
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float val = 0.f;
+        if (act) {
+          const int j = b * r.hb + ts + TS * q;
+          const int64_t o = (int64_t)t * r.H + r.perm[j];
+          const float hv = r.h_dtype == VQ2_F32 ? static_cast<const float*>(r.h)[o]
+                           : r.h_dtype == VQ2_F16 ? __half2float(static_cast<const __half*>(r.h)[o])
+                                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(r.h)[o]);
+          val = hv * static_cast<float>(r.sign[j]);
+        }
+        v[q] = val;
+      }
+      fwht8(v);
+      if (act) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int e = ts + TS * q;
+          sc[e + (e >> 5)] = v[q];
+        }
+      }
+      __syncthreads();
+      if (act) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int e = 8 * ts + q;
+          v[q] = sc[e + (e >> 5)];
+        }
+      }
+      fwht8(v);
+      for (int td = 1; td <= (TS >> 4); td <<= 1) {
+        const bool upper = (ts & td) != 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float o = __shfl_xor_sync(0xffffffffu, v[q], td);
+          v[q] = upper ? (o - v[q]) : (v[q] + o);
+        }
+      }
+      if (act) {
+        float* o = r.xrot + (int64_t)t * r.H + b * r.hb + 8 * ts;
+        reinterpret_cast<float4*>(o)[0] = make_float4(v[0] * r.rot_scale, v[1] * r.rot_scale, v[2] * r.rot_scale,
+                                                      v[3] * r.rot_scale);
+        reinterpret_cast<float4*>(o)[1] = make_float4(v[4] * r.rot_scale, v[5] * r.rot_scale, v[6] * r.rot_scale,
+                                                      v[7] * r.rot_scale);
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---- stable compaction of the T * ks problems (pool row >= 0) and per-token ranges
+  const int P = r.T * r.ks;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < P; c0 += kRouteThreads) {
+    const int p = c0 + tid;
+    const int32_t id = p < P ? r.ids[p] : -1;
+    const bool keep = id >= 0;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int off = base;
+    for (int wv = 0; wv < warp; ++wv) off += warp_tot[wv];
+    if (keep) {
+      const int pos = off + __popc(m & ((1u << lane) - 1u));
+      r.c_ids[pos] = id;
+      r.c_map[pos] = p;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int wv = 0; wv < 32; ++wv) tot += warp_tot[wv];
+      base += tot;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) *r.c_cnt = base;
+  // per-token ranges: count of kept problems before token t and within it
+  for (int t = tid; t < r.T; t += kRouteThreads) {
+    int before = 0, mine = 0;
+    for (int p = 0; p < t * r.ks; ++p) before += r.ids[p] >= 0 ? 1 : 0;
+    for (int k = 0; k < r.ks; ++k) mine += r.ids[t * r.ks + k] >= 0 ? 1 : 0;
+    r.tstart[t] = before;
+    r.tcnt[t] = mine;
+    if (mine == 0 && r.out != nullptr) {  // nothing of this token is computed here: its output is zero
+      for (int k = 0; k < r.H; ++k) {
+        const int64_t o = (int64_t)t * r.H + k;
+        if (r.out_dtype == VQ2_F16) static_cast<__half*>(r.out)[o] = __float2half_rn(0.f);
+        else if (r.out_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(r.out)[o] = __float2bfloat16_rn(0.f);
+        else static_cast<float*>(r.out)[o] = 0.f;
+      }
+    }
+  }
+}
+
+int run_route(const RouteArgs& r, cudaStream_t st) {
+  if (r.T <= 0 || r.E <= 0 || r.E > kRouteThreads || r.K <= 0 || r.K > 32 || r.K > r.E) return VQ2_ERR_SHAPE;
+  if (r.layer) {
+    if (!r.xrot || !r.perm || !r.sign || !r.c_ids || !r.c_map || !r.c_cnt || !r.tstart || !r.tcnt) return VQ2_ERR_ARG;
+    if (r.hb < 64 || r.hb > 2048 || (r.hb & (r.hb - 1)) != 0 || r.H % r.hb != 0) return VQ2_ERR_SHAPE;
+    if (!aligned(r.xrot, 16) || r.world <= 0 || r.rank < 0 || r.rank >= r.world) return VQ2_ERR_ARG;
+  }
+  const int tpt = r.E <= 32 ? 32 : r.E <= 64 ? 64 : r.E <= 128 ? 128 : r.E <= 256 ? 256 : r.E <= 512 ? 512 : 1024;
+  switch (tpt) {
+    case 32: return launch_kernel(moe_route_kernel<32>, dim3(1), dim3(kRouteThreads), 0, st, r);
+    case 64: return launch_kernel(moe_route_kernel<64>, dim3(1), dim3(kRouteThreads), 0, st, r);
+    case 128: return launch_kernel(moe_route_kernel<128>, dim3(1), dim3(kRouteThreads), 0, st, r);
+    case 256: return launch_kernel(moe_route_kernel<256>, dim3(1), dim3(kRouteThreads), 0, st, r);
+    case 512: return launch_kernel(moe_route_kernel<512>, dim3(1), dim3(kRouteThreads), 0, st, r);
+    default: return launch_kernel(moe_route_kernel<1024>, dim3(1), dim3(kRouteThreads), 0, st, r);
   }
 }
 
@@ -176,12 +326,12 @@ extern "C" int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t 
                              void* stream) {
   using namespace vq2;
   if (!logits || !ids || !w) return VQ2_ERR_ARG;
-  if (T <= 0 || E <= 0 || E > kMaxRouteE || K <= 0 || K > 32 || K > E) return VQ2_ERR_SHAPE;
-  if (shared_gate && (!h || !shared_w || H <= 0)) return VQ2_ERR_ARG;
+  if (T <= 0 || T > (1 << 20) || E <= 0 || E > kRouteThreads || K <= 0 || K > 32 || K > E) return VQ2_ERR_SHAPE;
+  if (shared_gate && (!h || !shared_w || H <= 0 || H > (1 << 24))) return VQ2_ERR_ARG;
   if (shared_gate && h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
-  const int64_t blocks = (T * 32 + 255) / 256;
-  if (blocks > INT32_MAX) return VQ2_ERR_SHAPE;
-  return launch_kernel(moe_route_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-                       static_cast<cudaStream_t>(stream), logits, T, (int)E, (int)K, ids, w, h, h_dtype,
-                       shared_gate, H, shared_w);
+  RouteArgs r{};
+  r.logits = logits; r.T = (int)T; r.E = (int)E; r.K = (int)K;
+  r.h = h; r.h_dtype = h_dtype; r.H = (int)H; r.gate = shared_gate;
+  r.ids = ids; r.w = w; r.ks = (int)K; r.shared_w = shared_w; r.layer = false;
+  return run_route(r, static_cast<cudaStream_t>(stream));
 }

@@ -171,3 +171,27 @@ extern "C" int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int6
                              scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream), false, false,
                              nullptr, false, nullptr, nullptr, &pr);
 }
+
+extern "C" int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E, int64_t top_k,
+                                const float* shared_gate, int64_t expert_lo, int64_t expert_hi, const void* pool,
+                                int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols,
+                                const void* cb0, int val_dtype, const int32_t* perm_in, const int8_t* sign_in,
+                                int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid,
+                                int64_t hb_mid, float scale_mid, void* workspace, int64_t workspace_bytes,
+                                void* const* peers_dev, int rank, int world, int64_t max_tokens, uint32_t* epochs,
+                                int32_t* err, void* out, int out_dtype, void* stream) {
+  if (T <= 0 || T > max_tokens) return VQ2_ERR_SHAPE;
+  if (!peers_dev || !epochs || world < 2 || world > 64) return VQ2_ERR_ARG;
+  vq2::PeerReduce pr;
+  pr.peers = reinterpret_cast<uint8_t* const*>(peers_dev);
+  pr.rank = rank;
+  pr.world = world;
+  pr.part_off = vq2::peer_flag_bytes(world);
+  pr.part_bytes = vq2::peer_slot_bytes(max_tokens, gu_cols * 8);
+  pr.epochs = reinterpret_cast<int32_t*>(epochs);
+  pr.err = err;
+  return vq2::moe_layer(h, h_dtype, T, logits, E, top_k, shared_gate, expert_lo, expert_hi, rank, world, pool,
+                        pool_rows, gu_rows, gu_cols, dn_rows, dn_cols, cb0, val_dtype, perm_in, sign_in, hb_in,
+                        scale_in, perm_mid, sign_mid, hb_mid, scale_mid, workspace, workspace_bytes, out, out_dtype,
+                        static_cast<cudaStream_t>(stream), &pr);
+}

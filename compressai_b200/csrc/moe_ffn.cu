@@ -138,6 +138,116 @@ int moe_expert_ffn(const void* h, int h_dtype, int64_t T, int64_t top_k, const i
   return run_combine(yd, w, T, (int)top_k, H, add, out, out_dtype, st, ids, num_experts);
 }
 
+// ---- one MoE layer from router logits ------------------------------------------------------
+// Workspace of moe_layer: [xrot fp32 T x H][ids, w: T x ks][compacted ids, map: P][count]
+// [tstart, tcnt: T][combine counters: T x ceil(dn_rows / 8)][gate_up out fp32 P x gu_rows]
+// [down out fp32 P x dn_rows], each part 256-byte aligned (P = T * ks).
+struct LayerWs {
+  float* xrot;
+  int32_t* ids;
+  float* w;
+  int32_t *c_ids, *c_map, *c_cnt, *tstart, *tcnt, *ctr;
+  float *gu, *yd;
+  int64_t ctr_n, bytes;
+};
+
+static LayerWs layer_ws(void* base, int64_t T, int64_t ks, int64_t H, int64_t gu_rows, int64_t dn_rows) {
+  LayerWs L{};
+  const int64_t P = T * ks;
+  char* p = static_cast<char*>(base);
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    char* q = p ? p + off : nullptr;
+    off += align256(bytes);
+    return q;
+  };
+  L.xrot = reinterpret_cast<float*>(take(T * H * 4));
+  L.ids = reinterpret_cast<int32_t*>(take(P * 4));
+  L.w = reinterpret_cast<float*>(take(P * 4));
+  L.c_ids = reinterpret_cast<int32_t*>(take(P * 4));
+  L.c_map = reinterpret_cast<int32_t*>(take(P * 4));
+  L.c_cnt = reinterpret_cast<int32_t*>(take(4));
+  L.tstart = reinterpret_cast<int32_t*>(take(T * 4));
+  L.tcnt = reinterpret_cast<int32_t*>(take(T * 4));
+  L.ctr_n = T * ((dn_rows + 7) / 8);
+  L.ctr = reinterpret_cast<int32_t*>(take(L.ctr_n * 4));
+  L.gu = reinterpret_cast<float*>(take(P * gu_rows * 4));
+  L.yd = reinterpret_cast<float*>(take(P * dn_rows * 4));
+  L.bytes = off;
+  return L;
+}
+
+int64_t moe_layer_workspace(int64_t T, int64_t ks, int64_t H, int64_t gu_rows, int64_t dn_rows) {
+  return layer_ws(nullptr, T, ks, H, gu_rows, dn_rows).bytes;
+}
+
+// Router + routed (and shared) expert FFN + combine of one MoE layer: three launches (route,
+// gate_up, down with the combine in its epilogue), or four with the cross-rank sum over peer
+// memory (route, gate_up, down, peer combine).
+int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E, int64_t K,
+              const float* shared_gate, int64_t lo, int64_t hi, int rank, int world, const void* pool,
+              int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0,
+              int val_dtype, const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in,
+              const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid, void* ws,
+              int64_t ws_bytes, void* out, int out_dtype, cudaStream_t st, const PeerReduce* peer) {
+  if (!h || !logits || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid || !ws || !out)
+    return VQ2_ERR_ARG;
+  if (T <= 0 || T > 4096 || E <= 0 || K <= 0 || K > 32 || K > E) return VQ2_ERR_SHAPE;
+  if (gu_rows <= 0 || gu_rows % 2 != 0 || gu_cols <= 0 || gu_cols % 8 != 0 || dn_cols <= 0 || dn_cols % 8 != 0)
+    return VQ2_ERR_SHAPE;
+  if (dn_cols * 8 != gu_rows / 2 || dn_rows != gu_cols * 8) return VQ2_ERR_SHAPE;
+  if (lo < 0 || hi < lo || hi > E || world <= 0 || rank < 0 || rank >= world) return VQ2_ERR_ARG;
+  const int64_t ks = K + (shared_gate ? 1 : 0);
+  const int64_t shared_row = hi - lo;
+  if (pool_rows < shared_row + (shared_gate ? 1 : 0)) return VQ2_ERR_SHAPE;
+  if (h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (out_dtype != VQ2_F32 && out_dtype != VQ2_F16 && out_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  const int64_t H = gu_cols * 8, I = gu_rows / 2;
+  const RecordLayout R = record_layout(gu_rows, gu_cols, dn_rows, dn_cols);
+  if (R.bytes % 16 != 0 || R.dn_idx % 16 != 0) return VQ2_ERR_ALIGN;
+  if (!aligned(pool, 16) || !aligned(cb0, 16) || !aligned(ws, 256)) return VQ2_ERR_ALIGN;
+  const LayerWs L = layer_ws(ws, T, ks, H, gu_rows, dn_rows);
+  if (ws_bytes < L.bytes) return VQ2_ERR_ARG;
+  const int64_t P = T * ks;
+
+  RouteArgs r{};
+  r.logits = logits; r.T = (int)T; r.E = (int)E; r.K = (int)K;
+  r.h = h; r.h_dtype = h_dtype; r.H = (int)H; r.gate = shared_gate;
+  r.ids = L.ids; r.w = L.w; r.ks = (int)ks; r.layer = true;
+  r.lo = (int)lo; r.hi = (int)hi; r.shared_row = (int)shared_row; r.rank = rank; r.world = world;
+  r.perm = perm_in; r.sign = sign_in; r.hb = (int)hb_in; r.rot_scale = scale_in; r.xrot = L.xrot;
+  r.c_ids = L.c_ids; r.c_map = L.c_map; r.c_cnt = L.c_cnt; r.tstart = L.tstart; r.tcnt = L.tcnt;
+  r.zero = peer ? nullptr : L.ctr; r.zero_n = peer ? 0 : L.ctr_n;
+  r.out = peer ? nullptr : out; r.out_dtype = out_dtype;
+  int s = run_route(r, st);
+  if (s != VQ2_OK) return s;
+
+  const char* base = static_cast<const char*>(pool);
+  GemvArgs a{};
+  a.nprob = 0;
+  a.x = L.xrot; a.x_dtype = VQ2_F32; a.x_mode = VQ2_ACT_ROTATED; a.x_row_stride = 0; a.x_k_stride = H;
+  a.x_k_div = ks; a.M = 1;
+  a.idx0 = reinterpret_cast<const int16_t*>(base + R.gu_idx); a.cb0 = cb0;
+  a.scale = base + R.gu_scale; a.y = L.gu; a.y_dtype = VQ2_F32; a.y_row_stride = 0; a.y_k_stride = gu_rows;
+  a.e_ids = L.c_ids; a.prob_count = L.c_cnt; a.prob_map = L.c_map;
+  a.num_experts = pool_rows; a.idx_e_stride = R.bytes / 2; a.idx1_e_stride = R.bytes; a.scale_e_stride = R.bytes / 2;
+  a.out = (int)gu_rows; a.n = (int)H; a.rs = 1.f; a.K = (int)P;
+  if ((s = run_gemv(a, gu_rows * P, false, val_dtype, st)) != VQ2_OK) return s;
+
+  GemvArgs b = a;
+  b.x = L.gu; b.x_mode = VQ2_ACT_SWIGLU_RHT; b.x_k_stride = gu_rows; b.x_k_div = 1;
+  b.perm = perm_mid; b.sign = sign_mid; b.hb = (int)hb_mid; b.rot_scale = scale_mid;
+  b.idx0 = reinterpret_cast<const int16_t*>(base + R.dn_idx); b.scale = base + R.dn_scale;
+  b.y = L.yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
+  if (!peer) {  // the routing-weighted sum of each token's problems in the down GEMV's epilogue
+    b.comb_w = L.w; b.comb_tstart = L.tstart; b.comb_tcnt = L.tcnt; b.comb_ctr = L.ctr;
+    b.comb_out = out; b.comb_dtype = out_dtype; b.comb_ks = (int)ks;
+  }
+  if ((s = run_gemv(b, dn_rows * P, false, val_dtype, st)) != VQ2_OK) return s;
+  if (peer) return run_combine_peer(L.yd, L.w, T, (int)ks, H, L.ids, pool_rows, *peer, out, out_dtype, st);
+  return VQ2_OK;
+}
+
 }  // namespace vq2
 
 extern "C" int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows, int64_t dn_rows) {
@@ -229,4 +339,23 @@ extern "C" int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T,
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
                              scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream), false, true);
+}
+
+extern "C" int64_t vq2_moe_layer_workspace(int64_t T, int64_t top_k, int has_shared, int64_t hidden, int64_t gu_rows,
+                                           int64_t dn_rows) {
+  if (T <= 0 || top_k <= 0 || hidden <= 0 || gu_rows <= 0 || dn_rows <= 0) return -1;
+  return vq2::moe_layer_workspace(T, top_k + (has_shared ? 1 : 0), hidden, gu_rows, dn_rows);
+}
+
+extern "C" int vq2_moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E, int64_t top_k,
+                             const float* shared_gate, int64_t expert_lo, int64_t expert_hi, int rank, int world,
+                             const void* pool, int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                             int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in,
+                             const int8_t* sign_in, int64_t hb_in, float scale_in, const int32_t* perm_mid,
+                             const int8_t* sign_mid, int64_t hb_mid, float scale_mid, void* workspace,
+                             int64_t workspace_bytes, void* out, int out_dtype, void* stream) {
+  return vq2::moe_layer(h, h_dtype, T, logits, E, top_k, shared_gate, expert_lo, expert_hi, rank, world, pool,
+                        pool_rows, gu_rows, gu_cols, dn_rows, dn_cols, cb0, val_dtype, perm_in, sign_in, hb_in,
+                        scale_in, perm_mid, sign_mid, hb_mid, scale_mid, workspace, workspace_bytes, out, out_dtype,
+                        static_cast<cudaStream_t>(stream), nullptr);
 }

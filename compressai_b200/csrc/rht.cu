@@ -46,7 +46,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g))
 
 // TO = float: fp32 result in xr. TO = __half / __nv_bfloat16 (forward modes only): the result w
 // stored as hi = TO(w) in xr and lo = TO(w - float(hi)) in xl, both [M, n] with row stride
-// xr_row_stride.
+// xr_row_stride; with xl null only the hi half is written.
 template <int LOG_HB, int MODE, typename TX, typename TO = float>
 __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, int64_t x_row_stride, int64_t M,
                                                   int64_t n, const int32_t* __restrict__ perm,
@@ -114,15 +114,15 @@ __global__ void __launch_bounds__(256) rht_kernel(const void* __restrict__ x, in
       lo[i] = from_f32<TO>(w - to_f32<TO>(hi[i]));
     }
     TO* oh = static_cast<TO*>(xr_) + m * xr_row_stride + j0;
-    TO* ol = static_cast<TO*>(xl_) + m * xr_row_stride + j0;
-    if (aligned(oh, 16) && aligned(ol, 16)) {
+    TO* ol = xl_ ? static_cast<TO*>(xl_) + m * xr_row_stride + j0 : nullptr;  // null: hi only
+    if (aligned(oh, 16) && (!ol || aligned(ol, 16))) {
       *reinterpret_cast<uint4*>(oh) = *reinterpret_cast<const uint4*>(hi);
-      *reinterpret_cast<uint4*>(ol) = *reinterpret_cast<const uint4*>(lo);
+      if (ol) *reinterpret_cast<uint4*>(ol) = *reinterpret_cast<const uint4*>(lo);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         oh[i] = hi[i];
-        ol[i] = lo[i];
+        if (ol) ol[i] = lo[i];
       }
     }
     return;

@@ -80,7 +80,8 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // x = hi + lo in the 16-bit type TV, hi = round(x), lo = round(x - hi): the operand split of the
-// tensor-core path, written once per call for all CTAs (xh [M, n] then xl [M, n]).
+// tensor-core path, written once per call for all CTAs (xh [M, n] then xl [M, n]; xl null: hi
+// only).
 template <typename TV>
 __global__ void __launch_bounds__(256) split_hilo_kernel(const void* __restrict__ x, int x_dtype, int64_t M, int64_t n,
                                                          int64_t x_row_stride, TV* __restrict__ xh,
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(256) split_hilo_kernel(const void* __restrict_
   else v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[off]);
   const TV hi = Mma<TV>::cvt(v);
   xh[i] = hi;
-  xl[i] = Mma<TV>::cvt(v - Mma<TV>::back(hi));
+  if (xl) xl[i] = Mma<TV>::cvt(v - Mma<TV>::back(hi));
 }
 
 // NT: 8-token tiles per M tile (M tile = 8 * NT tokens); RES: 3 bpw. a.x = the hi halves
@@ -345,6 +346,25 @@ static int run_split(const GemvArgs& a, void* ws, cudaStream_t st) {
 }
 
 int64_t gemm_tc_workspace(int64_t M, int64_t n) { return 2 * M * n * 2; }
+
+int tc_operands(const GemvArgs& a, void* xh, void* xl, int val_dtype, cudaStream_t st) {
+  if (!aligned(xh, 16) || (xl && !aligned(xl, 16))) return VQ2_ERR_ALIGN;
+  if (a.x_mode != VQ2_ACT_ROTATED)
+    return rht_split(a.x, a.x_dtype, a.x_mode, a.x_row_stride, a.M, a.n, a.hb, a.perm, a.sign, a.rot_scale, xh, xl,
+                     val_dtype, st);
+  const int64_t total = (int64_t)a.M * a.n;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > INT32_MAX) return VQ2_ERR_SHAPE;
+  if (val_dtype == VQ2_F16)
+    return launch_kernel(split_hilo_kernel<__half>, dim3((unsigned)blocks), dim3(256), 0, st, a.x, a.x_dtype,
+                         (int64_t)a.M, (int64_t)a.n, a.x_row_stride, static_cast<__half*>(xh),
+                         static_cast<__half*>(xl));
+  if (val_dtype == VQ2_BF16)
+    return launch_kernel(split_hilo_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, st, a.x,
+                         a.x_dtype, (int64_t)a.M, (int64_t)a.n, a.x_row_stride, static_cast<__nv_bfloat16*>(xh),
+                         static_cast<__nv_bfloat16*>(xl));
+  return VQ2_ERR_DTYPE;
+}
 
 // Tensor-core path for multi-matrix problems with n % 128 == 0; `ws` holds
 // gemm_tc_workspace(M, n) bytes for the split operand. Pre-rotated activations are split by

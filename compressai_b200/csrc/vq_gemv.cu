@@ -54,6 +54,38 @@ __device__ __forceinline__ void stage_tile(const ActSrc& a, int64_t xoff, int mc
   else stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
 }
 
+// Fused combine after an item of expert-indexed problem o, row block rb (RPC rows) is written:
+// arrival count per (token, row block); the CTA that brings it to the token's problem count sums
+// the token's problems over the block's rows in problem order (the fmaf chain of
+// moe_combine_kernel, so the result is bit-identical) and writes comb_out. Called by all
+// threads of the CTA at the same point of the item sequence.
+__device__ __noinline__ void combine_tail(const GemvArgs& a, int o, int rb, int rpc) {
+  __shared__ int s_last;
+  __threadfence();  // this thread's output rows are visible GPU-wide before the arrival
+  __syncthreads();
+  const int t = o / a.comb_ks;
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(a.comb_ctr + (int64_t)t * a.row_blocks + rb, 1);
+    s_last = (old == a.comb_tcnt[t] - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int r = rb * rpc + (int)threadIdx.x;
+  if ((int)threadIdx.x < rpc && r < a.out) {
+    const int c0 = a.comb_tstart[t], cn = a.comb_tcnt[t];
+    float s = 0.f;
+    for (int c = c0; c < c0 + cn; ++c) {
+      const int oo = a.prob_map ? a.prob_map[c] : c;
+      s = fmaf(a.comb_w[oo], __ldcg(static_cast<const float*>(a.y) + (int64_t)oo * a.y_k_stride + r), s);
+    }
+    const int64_t i = (int64_t)t * a.out + r;
+    if (a.comb_dtype == VQ2_F16) static_cast<__half*>(a.comb_out)[i] = __float2half_rn(s);
+    else if (a.comb_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(a.comb_out)[i] = __float2bfloat16_rn(s);
+    else static_cast<float*>(a.comb_out)[i] = s;
+  }
+}
+
 // Variants that stage the fast way: all but the 3 bpw two-row register variant, whose
 // registers are taken by its two rows of residual indices.
 template <int RW, bool RES, bool XREG>
@@ -332,6 +364,7 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
           if (lane == 0 && mi < mcount && b) atomicMax(a.argmax + m0 + mi, b);
         }
       }
+      if (!multi && a.comb_w != nullptr) combine_tail(a, cur.o, cur.rb, RPC);  // uniform over the CTA
     }
     item = nitem;
     chunk = nchunk;
@@ -471,7 +504,11 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
   // the GPU with 128-row items (measured: lm_head at M = 4 is faster there than on CUDA cores).
   const bool tc = a.M >= kTcMinRows || (a.M >= 2 && total_rows >= kTcTallRows);
   if (tc && a.nprob > 0 && !a.argmax && ws != nullptr && ws_bytes >= gemm_tc_workspace(a.M, a.n)) {
-    const int r = run_gemm_tc(a, res, val_dtype, ws, st);  // batched: decode into tensor-core MMAs
+    // batched: decode into tensor-core MMAs -- tcgen05 / TMEM when the 128-row tiles fill the
+    // GPU, else the split-K mma.sync kernel
+    int r = run_gemm_umma(a, res, val_dtype, ws, ws_bytes, st);
+    if (r != -1) return r;
+    r = run_gemm_tc(a, res, val_dtype, ws, st);
     if (r != -1) return r;
   }
   const int mt = pick_mt(a.M, a.n);

@@ -109,12 +109,26 @@ VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, in
 
 /*
  * Workspace bytes vq2_gemv_multi / vq2_gemv use for M activation rows of length n (0 for one
- * row; -1 on bad sizes). With mode ROTATED, n % 128 == 0 and M >= 4 (or M >= 2 when the
- * matrices total >= 16384 rows) the GEMV runs on the tensor cores (mma.sync m16n8k16 fed directly by the codebook gathers, activations split into
- * 16-bit hi + lo halves held in the workspace, 16-byte aligned); with no workspace, or one too
- * small, it runs on the CUDA cores with the same result.
+ * row; -1 on bad sizes). With n % 128 == 0 and M >= 4 (or M >= 2 when the matrices total
+ * >= 16384 rows) the GEMV runs on the tensor cores, its 16-bit activation operand(s) held in the
+ * workspace (16-byte aligned; 128-byte aligned for the tcgen05 kernel):
+ *   - matrices with at least one 128-row tile per SM: tcgen05.mma with the accumulator in tensor
+ *     memory, the activation tile loaded by TMA, the codebook rows gathered into swizzled shared
+ *     memory (fp16 codebooks: activations rounded once to fp16, max error ~2e-4 of max|y|; bf16:
+ *     hi + lo halves, two MMAs per step);
+ *   - smaller matrices: mma.sync m16n8k16 fed directly by the gathers, split-K over thread-block
+ *     clusters, activations as hi + lo halves (fp32-level accuracy).
+ * With no workspace, or one too small, it runs on the CUDA cores.
  */
 VQ2_API int64_t vq2_gemv_workspace(int64_t M, int64_t n);
+
+/*
+ * Sticky status of the tcgen05 GEMV kernel on the current device: VQ2_ERR_TIMEOUT once one of
+ * its bounded on-chip waits gave up (the affected CTA freed its tensor memory and returned, its
+ * outputs incomplete), else VQ2_OK; reset != 0 clears it. Synchronous (reads device memory).
+ * No reference counterpart (the reference has no device-side waits).
+ */
+VQ2_API int vq2_tc_status(int reset);
 
 /*
  * VQ GEMV on a pre-rotated activation, one matrix (vq2_gemv_multi with P = 1, mode ROTATED;
@@ -244,6 +258,38 @@ VQ2_API int vq2_moe_expert_ffn_res(const void* h, int h_dtype, int64_t T, int64_
                                    int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
 /*
+ * One sparse MoE layer from router logits, three launches on `stream`:
+ *   1. one CTA: router (softmax over E, top_k by logit with ties to the lower id, weights
+ *      renormalised over the selected), the shared expert's sigmoid gate, the mapping of expert
+ *      ids to this rank's pool rows, the input RHT of every token (written once to the
+ *      workspace) and the ordered list of (token, expert) problems computed here;
+ *   2. gate_up GEMV over those problems;
+ *   3. down GEMV (SwiGLU + RHT 512 in its prologue) whose epilogue also forms
+ *      out[t] = sum_j w[t, j] * down_j(t) in problem order (the CTA completing a token's last
+ *      problem in a row block sums it).
+ * h: [T, H] in h_dtype (H = gu_cols * 8); logits: fp32 [T, E] (E <= 1024, top_k <= 32,
+ * T <= 4096); shared_gate: fp32 [H] or NULL (no shared expert). Pool rows: experts
+ * [expert_lo, expert_hi) at rows 0..hi-lo-1 and, with a shared gate, the shared expert at row
+ * hi-lo; its problem for token t is computed on rank t % world (rank/world: 0/1 on one GPU).
+ * Tokens with no problem on this rank get zero rows. Workspace: vq2_moe_layer_workspace bytes,
+ * 256-byte aligned, no state kept between calls. out: [T, H] in out_dtype.
+ * Replaces: Qwen3_5MoeSparseMoeBlock.forward's router + shared expert (installed transformers
+ * modeling_qwen3_5_moe.py:762-791) around the reference's expert call
+ * (vq2/load_and_test_full_35b.py:53-95, vq2/paged_runtime.py:439-511).
+ */
+VQ2_API int64_t vq2_moe_layer_workspace(int64_t T, int64_t top_k, int has_shared, int64_t hidden,
+                                        int64_t gu_rows, int64_t dn_rows);
+VQ2_API int vq2_moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E,
+                          int64_t top_k, const float* shared_gate, int64_t expert_lo,
+                          int64_t expert_hi, int rank, int world, const void* pool,
+                          int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                          int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in,
+                          const int8_t* sign_in, int64_t hb_in, float scale_in,
+                          const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
+                          float scale_mid, void* workspace, int64_t workspace_bytes, void* out,
+                          int out_dtype, void* stream);
+
+/*
  * Expert-parallel vq2_moe_expert_ffn whose combine also sums over the ranks of a group, in one
  * kernel over NVLink peer memory (instead of combine -> NCCL all_reduce -> cast). ids: this
  * rank's local pool rows (-1 for experts of other ranks). peers_dev: device array of `world`
@@ -264,6 +310,25 @@ VQ2_API int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int64_t
                                   int64_t workspace_bytes, void* const* peers_dev, int rank,
                                   int world, int64_t max_tokens, uint32_t* epochs, int32_t* err,
                                   void* out, int out_dtype, void* stream);
+
+/*
+ * Expert-parallel vq2_moe_layer: the same route / gate_up / down sequence on this rank's
+ * experts, then the routing-weighted combine and the sum over the ranks in one kernel over
+ * NVLink peer memory (peers_dev, epochs, err and max_tokens as vq2_moe_expert_ffn_ep). Every
+ * rank makes the same calls with the same logits and hidden states; the output is identical
+ * on every rank.
+ */
+VQ2_API int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E,
+                             int64_t top_k, const float* shared_gate, int64_t expert_lo,
+                             int64_t expert_hi, const void* pool, int64_t pool_rows,
+                             int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols,
+                             const void* cb0, int val_dtype, const int32_t* perm_in,
+                             const int8_t* sign_in, int64_t hb_in, float scale_in,
+                             const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
+                             float scale_mid, void* workspace, int64_t workspace_bytes,
+                             void* const* peers_dev, int rank, int world, int64_t max_tokens,
+                             uint32_t* epochs, int32_t* err, void* out, int out_dtype,
+                             void* stream);
 
 /* Workspace bytes vq2_moe_expert_ffn needs for T tokens x top_k experts (-1 on bad sizes). */
 VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t gu_rows,

@@ -331,10 +331,13 @@ def test_tensor_core_batched_gemv(cbs, M, bits, cbdt):
     assert rel_err(y, ref) < 3e-5
 
 
-@pytest.mark.parametrize("out,n,M", [(2048, 6144, 16), (9000, 1024, 24), (40000, 2048, 8), (130, 256, 64)])
-def test_tensor_core_split_k_shapes(cbs, out, n, M):
-    """Split-K over thread-block clusters (items that fill less than half the GPU: S = 8, 4, 1,
-    and K too short to split) agrees with the fp64 oracle to fp32 accuracy."""
+@pytest.mark.parametrize("out,n,M,tol", [(2048, 6144, 16, 3e-5), (9000, 1024, 24, 3e-5), (40000, 2048, 8, 1e-3),
+                                         (130, 256, 64, 3e-5)])
+def test_tensor_core_split_k_shapes(cbs, out, n, M, tol):
+    """Split-K over thread-block clusters (items that fill less than half the GPU: S = 8, 4, and
+    K too short to split) agrees with the fp64 oracle to fp32 accuracy (hi + lo operands); the
+    40000-row matrix has a 128-row tile per SM and runs on the tcgen05 kernel (fp16 operand:
+    1e-3)."""
     idx, scale = synth.random_matrix(out + n, out, n)
     cbd = dev_cbs(cbs)
     sc = torch.from_numpy(scale).to(DEV)
@@ -343,7 +346,7 @@ def test_tensor_core_split_k_shapes(cbs, out, n, M):
                         out_dtype=torch.float32).cpu().numpy()
     cb_np = cbd["16"].float().cpu().numpy()
     ref = np.stack([O.vq_gemv_legacy(x[m], idx[0], cb_np, scale.astype(np.float32), 1.0) for m in range(M)])
-    assert rel_err(y, ref) < 3e-5
+    assert rel_err(y, ref) < tol
 
 
 def test_tensor_core_path_without_workspace_falls_back_exactly(cbs):
