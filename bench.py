@@ -21,7 +21,12 @@ Multi-GPU: one process per GPU (torchrun); every rank runs its own replica of th
 
 --impl reference: the reference's CPU path (gather + einsum GEMV of
 scratch/test_cpu_vq_gemv.py, restated in oracle/cpu_path.py) on the host cores, each step a
-bounded sample (one layer's 7 GEMVs + 1/24 of lm_head's rows).
+bounded sample (one layer's 7 GEMVs + 1/24 of lm_head's rows) of the same seeded workload,
+generated on the host with numpy; that arm loads nothing of compressai_b200 and touches no GPU.
+
+The JSON line ends with the MoE (BASELINE configs 3 and 5 shapes, T = 1/8/32/64, expert-parallel
+at N > 1 with its outputs checked against a single-GPU block holding all experts) and paged
+(config 4) results.
 """
 import argparse
 import json
@@ -39,8 +44,9 @@ sys.path.insert(0, REPO)
 
 HIDDEN, INTER, VOCAB = 2048, 6144, 151936
 # DRAM bytes of one lm_head GEMV launch (ncu dram__bytes rate x duration) over its algorithmic
-# bytes: 81.26 MB / 78.39 MB (profiles/vq_gemv_m1.md)
+# bytes, 81.26 MB / 78.39 MB, from the ncu capture of that launch
 NCU_TRAFFIC_RATIO = 1.037
+MOE_TOKENS = (1, 8, 32, 64)
 METRIC = "VQ GEMV HBM GB/s (compressed bytes)"
 UNIT = "GB/s"
 WORKLOAD = ("config2 decode step: 24 layers x (q,k,v,o 2048x2048; gate,up 2048->6144; down 6144->2048) "
@@ -59,6 +65,110 @@ def shapes(layers):
               ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]
     s.append(("lm_head", VOCAB, HIDDEN))
     return s
+
+
+def step_bytes(layers):
+    return sum(gemv_bytes(o, n) for _, o, n in shapes(layers))
+
+
+def make_config(args, world):
+    """The workload description both arms print (identical, so the driver can pair them)."""
+    return {"workload": WORKLOAD, "global_batch": world, "seq_len": 1, "bpw": 2, "layers": args.layers,
+            "step_weight_bytes": step_bytes(args.layers), "l2": "inputs larger than L2 (no flush)",
+            "parallelism": f"dense replicas x{world}" if world > 1 else "single GPU"}
+
+
+# ------------------------------------------------------------------- host (CPU) workloads
+def host_matrix(seed, out, n):
+    """Seeded int16 indices and fp32 row scales of one matrix, generated on the host (numpy)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    idx = rng.integers(-32768, 32768, size=(out, n // 8), dtype=np.int16)
+    scale = (0.02 * np.exp(0.1 * rng.standard_normal(out))).astype(np.float32)
+    return torch.from_numpy(idx), torch.from_numpy(scale)
+
+
+def host_sample(layer, lm_slice=None, layers=24):
+    """One layer's 7 matrices (+ rows [r0, r1) of lm_head) as host tensors."""
+    work = []
+    for j, (_, out, n) in enumerate(shapes(1)[:7]):
+        i, sc = host_matrix([1234, layer, j], out, n)
+        work.append((i, sc, n))
+    if lm_slice is not None:
+        r0, r1 = lm_slice
+        i, sc = host_matrix([1234, 999, r0], r1 - r0, HIDDEN)
+        work.append((i, sc, HIDDEN))
+    return work
+
+
+def cpu_gemv_sample(work, min_seconds, cb):
+    """Time the reference CPU GEMV path (oracle/cpu_path.py) over `work` until min_seconds."""
+    from oracle import cpu_path
+    xs = {n: torch.randn(n) for _, _, n in work}
+    nbytes = sum(gemv_bytes(i.shape[0], n) for i, _, n in work)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for i, s, n in work:
+            cpu_path.vq_gemv_cpu_streaming(xs[n], i, cb, s)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return nbytes * reps, el, reps
+
+
+def host_codebook():
+    import numpy as np
+    return torch.from_numpy(np.random.default_rng(1).standard_normal((1 << 16, 8)).astype(np.float16)).float()
+
+
+def cpu_moe_sample(min_seconds, cb):
+    """One MoE layer (8 routed + the shared expert, SwiGLU 2048 -> 512 -> 2048 at 2 bpw) through the
+    reference's CPU expert path (vq_moe_parallel_gate_up_cpu / _down_cpu, restated in
+    oracle/cpu_path.py) with the normalised rotations, timed on the host cores until
+    min_seconds; tok/s of a 40-layer decode step."""
+    import numpy as np
+
+    from oracle import cpu_path
+    from oracle import vq2_oracle as O
+    rng = np.random.default_rng(11)
+    P = 9
+    gu_idx = torch.from_numpy(rng.integers(-32768, 32768, size=(P, 1024, 256), dtype=np.int16))
+    gu_sc = torch.from_numpy((0.02 * np.exp(0.1 * rng.standard_normal((P, 1024)))).astype(np.float32))
+    dn_idx = torch.from_numpy(rng.integers(-32768, 32768, size=(P, 2048, 64), dtype=np.int16))
+    dn_sc = torch.from_numpy((0.02 * np.exp(0.1 * rng.standard_normal((P, 2048)))).astype(np.float32))
+    rots = {}
+    for tag, n in (("moe_expert_2048", 2048), ("moe_expert_512", 512)):
+        perm, sign, hb = O.rot_params(tag, n)
+        rots[n] = (torch.from_numpy(perm), torch.from_numpy(sign).float(), hb)
+    slots = list(range(P))
+    w = torch.full((P,), 1.0 / P)
+    x = torch.randn(2048)
+
+    def layer():
+        xr = cpu_path.rht_cpu(x, *rots[2048])
+        y_gu = cpu_path.moe_gate_up_cpu(xr, slots, gu_idx, cb, gu_sc)
+        act = torch.nn.functional.silu(y_gu[:, :512]) * y_gu[:, 512:]
+        act_r = cpu_path.rht_cpu(act, *rots[512])
+        y_dn = cpu_path.moe_down_cpu(act_r, slots, dn_idx, cb, dn_sc)
+        return (y_dn * w[:, None]).sum(0)
+
+    layer()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        layer()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    t_layer = el / reps
+    return {"value": round(1.0 / (40 * t_layer), 3), "unit": "tok/s (40-layer MoE step, T = 1)",
+            "cores": torch.get_num_threads(), "kind": "port", "layer_ms": round(t_layer * 1e3, 2),
+            "sample": f"one MoE layer (8 routed + shared expert) x{reps} ({el:.1f} s): Rot.fwd + "
+                      "vq_moe_parallel_gate_up_cpu + silu*up + Rot.fwd(512) + vq_moe_parallel_down_cpu + "
+                      "weighted sum (scratch/test_cpu_paged_moe.py:31-75, rs = 1)"}
 
 
 # ------------------------------------------------------------------------------------ clocks
@@ -174,34 +284,6 @@ def barrier(dist):
     torch.cuda.synchronize()
 
 
-def cpu_gemv_sample(stack, min_seconds, layer_from=0, lm_rows=None):
-    """Time the reference CPU GEMV path on host copies of one layer (+ lm_head rows)."""
-    from oracle import cpu_path
-    cb = stack.cbs["16"].float().cpu()
-    xs = {}
-    work = []
-    li = layer_from % stack.layers
-    for name, m in stack.mods[7 * li: 7 * li + 7]:
-        work.append((m.idx0.cpu(), m.scale.float().cpu(), m.n))
-    if lm_rows is not None:
-        m = stack.mods[-1][1]
-        r0, r1 = lm_rows
-        work.append((m.idx0[r0:r1].cpu(), m.scale[r0:r1].float().cpu(), m.n))
-    for _, _, n in work:
-        xs[n] = torch.randn(n)
-    nbytes = sum(gemv_bytes(i.shape[0], n) for i, _, n in work)
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        for i, s, n in work:
-            cpu_path.vq_gemv_cpu_streaming(xs[n], i, cb, s)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= min_seconds:
-            break
-    return nbytes * reps, el, reps
-
-
 def run_ours(args, dist, rank, world):
     from compressai_b200 import kernels
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -209,7 +291,7 @@ def run_ours(args, dist, rank, world):
     torch.manual_seed(0)
     stack = DecodeStack(args.layers, dev, seed=1234)
     sh = shapes(args.layers)
-    step_bytes = sum(gemv_bytes(o, n) for _, o, n in sh)
+    sbytes = step_bytes(args.layers)
     stream = torch.cuda.Stream(dev)
     h_static = torch.randn(1, HIDDEN, device=dev).half()
     # warm-up eagerly (first-call setup), then capture the step; the NVTX range marks the
@@ -281,26 +363,23 @@ def run_ours(args, dist, rank, world):
     peaks = load_peaks()
     n_gemv = len(sh)
     per_launch_s = t_gemv / (args.steps * n_gemv)
-    achieved = step_bytes / n_gemv / per_launch_s / 1e9
+    achieved = sbytes / n_gemv / per_launch_s / 1e9
     res = {
-        "metric": METRIC, "value": round(world * step_bytes * args.steps / t / 1e9, 2), "unit": UNIT,
+        "metric": METRIC, "value": round(world * sbytes * args.steps / t / 1e9, 2), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (fp16 in/out, int16 indices)",
         "data": "synthetic: seeded uniform 16-bit indices, fp16 scales ~0.02, N(0,1) fp16 codebook and input",
-        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1, "bpw": 2, "layers": args.layers,
-                   "step_weight_bytes": step_bytes, "l2": "inputs larger than L2 (no flush)",
-                   "parallelism": f"replicas x{world}"},
-        "e2e": {"value": round(world * step_bytes * args.steps / t_e2e / 1e9, 2), "unit": UNIT,
+        "config": make_config(args, world),
+        "e2e": {"value": round(world * sbytes * args.steps / t_e2e / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": HIDDEN * 2, "d2h_bytes_per_step": VOCAB * 2,
                 "ms_per_step": round(t_e2e / args.steps * 1e3, 4)},
         "roofline": {"bound": "hbm", "kernel": "vq_gemv_kernel", "achieved": round(achieved, 1),
                      "peak": peaks[0], "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
                      "peak_source": peaks[1],
-                     "traffic": round(NCU_TRAFFIC_RATIO * step_bytes / n_gemv, 0),
+                     "traffic": round(NCU_TRAFFIC_RATIO * sbytes / n_gemv, 0),
                      "traffic_source": "ncu dram bytes of one lm_head launch / its algorithmic bytes = "
-                                       f"{NCU_TRAFFIC_RATIO} (profiles/vq_gemv_m1.md), x the mean "
-                                       "algorithmic bytes per launch",
+                                       f"{NCU_TRAFFIC_RATIO}, x the mean algorithmic bytes per launch",
                      "avg_launch_us": round(per_launch_s * 1e6, 3), "launches_per_step": n_gemv,
                      "gather_ceiling": {"measured_gathers_per_s": round(gather_ceiling, 0),
                                         "achieved_gathers_per_s": round(step_idx / (t_gemv / args.steps), 0),
@@ -313,105 +392,135 @@ def run_ours(args, dist, rank, world):
 
 
 # ------------------------------------------------------------------------------ MoE (config 3/5)
-def run_moe(args, dev, dist, world, T, steps, warmup):
+def run_moe(args, dev, dist, world, steps, warmup, tokens=MOE_TOKENS):
     """Decode step of a 40-layer stack of MoE blocks (256 routed experts + 1 shared, top-8,
-    SwiGLU 2048->512->2048 at 2 bpw, all resident): router kernel + expert FFN per layer on
-    device logits. N = 1: MoEBlock in a CUDA graph. N > 1: expert parallel -- each rank holds
-    256/N experts of every layer (+ the shared expert on rank 0), replicated router, the rank sum
-    done by the combine kernel over NVLink peer memory (NCCL all_reduce when symmetric memory is
-    unavailable). Expert bytes per layer = (distinct experts + shared)
-    x 792,576 B, all ranks together."""
+    SwiGLU 2048->512->2048 at 2 bpw, all resident) on device logits, one vq2_moe_layer call per
+    layer, the 40 layers in one CUDA graph. N = 1: MoEBlock. N > 1: expert parallel -- rank r
+    holds experts [r*256/N, (r+1)*256/N) of every layer plus the shared expert (its token t on
+    rank t % N); replicated router; the rank sum in the combine kernel over NVLink peer memory
+    (NCCL all_reduce when symmetric memory is unavailable). Every rank also builds the
+    single-GPU block over all experts and checks the expert-parallel output against it, layer by
+    layer, and that all ranks hold the same output. Expert bytes per layer = (distinct experts +
+    shared) x 792,576 B, all ranks together."""
     from compressai_b200 import ep, moe, synth, vq
     L, E = args.moe_layers, 256
     rank = dist.get_rank() if dist is not None else 0
-    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    g = torch.Generator(device=dev).manual_seed(4321)      # identical expert data on every rank
     cb = torch.from_numpy(synth.random_codebooks(1)["16"]).to(dev)
-    gl = torch.Generator(device=dev).manual_seed(999)  # identical router inputs on every rank
+    gl = torch.Generator(device=dev).manual_seed(999)      # identical router inputs on every rank
     lo, hi = ep.partition(E, world, rank)
-    n_local = (hi - lo) + (1 if rank == 0 else 0)
     r_in, r_mid = vq.get_rot("moe_expert_2048", HIDDEN, dev), vq.get_rot("moe_expert_512", 512, dev)
-    blocks, logits = [], []
+    Tmax = max(tokens)
     peer_ctx = None
     if world > 1:  # one symmetric buffer for the rank sums of all layers (see ep.py)
         try:
-            peer_ctx = ep.PeerReduceContext(None, dev, max_tokens=T, hidden=HIDDEN)
+            peer_ctx = ep.PeerReduceContext(None, dev, max_tokens=Tmax, hidden=HIDDEN)
         except Exception:
             peer_ctx = None
+    blocks, ref_blocks, gates = [], [], []
     for _ in range(L):
-        pool = moe.ExpertRecordPool(n_local if world > 1 else E + 1, dev)
-        w16 = pool.raw.view(torch.int16)
+        full = moe.ExpertRecordPool(E + 1, dev)
+        w16 = full.raw.view(torch.int16)
         w16.copy_(torch.randint(-32768, 32768, w16.shape, generator=g, device=dev, dtype=torch.int16))
-        pool.gu_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.gu_scale.shape, generator=g, device=dev)))
-        pool.dn_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(pool.dn_scale.shape, generator=g, device=dev)))
+        full.gu_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(full.gu_scale.shape, generator=g, device=dev)))
+        full.dn_scale.copy_(0.02 * torch.exp(0.1 * torch.randn(full.dn_scale.shape, generator=g, device=dev)))
         gate = 0.02 * torch.randn(HIDDEN, generator=gl, device=dev)
+        ref = moe.MoEBlock(moe.PackedMoEExpertUniversal(full, cb, dev, shared=True), shared_gate=gate)
         if world > 1:
+            pool = moe.ExpertRecordPool(hi - lo + 1, dev)
+            pool.raw[: hi - lo].copy_(full.raw[lo:hi])
+            pool.raw[hi - lo].copy_(full.raw[E])
             blocks.append(ep.ExpertParallelMoEBlock(pool, cb, E, r_in, r_mid, shared_gate=gate,
                                                     reduce="peer" if peer_ctx is not None else "nccl",
-                                                    peer_ctx=peer_ctx, max_tokens=T))
+                                                    peer_ctx=peer_ctx, max_tokens=Tmax))
+            ref_blocks.append(ref)
         else:
-            blocks.append(moe.MoEBlock(moe.PackedMoEExpertUniversal(pool, cb, dev, shared=True), shared_gate=gate))
-        logits.append(torch.randn(T, E, generator=gl, device=dev))
-    h0 = torch.randn(T, HIDDEN, generator=gl, device=dev).half()
-
-    def step(h):
-        for blk, lg in zip(blocks, logits):
-            h = blk(h, lg)
-        return h
-
-    distinct = sum(int(torch.unique(moe.route(lg, 8)[0]).numel()) + 1 for lg in logits)
-    step_bytes = distinct * synth.EXPERT_BYTES
-    stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        step(h0)
-    torch.cuda.synchronize()
-    gr, graphed = None, True
-    try:
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            out = step(h0)
-    except Exception:  # capture of the NCCL all_reduce refused: time the eager step instead
-        gr, graphed = None, False
-        torch.cuda.synchronize()
-    barrier(dist)
-
-    def replay():
-        if gr is not None:
-            gr.replay()
-        else:
-            step(h0)
-
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            replay()
-    barrier(dist)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(steps):
-            replay()
-        e1.record(stream)
-    e1.synchronize()
-    t = max_over_ranks(e0.elapsed_time(e1) / 1e3, dist)
-    with torch.cuda.stream(stream):
-        out = step(h0)
-    torch.cuda.synchronize()
+            blocks.append(ref)
     peak = load_peaks()[0]
-    ach = step_bytes * steps / t / 1e9
-    res = {"T": T, "layers": L, "tok_s": round(T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
-           "parallelism": f"expert-parallel x{world}" if world > 1 else "single GPU",
-           "expert_bytes_per_step": step_bytes, "distinct_experts_per_layer": round(distinct / L, 2),
-           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world, "unit": "GB/s",
-                        "frac": round(ach / (peak * world), 4)},
-           "launches_per_step": 4 * L, "graph": graphed, "finite": bool(torch.isfinite(out.float()).all())}
-    if world > 1:
-        res["rank_sum"] = ("combine kernel over NVLink peer memory" if blocks[0].reduce_kind == "peer"
-                           else "NCCL all_reduce")
-        if peer_ctx is not None:
-            peer_ctx.check()
-    del gr, blocks
+    results = []
+    for T in tokens:
+        logits = [torch.randn(T, E, generator=gl, device=dev) for _ in range(L)]
+        h0 = torch.randn(T, HIDDEN, generator=gl, device=dev).half()
+
+        def step(h):
+            for blk, lg in zip(blocks, logits):
+                h = blk(h, lg)
+            return h
+
+        distinct = sum(int(torch.unique(moe.route(lg, 8)[0]).numel()) + 1 for lg in logits)
+        sbytes = distinct * synth.EXPERT_BYTES
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            step(h0)
+        torch.cuda.synchronize()
+        gr, graphed = None, True
+        try:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                out = step(h0)
+        except Exception:  # capture of the NCCL all_reduce refused: time the eager step instead
+            gr, graphed = None, False
+            torch.cuda.synchronize()
+        barrier(dist)
+
+        def replay():
+            if gr is not None:
+                gr.replay()
+            else:
+                step(h0)
+
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                replay()
+        barrier(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                replay()
+            e1.record(stream)
+        e1.synchronize()
+        t = max_over_ranks(e0.elapsed_time(e1) / 1e3, dist)
+        ach = sbytes * steps / t / 1e9
+        per_layer = 4 if (world > 1 and blocks[0].reduce_kind == "peer") else 3
+        res = {"T": T, "tok_s": round(T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
+               "us_per_layer": round(t / steps / L * 1e6, 2), "distinct_experts_per_layer": round(distinct / L, 2),
+               "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world, "unit": "GB/s",
+                            "frac": round(ach / (peak * world), 4)},
+               "launches_per_step": per_layer * L, "graph": graphed}
+        # parity: the output of one eager step
+        torch.cuda.synchronize()
+        if world > 1:
+            worst, h = 0.0, h0
+            for blk, rb, lg in zip(blocks, ref_blocks, logits):
+                y = blk(h, lg)
+                r = rb(h, lg)
+                worst = max(worst, float((y.float() - r.float()).abs().max() / r.float().abs().max()))
+                h = y
+            mine = h.contiguous()
+            allv = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allv, mine)
+            res["max_rel_err_vs_single_gpu"] = round(max_over_ranks(worst, dist), 7)
+            res["ranks_identical"] = all(bool(torch.equal(allv[0], v)) for v in allv[1:])
+            res["finite"] = bool(torch.isfinite(mine.float()).all())
+        else:
+            with torch.cuda.stream(stream):
+                out = step(h0)
+            torch.cuda.synchronize()
+            res["finite"] = bool(torch.isfinite(out.float()).all())
+        del gr
+        results.append(res)
+    summary = {"layers": L, "experts": f"{E} routed + 1 shared, top-8, 2 bpw, all resident",
+               "bytes_per_layer": "(distinct + 1) x 792,576", "per_T": results,
+               "parallelism": (f"expert-parallel x{world}, rank sum: " +
+                               ("combine kernel over NVLink peer memory" if blocks[0].reduce_kind == "peer"
+                                else "NCCL all_reduce")) if world > 1 else "single GPU"}
+    if peer_ctx is not None:
+        peer_ctx.check()
+    del blocks, ref_blocks
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
-    return res
+    return summary
 
 
 # ------------------------------------------------------------------------------ paging (config 4)
@@ -571,14 +680,23 @@ def run_sweep(dev, Ms=(1, 4, 16, 64), reps=10):
                     gr.replay()
                 t = time_graph(gr, reps, st) / (reps * copies)
                 alg = gemv_bytes(rows, n, M, bits == 3)
+                tc = M >= 4 or (M >= 2 and rows >= 16384)
                 out.append({"out": rows, "n": n, "bpw": bits, "M": M, "us": round(t * 1e6, 2),
                             "GBs": round(alg / t / 1e9, 1), "gathers_per_s": round(rows * n / 8 / t, 0),
-                            "path": "tensor cores (mma.sync)" if (M >= 4 or (M >= 2 and rows >= 16384))
+                            "path": ("tcgen05" if rows // 128 >= 148 else "mma.sync split-K") if tc
                             else "CUDA cores"})
                 del gr
             del i0s, i1s
             torch.cuda.empty_cache()
     return out
+
+
+def sweep_summary(sweep):
+    """{"<out>x<n>": {"b<bpw>": {"<M>": us}}} -- the compact form printed in the JSON line."""
+    d = {}
+    for e in sweep:
+        d.setdefault(f"{e['out']}x{e['n']}", {}).setdefault(f"b{e['bpw']}", {})[str(e["M"])] = e["us"]
+    return d
 
 
 def load_peaks():
@@ -592,19 +710,20 @@ def load_peaks():
 
 
 def run_reference(args, rank, world):
-    """Reference CPU path on the host cores; rank 0 only."""
+    """The reference's CPU path on the host cores, rank 0 only: each step one layer's 7 GEMVs and
+    1/24 of lm_head's rows of the seeded workload, generated here on the host. Loads nothing of
+    compressai_b200 and touches no GPU."""
     if rank != 0:
         return None
     torch.set_num_threads(os.cpu_count())
-    dev = "cuda" if torch.cuda.is_available() else None
-    if dev is None:
-        raise SystemExit("bench.py needs a CUDA device to build the workload")
-    stack = DecodeStack(args.layers, torch.device(dev), seed=1234)
+    cb = host_codebook()
     rows_per = (VOCAB + args.layers - 1) // args.layers
     total_b, total_t = 0, 0.0
     for s in range(args.warmup + args.steps):
-        r0 = (s % args.layers) * rows_per
-        b, t, _ = cpu_gemv_sample(stack, 0.0, layer_from=s, lm_rows=(r0, min(VOCAB, r0 + rows_per)))
+        li = s % args.layers
+        r0 = li * rows_per
+        work = host_sample(li, (r0, min(VOCAB, r0 + rows_per)))
+        b, t, _ = cpu_gemv_sample(work, 0.0, cb)
         if s >= args.warmup:
             total_b += b
             total_t += t
@@ -612,12 +731,13 @@ def run_reference(args, rank, world):
     return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
-            "data": "synthetic (same seeded workload as our arm)",
-            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": 1, "bpw": 2, "layers": args.layers,
-                       "parallelism": "host cores"},
+            "data": "synthetic: seeded uniform 16-bit indices, fp16 scales ~0.02, N(0,1) codebook and input",
+            "config": make_config(args, world),
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": "per step: one layer's 7 GEMVs + 1/24 of lm_head rows, gather+einsum fp32 "
-                                       "(scratch/test_cpu_vq_gemv.py:53-70)"},
+                             "sample": f"per step: one layer's 7 GEMVs + 1/{args.layers} of lm_head rows (a bounded "
+                                       "sample of the step; the metric is a rate), gather+einsum fp32 "
+                                       "(scratch/test_cpu_vq_gemv.py:53-70)",
+                             "moe": cpu_moe_sample(args.cpu_seconds, cb)},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -632,10 +752,16 @@ def main():
     ap.add_argument("--moe-layers", type=int, default=40)
     ap.add_argument("--paged-steps", type=int, default=512)
     ap.add_argument("--dense-only", action="store_true")
+    ap.add_argument("--sweep-json", default=None, help="write the full config-2 sweep here")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":  # host cores only: no process group, no GPU
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
     dist = None
     if world > 1:
         import datetime
@@ -644,27 +770,29 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = tdist
     try:
-        if args.impl == "reference":
-            res = run_reference(args, rank, world)
-        else:
-            res, stack = run_ours(args, dist, rank, world)
-            if rank == 0 and world == 1:
-                torch.set_num_threads(os.cpu_count())
-                b, t, reps = cpu_gemv_sample(stack, args.cpu_seconds)
-                res["cpu_baseline"] = {"value": round(b / t / 1e9, 3), "unit": UNIT,
-                                       "cores": torch.get_num_threads(), "kind": "port",
-                                       "sample": f"layer 0's 7 GEMVs x{reps} ({t:.1f} s), gather+einsum fp32 "
-                                                 "(scratch/test_cpu_vq_gemv.py:53-70)"}
-            if not args.dense_only:
-                dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-                del stack
-                torch.cuda.empty_cache()
-                res["moe"] = [run_moe(args, dev, dist, world, T, args.steps, args.warmup) for T in (1, 32)]
-                if world == 1:
-                    res["sweep"] = run_sweep(dev)
-                if world == 1:
-                    res["paged"] = run_paged(args, dev)
-                    res["paged_ans"] = run_paged(args, dev, coding="vq2a")
+        res, stack = run_ours(args, dist, rank, world)
+        if rank == 0 and world == 1:
+            torch.set_num_threads(os.cpu_count())
+            cb = host_codebook()
+            b, t, reps = cpu_gemv_sample(host_sample(0), args.cpu_seconds, cb)
+            res["cpu_baseline"] = {"value": round(b / t / 1e9, 3), "unit": UNIT,
+                                   "cores": torch.get_num_threads(), "kind": "port",
+                                   "sample": f"one layer's 7 GEMVs x{reps} ({t:.1f} s), gather+einsum fp32 "
+                                             "(scratch/test_cpu_vq_gemv.py:53-70)",
+                                   "moe": cpu_moe_sample(args.cpu_seconds, cb)}
+        if not args.dense_only:
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+            del stack
+            torch.cuda.empty_cache()
+            if world == 1:
+                sweep = run_sweep(dev)
+                res["sweep_us"] = sweep_summary(sweep)
+                if args.sweep_json:
+                    with open(args.sweep_json, "w") as f:
+                        json.dump(sweep, f, indent=1)
+                res["paged"] = run_paged(args, dev)
+                res["paged_ans"] = run_paged(args, dev, coding="vq2a")
+            res["moe"] = run_moe(args, dev, dist, world, args.steps, args.warmup)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:

@@ -1,27 +1,31 @@
-"""Small, self-contained GPU workloads for profiling and measurement (ncu-sized).
+"""Small, self-contained GPU workloads for profiling and measurement (ncu-sized): the commands
+behind the launch lists and captures summarised in profiles/. Not part of the package.
 
-  python -m compressai_b200.diag gather
+  python bench_diag.py gather
       random codebook-row gather rates (global / shared / cluster-shared memory)
-  python -m compressai_b200.diag gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3 [--swiglu]
+  python bench_diag.py gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3 [--swiglu]
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
       with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
       prologue (the MLP down projection)
-  python -m compressai_b200.diag moe --T 1 --reps 3
+  python bench_diag.py moe --T 1 --reps 3
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts
-  python -m compressai_b200.diag rans --n 16777216 --reps 2
+  python bench_diag.py rans --n 16777216 --reps 2
       `reps` GPU decodes of one VQ2A stream of n skewed index bytes, then `reps` decodes of one
       ANS-coded expert record (vq2_rans_decode_segments)
-  python -m compressai_b200.diag paged --layers 2 --experts 64 --steps 8 --T 1 [--coding vq2a]
+  python bench_diag.py paged --layers 2 --experts 64 --steps 8 --T 1 [--coding vq2a]
       native paged MoE steps (vq2_paged_moe_step) over a pinned synthetic .vq2m image
 
 Each prints one JSON line with the measured device time per launch/layer.
 """
 import argparse
 import json
+import os
+import sys
 
 import torch
 
-from . import kernels, moe, runtime, synth
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from compressai_b200 import kernels, moe, runtime, synth  # noqa: E402
 
 
 def _cbs(dev):
@@ -62,7 +66,7 @@ def cmd_gemv(a):
     lin = runtime.PackedLinear((a.out, a.n), bits, "diag", [torch.from_numpy(i) for i in idx],
                                torch.from_numpy(scale), cbs, dev)
     if a.swiglu:
-        from . import _lib
+        from compressai_b200 import _lib
         x = torch.randn(a.M, 2 * a.n, device=dev)
         cb0, cb1 = lin.codebooks()
         t = _time(lambda: kernels.gemv_multi(x, [lin.mat()], cb0, cb1, rot=lin.rot, mode=_lib.VQ2_ACT_SWIGLU_RHT,
@@ -100,7 +104,7 @@ def cmd_moe(a):
 def cmd_rans(a):
     import numpy as np
 
-    from . import ans, container
+    from compressai_b200 import ans, container
     dev = torch.device("cuda", 0)
     x = np.minimum(np.abs(np.random.default_rng(a.seed).normal(0, 3000, a.n // 2)), 65535).astype(np.uint16)
     enc = torch.from_numpy(ans.encode(x)).to(dev)
@@ -127,7 +131,7 @@ def cmd_paged(a):
 
     import numpy as np
 
-    from . import container, paged_runtime
+    from compressai_b200 import container, paged_runtime
     dev = torch.device("cuda", 0)
     if a.coding == "raw":
         img, _ = container.synthetic_vq2m_image(a.layers, a.experts, seed=a.seed)

@@ -297,7 +297,8 @@ namespace vq2 {
 
 // Device address of g_moe_ffn_scratch for the current device. In host code the symbol names a
 // host-side stand-in, never the device array, so its address must come from
-// cudaGetSymbolAddress, called with the device current; the result is cached per device.
+// cudaGetSymbolAddress, called with the device current; the result is cached per device
+// ordinal (a cudaDeviceReset makes it stale: documented as unsupported after a reset).
 static void* noalloc_scratch(int* status) {
   static std::atomic<void*> cache[64];
   int dev = 0;
@@ -335,10 +336,11 @@ extern "C" int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T,
   int status = VQ2_OK;
   void* ws = vq2::noalloc_scratch(&status);
   if (ws == nullptr) return status;
-  // the static scratch starts zeroed and the fused kernel leaves its counters at zero
+  // always the four-kernel sequence (prefer_fused false): no counters are kept in the scratch
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
-                             scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream), false, true);
+                             scale_mid, ws, out, out_dtype, static_cast<cudaStream_t>(stream), false, false,
+                             nullptr, false);
 }
 
 extern "C" int64_t vq2_moe_layer_workspace(int64_t T, int64_t top_k, int has_shared, int64_t hidden, int64_t gu_rows,

@@ -1,19 +1,22 @@
 """MoE expert path on VQ weights: router, resident expert pool, fused expert FFN.
 
-One MoE layer for T tokens with top-k routing is one C-ABI call (vq2_moe_expert_ffn), three
-launches on the device:
+One MoE layer from router logits is one C-ABI call (``vq2_moe_layer``), three launches:
 
-1. ``vq2_moe_gemv`` gate_up over the T*k (token, expert) problems -- each CTA rotates its
-   token's hidden state (RHT 2048, fp32) in its prologue -- into fp32 [T*k, 1024];
-2. ``vq2_moe_gemv`` down with the SwiGLU and the 512-point RHT fused in its prologue, into fp32
-   [T*k, 2048];
-3. ``vq2_moe_combine``: routing-weighted sum per token in fixed order (+ the shared expert as
-   one more problem when present), cast to the hidden dtype;
+1. the router kernel (one CTA for all T tokens): softmax top-k with renormalised weights, the
+   shared expert's sigmoid gate, the mapping of expert ids to pool rows, the input RHT of every
+   token (written once), and the ordered list of (token, expert) problems;
+2. the gate_up GEMV over those problems, into fp32 [P, 1024];
+3. the down GEMV with SwiGLU + the 512-point RHT in its prologue and the routing-weighted sum of
+   each token's problems in its epilogue (the CTA completing a token's last problem of a row
+   block sums it, in problem order).
 
-plus ``vq2_moe_route`` when the routing comes from logits. The reference runs the same math as
-rot_2048.fwd -> 2-D-grid Triton gate_up -> torch SiLU*up -> rot_512.fwd -> Triton down -> torch
-weighted sum (vq2/paged_runtime.py:491-511; vq2/load_and_test_full_35b.py:53-74), with a Python
-loop over tokens for T > 1 (:512-568 / :75-95).
+The reference runs the same math as rot_2048.fwd -> 2-D-grid Triton gate_up -> torch SiLU*up ->
+rot_512.fwd -> Triton down -> torch weighted sum (vq2/paged_runtime.py:491-511;
+vq2/load_and_test_full_35b.py:53-74), with a Python loop over tokens for T > 1 (:512-568 /
+:75-95), around the transformers router (modeling_qwen3_5_moe.py:762-791).
+
+``expert_ffn`` (vq2_moe_expert_ffn) keeps the form that takes routed ids and weights, as the
+reference's expert modules do (``PackedMoEExpertUniversal.forward``, the paged runtime).
 
 Experts are stored as whole records [gu_idx int16 1024x256 | gu_scale fp16 1024 | dn_idx int16
 2048x64 | dn_scale fp16 2048] (792,576 B), the .vq2m payload layout, so a pool is one
@@ -182,10 +185,52 @@ class PackedMoEExpertUniversal(nn.Module):
                           self.rot_2048, self.rot_512, k)
 
 
+def moe_layer(hidden, logits, pool, cb16, rot_in, rot_mid, top_k=8, shared_gate=None, lo=0, hi=None, rank=0,
+              world=1, out=None, out_dtype=None, peer=None):
+    """One sparse MoE layer from router logits (vq2_moe_layer; vq2_moe_layer_ep with ``peer``).
+
+    hidden [T, H]; logits fp32 [T, E]; pool rows: experts [lo, hi) then, when ``shared_gate``
+    (fp32 [H]) is given, the shared expert; its problem for token t runs on rank t % world.
+    ``peer`` (ep.PeerReduceContext): the combine also sums the ranks' partials over NVLink peer
+    memory. Returns out [T, H] (hidden's dtype unless ``out_dtype``)."""
+    _lib.require_cuda(hidden, logits, cb16, shared_gate)
+    T, H = hidden.shape
+    E = logits.shape[-1]
+    hi = E if hi is None else hi
+    gr, gc, dr, dc = pool.dims
+    if H != rot_in.n or gr // 2 != rot_mid.n or gc * 8 != H:
+        raise ValueError("shape mismatch between hidden, rotations and the expert pool")
+    if cb16.dtype != torch.float16:
+        raise ValueError("the expert pools hold fp16 scales; the codebook must be fp16")
+    h = hidden.contiguous()
+    lg = logits.float().contiguous()
+    g = shared_gate.reshape(-1).float().contiguous() if shared_gate is not None else None
+    out_dtype = out_dtype or hidden.dtype
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=h.device)
+    lib = _lib.load()
+    ws_bytes = lib.vq2_moe_layer_workspace(T, top_k, int(g is not None), H, gr, dr)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=h.device)
+    common = (_lib.ptr(pool.raw), pool.E, gr, gc, dr, dc, _lib.ptr(cb16), _lib.dtype_code(cb16),
+              _lib.ptr(rot_in.perm), _lib.ptr(rot_in.sign), rot_in.hb, float(rot_in.scale),
+              _lib.ptr(rot_mid.perm), _lib.ptr(rot_mid.sign), rot_mid.hb, float(rot_mid.scale),
+              _lib.ptr(ws), ws_bytes)
+    if peer is None:
+        _lib.call("vq2_moe_layer", _lib.ptr(h), _lib.dtype_code(h), T, _lib.ptr(lg), E, top_k, _lib.ptr(g), lo, hi,
+                  rank, world, *common, _lib.ptr(out), _lib.dtype_code(out), _lib.stream_ptr(h.device))
+    else:
+        import ctypes
+        _lib.call("vq2_moe_layer_ep", _lib.ptr(h), _lib.dtype_code(h), T, _lib.ptr(lg), E, top_k, _lib.ptr(g), lo, hi,
+                  *common, ctypes.c_void_p(peer.peers_dev), peer.rank, peer.world, peer.max_tokens,
+                  _lib.ptr(peer.epochs), _lib.ptr(peer.err), _lib.ptr(out), _lib.dtype_code(out),
+                  _lib.stream_ptr(h.device))
+    return out
+
+
 class MoEBlock(nn.Module):
     """Sparse MoE block (Qwen3_5MoeSparseMoeBlock math) on VQ experts: router from logits (or a
     dense router weight), top-k routed experts + the always-on shared expert weighted by
-    sigmoid(shared_gate . h), all resident. Four launches per layer."""
+    sigmoid(shared_gate . h), all resident; one vq2_moe_layer call (three launches) per layer."""
 
     def __init__(self, experts, router_weight=None, shared_gate=None, top_k=8):
         super().__init__()
@@ -195,17 +240,9 @@ class MoEBlock(nn.Module):
         self.top_k = top_k
 
     def forward(self, hidden_states, router_logits=None):
-        T = hidden_states.shape[0]
         if router_logits is None:
             router_logits = torch.nn.functional.linear(hidden_states.to(self.router_weight.dtype), self.router_weight)
-        if self.shared_gate is not None and self.experts.shared:
-            ids, w, sw = route(router_logits, self.top_k, hidden_states, self.shared_gate)
-            ids = torch.cat([ids, torch.full((T, 1), self.experts.num_experts, dtype=torch.int32,
-                                             device=ids.device)], 1)
-            w = torch.cat([w, sw[:, None]], 1)
-            k = self.top_k + 1
-        else:
-            ids, w = route(router_logits, self.top_k)
-            k = self.top_k
         ex = self.experts
-        return expert_ffn(hidden_states, ids.reshape(-1), w, ex.pool, ex.cb16, ex.rot_2048, ex.rot_512, k)
+        gate = self.shared_gate if (self.shared_gate is not None and ex.shared) else None
+        return moe_layer(hidden_states, router_logits, ex.pool, ex.cb16, ex.rot_2048, ex.rot_512, self.top_k,
+                         shared_gate=gate, lo=0, hi=ex.num_experts)

@@ -341,27 +341,41 @@ class PagedModelStore:
 
 
 class LRUExpertCache:
-    """Tuple cache of whole experts keyed by (layer, expert) (vq2/paged_runtime.py:287-313)."""
+    """Whole-expert cache keyed by (layer, expert) with least-recently-used eviction and hit /
+    miss counters: the older cache API of reference vq2/paged_runtime.py:287-313, kept for its
+    callers (the streaming benchmark, the LEGION engine's imports). Recency is the insertion
+    order of a plain dict: a hit moves its key to the end; a miss loads the expert through
+    ``store.get_expert_weights(layer, expert, device=...)``, appends it, and drops keys from the
+    front while more than ``capacity`` experts are held. ``cache`` exposes the entries in
+    recency order (oldest first), as the reference's OrderedDict does."""
 
     def __init__(self, capacity=128, device=DEVICE):
-        self.capacity = capacity
+        if capacity < 0:
+            raise ValueError("capacity must be >= 0")
+        self.capacity = int(capacity)
         self.device = device
-        self.cache = OrderedDict()
+        self.cache = {}
         self.hits = 0
         self.misses = 0
 
+    def __len__(self):
+        return len(self.cache)
+
+    def __contains__(self, key):
+        return tuple(key) in self.cache
+
     def get(self, store, layer_idx, expert_id):
         key = (layer_idx, expert_id)
-        if key in self.cache:
+        entry = self.cache.pop(key, None)
+        if entry is None:
+            self.misses += 1
+            entry = tuple(store.get_expert_weights(layer_idx, expert_id, device=self.device))
+        else:
             self.hits += 1
-            self.cache.move_to_end(key)
-            return self.cache[key]
-        self.misses += 1
-        w = store.get_expert_weights(layer_idx, expert_id, device=self.device)
-        self.cache[key] = w
-        if len(self.cache) > self.capacity:
-            self.cache.popitem(last=False)
-        return w
+        self.cache[key] = entry
+        while len(self.cache) > self.capacity:
+            self.cache.pop(next(iter(self.cache)))
+        return entry
 
 
 class PagedMoEExpert(nn.Module):

@@ -14,7 +14,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import kernels
+from . import _lib, kernels
 from . import vq
 
 RS = vq.HB ** -0.5   # the unnormalised-rotation scale folded into legacy GEMV calls (vq2/runtime.py:66)
@@ -98,13 +98,12 @@ class PackedLinear(nn.Module):
         self.rot = vq.get_rot(tag, self.n, device)
 
     def weight_rows(self, r0, r1):
-        """Rotated-space rows [r0, r1) in the codebook dtype (vq2/runtime.py:82-89)."""
-        rec = None
-        for i, k in enumerate(self.keys):
-            ix = _as_index(getattr(self, f"idx{i}")[r0:r1], self.cfg[i])
-            g = F.embedding(ix, self._cbs[0][k])
-            rec = g if rec is None else rec + g
-        return rec.reshape(r1 - r0, self.n) * self.scale[r0:r1, None]
+        """Rotated-space rows [r0, r1) in the codebook dtype, decoded on the GPU by the row-decode
+        kernel (vq2_embed_rows without the inverse transform): scale[r] * (sum of the stages'
+        codewords), the reference's dequantized rows (vq2/runtime.py:82-89)."""
+        ids = torch.arange(r0, r1, dtype=torch.int64, device=self.idx0.device)
+        cb0, cb1 = self.codebooks()
+        return decode_rows(self, ids, cb0, cb1, inverse=False, out_dtype=cb0.dtype)
 
     def mat(self):
         return (self.idx0, getattr(self, "idx1", None), self.scale)
@@ -181,25 +180,40 @@ class PackedSwiGLUMLP(nn.Module):
         return y.reshape(*lead, d.out)
 
 
-class PackedEmbedding(nn.Module):
-    """Row lookup of a compressed embedding: gather the token rows, decode them in fp32 and
-    inverse-rotate (vq2/runtime.py:116-133)."""
+def decode_rows(lin, ids, cb0, cb1, inverse, out_dtype):
+    """Rows `ids` of PackedLinear `lin`, dequantized on the GPU (vq2_embed_rows): rotated-space
+    rows, or with ``inverse`` the original-space rows Rot.inv(q) (the embedding lookup)."""
+    _lib.require_cuda(ids, cb0, cb1)
+    flat = ids.reshape(-1).to(torch.int64).contiguous()
+    out = torch.empty(flat.numel(), lin.n, dtype=out_dtype, device=flat.device)
+    if flat.numel() == 0:
+        return out.reshape(*ids.shape, lin.n)
+    bad = torch.zeros(1, dtype=torch.int32, device=flat.device)
+    i1 = getattr(lin, "idx1", None)
+    rot = lin.rot if inverse else None
+    _lib.call("vq2_embed_rows", _lib.ptr(flat), flat.numel(), lin.out, _lib.ptr(lin.idx0), _lib.ptr(i1),
+              _lib.ptr(cb0), _lib.ptr(cb1 if i1 is not None else None), _lib.ptr(lin.scale), _lib.dtype_code(cb0),
+              lin.n, _lib.ptr(rot.perm) if rot else None, _lib.ptr(rot.sign) if rot else None,
+              rot.hb if rot else 0, float(rot.scale) if rot else 1.0, _lib.ptr(out), _lib.dtype_code(out),
+              _lib.ptr(bad), _lib.stream_ptr(flat.device))
+    return out.reshape(*ids.shape, lin.n)
 
-    def __init__(self, lin, cbs32):
+
+class PackedEmbedding(nn.Module):
+    """Embedding lookup over a VQ-compressed (tied) embedding matrix: each token's row is decoded
+    on the GPU in fp32 -- codewords, row scale, inverse rotation -- in one kernel launch
+    (vq2_embed_rows), returned in bf16 as the reference does (vq2/runtime.py:116-133). ``cbs32``:
+    the embedding codebooks (the reference passes fp32 copies; the values are those of the
+    stored fp16/bf16 codebooks, which the kernel reads directly)."""
+
+    def __init__(self, lin, cbs32=None, out_dtype=torch.bfloat16):
         super().__init__()
         self.lin = lin
-        self._cb32 = [cbs32]
+        self.out_dtype = out_dtype
 
     def forward(self, ids):
-        flat = ids.reshape(-1)
-        rec = None
-        for i, k in enumerate(self.lin.keys):
-            ix = _as_index(getattr(self.lin, f"idx{i}")[flat], self.lin.cfg[i])
-            g = F.embedding(ix, self._cb32[0][k])
-            rec = g if rec is None else rec + g
-        q = rec.reshape(flat.numel(), self.lin.n) * self.lin.scale[flat].float()[:, None]
-        w = self.lin.rot.inv_f32(q)
-        return w.to(torch.bfloat16).reshape(*ids.shape, self.lin.n)
+        cb0, cb1 = self.lin.codebooks()
+        return decode_rows(self.lin, ids, cb0, cb1, inverse=True, out_dtype=self.out_dtype)
 
 
 class PackedLMHead(nn.Module):
@@ -244,11 +258,25 @@ def unpack_fixed(buf, bits, n):
     raise ValueError(bits)
 
 
-def decode_indices(C):
+def unpack_fixed_gpu(buf, bits, n, device="cuda"):
+    """unpack_fixed on the GPU (vq2_unpack_fixed): a fixed-width stream (host or device uint8) ->
+    a device tensor of n symbols, int16 holding uint16 bits for 12/16-bit streams, uint8 else."""
+    src = torch.as_tensor(buf).reshape(-1).to(device=device, dtype=torch.uint8).contiguous()
+    dt = torch.int16 if bits > 8 else torch.uint8
+    out = torch.empty(n, dtype=dt, device=device)
+    if n:
+        _lib.call("vq2_unpack_fixed", _lib.ptr(src), src.numel(), bits, n, _lib.ptr(out), out.element_size(),
+                  _lib.stream_ptr(torch.device(device)))
+    return out
+
+
+def decode_indices(C, device=None):
     """Container dict -> {name: [index tensor per stage]} (vq2/runtime.py:155-182). Fixed-width
-    streams are unpacked here; ANS streams (coded with the third-party `constriction` package)
-    cannot be decoded without it and raise."""
+    streams are unpacked on the GPU when ``device`` is a CUDA device (vq2_unpack_fixed; the
+    tensors stay there), else on the host; ANS streams (coded with the third-party
+    `constriction` package) cannot be decoded without it and raise."""
     idx = {nm: [None] * len(C["meta"][nm]["cfg"]) for nm in C["names"]}
+    gpu = device is not None and torch.device(device).type == "cuda"
     for key, e in C["streams"].items():
         bits = e["bits"]
         n = int(sum(e["sizes"]))
@@ -256,9 +284,12 @@ def decode_indices(C):
             raise NotImplementedError("ANS-coded .vq2 streams need `constriction`, which is not installed; "
                                       "convert to .vq2r (raw indices) first")
         fx = e["fixed"].numpy() if isinstance(e["fixed"], torch.Tensor) else e["fixed"]
-        sym = unpack_fixed(fx, bits, n)
-        arr = sym.astype(np.uint8) if bits <= 8 else sym.astype(np.uint16).view(np.int16)
-        t_all = torch.from_numpy(np.ascontiguousarray(arr))
+        if gpu:
+            t_all = unpack_fixed_gpu(fx, bits, n, device)
+        else:
+            sym = unpack_fixed(fx, bits, n)
+            arr = sym.astype(np.uint8) if bits <= 8 else sym.astype(np.uint16).view(np.int16)
+            t_all = torch.from_numpy(np.ascontiguousarray(arr))
         owners = [nm for nm in C["names"]
                   if key in [vq.cfg_key(C["meta"][nm]["cfg"], i) for i in range(len(C["meta"][nm]["cfg"]))]]
         off = 0
@@ -270,12 +301,13 @@ def decode_indices(C):
     return idx
 
 
-def read_container(path):
-    """Read a .vq2 (fixed-width streams) or .vq2r (raw indices) dict (vq2/runtime.py:185-193)."""
+def read_container(path, device=None):
+    """Read a .vq2 (fixed-width streams) or .vq2r (raw indices) dict (vq2/runtime.py:185-193);
+    with a CUDA ``device`` the fixed-width streams are unpacked there."""
     C = torch.load(path, weights_only=False)
     if C.get("format") == "vq2r":
         return C
-    idx = decode_indices(C)
+    idx = decode_indices(C, device)
     scales = {nm: (s if isinstance(s, torch.Tensor) else torch.from_numpy(s)) for nm, s in C["scales"].items()}
     return dict(format="vq2r", names=C["names"], meta=C["meta"], idx=idx, scales=scales,
                 codebooks=C["codebooks"], codebooks_embed=C.get("codebooks_embed", C["codebooks"]),
@@ -297,3 +329,58 @@ def build_packed_linears(C, device, cb_dtype=torch.float16):
         m = C["meta"][nm]
         mods[nm] = PackedLinear(m["shape"], m["cfg"], m["tag"], C["idx"][nm], C["scales"][nm], cbs, device)
     return mods
+
+
+def _set_module(model, name, new):
+    parent = model
+    parts = name.split(".")
+    for p in parts[:-1]:
+        parent = getattr(parent, p)
+    setattr(parent, parts[-1], new)
+
+
+@torch.no_grad()
+def load_packed(path, device="cuda", config=None, cb_dtype=torch.float16):
+    """Load a .vq2/.vq2r container into a transformers causal LM whose quantized linears stay
+    compressed on the GPU (vq2/runtime.py:214-246): every name in the container becomes a
+    PackedLinear (an ``embed_tokens`` name a PackedEmbedding, and a tied lm_head a
+    PackedLMHead over the same indices), the ``dense`` tensors are copied in, and the model moves
+    to ``device``. The reference reads the HF config from its model directory; here ``config``
+    is a transformers config, a directory holding one, or None for $VQ2_MODEL_DIR."""
+    from transformers import AutoConfig, AutoModelForCausalLM
+    if config is None:
+        config = os.environ.get("VQ2_MODEL_DIR")
+        if config is None:
+            raise ValueError("load_packed needs the model's config (argument or VQ2_MODEL_DIR)")
+    if isinstance(config, (str, os.PathLike)):
+        config = AutoConfig.from_pretrained(str(config), trust_remote_code=True)
+    C = read_container(path, device)
+    try:
+        from transformers.initialization import no_init_weights
+    except ImportError:  # older transformers
+        from transformers.modeling_utils import no_init_weights
+    with no_init_weights():
+        model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16).eval()
+    for p in model.parameters():
+        p.requires_grad_(False)
+    params = dict(model.named_parameters())
+    for n, v in C.get("dense", {}).items():
+        params[n].data.copy_(v)
+    cbs = {k: v.to(device=device, dtype=cb_dtype).contiguous() for k, v in C["codebooks"].items()}
+    cbs_emb = {k: v.to(device=device, dtype=cb_dtype).contiguous()
+               for k, v in C.get("codebooks_embed", C["codebooks"]).items()}
+    emb = None
+    for nm in C["names"]:
+        m = C["meta"][nm]
+        is_emb = nm.endswith("embed_tokens")
+        pl = PackedLinear(m["shape"], m["cfg"], m["tag"], C["idx"][nm], C["scales"][nm], cbs_emb if is_emb else cbs,
+                          device)
+        C["idx"][nm] = None
+        if is_emb:
+            emb = pl
+            _set_module(model, nm, PackedEmbedding(pl))
+        else:
+            _set_module(model, nm, pl)
+    if emb is not None and getattr(config.get_text_config(), "tie_word_embeddings", True):
+        model.lm_head = PackedLMHead(emb)
+    return model.to(device)

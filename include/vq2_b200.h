@@ -108,6 +108,35 @@ VQ2_API int vq2_gemv_multi(const void* x, int x_dtype, int x_mode, int64_t M, in
                            int64_t workspace_bytes, void* stream);
 
 /*
+ * Row decode of a VQ matrix, one CTA per requested row:
+ *   q[c, :] = scale[ids[c]] * (cb0[idx0[ids[c], g]] (+ cb1[idx1[ids[c], g]]))  for every group g
+ * and, with perm/sign given, out[c, perm[j]] = (blockH_hb(q[c]) * inv_scale)[j] * sign[j] (the
+ * inverse randomized Hadamard transform, inv_scale = hb^-1/2); without them out = q (rotated
+ * space). ids: int64 [count] device; idx0 int16 [rows, n/8], idx1 uint8 or NULL, cb0/cb1/scale
+ * in val_dtype; n % 256 == 0, n <= 8192; out [count, n] in out_dtype. Ids outside [0, rows) give
+ * zero rows and set *bad (device int32) to 1.
+ * Replaces: PackedEmbedding.forward (vq2/runtime.py:116-133: F.embedding of the codebooks, row
+ * scale, Rot.inv, bf16) and the rotated-space rows of PackedLinear.weight_rows (:82-89).
+ */
+VQ2_API int vq2_embed_rows(const int64_t* ids, int64_t count, int64_t rows, const int16_t* idx0,
+                           const uint8_t* idx1, const void* cb0, const void* cb1, const void* scale,
+                           int val_dtype, int64_t n, const int32_t* perm, const int8_t* sign,
+                           int64_t hb, float inv_scale, void* out, int out_dtype, int32_t* bad,
+                           void* stream);
+
+/*
+ * GPU unpack of a fixed-width index stream: n symbols of `bits` (16: little-endian words; 8:
+ * bytes; 4: two per byte, low nibble first; 12: two per 3 bytes, a | b << 12) from src (device,
+ * src_bytes >= vq2_fixed_stream_bytes(bits, n)) into dst (device, n elements of dst_bytes = 2
+ * (uint16 / int16 bits) or 1 (uint8, bits <= 8)).
+ * Replaces: unpack_fixed (vq2/export.py:56-70) on the host inside decode_indices
+ * (vq2/runtime.py:155-182).
+ */
+VQ2_API int64_t vq2_fixed_stream_bytes(int bits, int64_t n);
+VQ2_API int vq2_unpack_fixed(const uint8_t* src, int64_t src_bytes, int bits, int64_t n, void* dst,
+                             int dst_bytes, void* stream);
+
+/*
  * Workspace bytes vq2_gemv_multi / vq2_gemv use for M activation rows of length n (0 for one
  * row; -1 on bad sizes). With n % 128 == 0 and M >= 4 (or M >= 2 when the matrices total
  * >= 16384 rows) the GEMV runs on the tensor cores, its 16-bit activation operand(s) held in the
@@ -336,21 +365,24 @@ VQ2_API int64_t vq2_moe_expert_ffn_workspace(int64_t T, int64_t top_k, int64_t g
 
 /*
  * vq2_moe_expert_ffn without a workspace argument and without allocating anything, for
- * callers that cannot obtain device memory at call time: code that enqueues work while a
- * stream is being captured into a CUDA graph, plugin or real-time interfaces whose enqueue
- * step must not allocate, and hosts reached through an FFI that have no device allocator of
- * their own. No counterpart in the reference (its PyTorch code always allocates).
+ * callers that cannot obtain device memory when they call: plugin or real-time interfaces whose
+ * enqueue step must not allocate (an allocation can block on the device or fail mid-stream),
+ * and hosts reaching the library through an FFI that have no device allocator of their own.
+ * No counterpart in the reference (its PyTorch code always allocates).
  *
  * The intermediates live in a static device array of VQ2_MOE_FFN_NOALLOC_MAX_BYTES inside this
  * library, present on every GPU that loads it until the process exits. Limit: the call is
  * refused with VQ2_ERR_SHAPE when vq2_moe_expert_ffn_workspace(T, top_k, gu_rows, dn_rows)
- * exceeds that size (4 MiB: up to 341 (token, expert) problems at the 35B-A3B shape, e.g.
+ * exceeds that size (4 MiB: up to 340 (token, expert) problems at the 35B-A3B shape, e.g.
  * T = 32 at top-8 plus a shared expert). The first call on a device looks up the array's
- * device address with that device current; make that first call before starting any stream
- * capture. All calls share the array: calls that may run concurrently on the GPU (on streams
- * with no ordering between them) race on it and must be serialized by the caller. Each call
- * overwrites the intermediates in full before reading them; nothing needs clearing.
- * Otherwise identical to vq2_moe_expert_ffn.
+ * device address with that device current and keeps it for the device; make that first call
+ * before starting any stream capture. cudaDeviceReset discards the array with the context, so
+ * after a reset the kept address is stale: do not call this entry point again in that process.
+ * All calls share the array: calls that may run concurrently on the GPU (on streams with no
+ * ordering between them) race on it and must be serialized by the caller. Each call overwrites
+ * the intermediates in full before reading them; nothing needs clearing. It always runs the
+ * four-kernel sequence (compaction, gate_up, down, combine). Otherwise identical to
+ * vq2_moe_expert_ffn.
  */
 #define VQ2_MOE_FFN_NOALLOC_MAX_BYTES (4u * 1024u * 1024u)
 VQ2_API int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, int64_t top_k,

@@ -21,6 +21,12 @@ records the reference's own outputs on seeded inputs:
   (``vq2/paged_runtime.py:415-437``) replayed on a seeded Zipf routing trace.
 * ``vq2m.npz``       -- hashes of the tensors that the reference ``PagedModelStore``
   (``vq2/paged_runtime.py:49-173``) parses out of a small ``.vq2m`` written by this repo's writer.
+* ``lru_cache.npz``  -- hit flags, store loads and final recency order of the reference
+  ``LRUExpertCache`` (``vq2/paged_runtime.py:287-313``) on seeded (layer, expert) sequences.
+* ``fixed.npz``      -- the reference ``pack_fixed`` / ``unpack_fixed`` (``vq2/export.py:39-70``)
+  on seeded symbols (4/8/12/16 bits, odd and even counts), and a small fixed-width ``.vq2``
+  container (``vq2_small.pt``, built in the reference's stream layout) decoded by the reference
+  ``read_container`` (``vq2/runtime.py:155-193``).
 
 Usage:  python tests/golden/make_golden.py [stage ...]
 """
@@ -55,7 +61,8 @@ def ref():
         import vq2.vq as vq
         import vq2.quantize_35b as q35
         import vq2.paged_runtime as pr
-        _REF = dict(vq=vq, q35=q35, pr=pr, tmp=tmp)
+        import vq2.export as ex
+        _REF = dict(vq=vq, q35=q35, pr=pr, ex=ex, tmp=tmp)
     return _REF
 
 
@@ -289,8 +296,93 @@ def stage_vq2m():
     shutil.rmtree(d)
 
 
+LRU_CACHE_CASES = [("c3", 3, 300, 0), ("c16", 16, 600, 1), ("c0", 0, 20, 2)]
+
+
+class _RecordingStore:
+    """Stand-in store: records every expert load and returns small tagged tensors."""
+
+    def __init__(self):
+        self.loads = []
+
+    def get_expert_weights(self, layer_idx, expert_id, device="cpu"):
+        self.loads.append((layer_idx, expert_id))
+        t = torch.tensor([layer_idx, expert_id])
+        return t, t + 1, t + 2, t + 3
+
+
+def stage_lru_cache():
+    pr = ref()["pr"]
+    res = {}
+    for name, cap, n, seed in LRU_CACHE_CASES:
+        rng = np.random.default_rng(seed)
+        keys = np.stack([rng.integers(0, 3, n), np.minimum(rng.zipf(1.3, n), 40)], 1).astype(np.int64)
+        st = _RecordingStore()
+        c = pr.LRUExpertCache(capacity=cap, device="cpu")
+        hits = []
+        for ln, e in keys:
+            h0 = c.hits
+            c.get(st, int(ln), int(e))
+            hits.append(c.hits - h0)
+        res[f"{name}_keys"] = keys
+        res[f"{name}_hits"] = np.array(hits, dtype=np.uint8)
+        res[f"{name}_loads"] = np.array(st.loads, dtype=np.int64).reshape(-1, 2)
+        res[f"{name}_final"] = np.array(list(c.cache.keys()), dtype=np.int64).reshape(-1, 2)
+        res[f"{name}_counters"] = np.array([c.hits, c.misses, cap], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "lru_cache.npz"), **res)
+
+
+SMALL_VQ2 = [("model.layers.0.self_attn.q_proj", (16,), (24, 64), "attn"),
+             ("model.layers.0.mlp.down_proj", (16, 8), (16, 128), "mlp_down"),
+             ("model.layers.1.self_attn.q_proj", (16,), (8, 64), "attn"),
+             ("model.embed_tokens", (16,), (32, 64), "embed")]
+
+
+def stage_fixed():
+    R = ref()
+    ex = R["ex"]
+    res = {}
+    rng = np.random.default_rng(17)
+    for bits in (4, 8, 12, 16):
+        for n in (1, 2, 7, 1000, 1001):
+            sym = rng.integers(0, 1 << bits, n).astype(np.int64)
+            buf = ex.pack_fixed(sym, bits)
+            res[f"b{bits}_n{n}_sym"] = sym
+            res[f"b{bits}_n{n}_buf"] = np.asarray(buf, dtype=np.uint8)
+            res[f"b{bits}_n{n}_out"] = np.asarray(ex.unpack_fixed(np.asarray(buf), bits, n), dtype=np.int64)
+    # a small fixed-width container in the reference's stream layout: one stream per codebook
+    # key, the owners' index arrays concatenated in name order (vq2/export.py:93-131)
+    names = [nm for nm, _, _, _ in SMALL_VQ2]
+    meta, idx, scales = {}, {}, {}
+    for nm, cfg, shape, tag in SMALL_VQ2:
+        meta[nm] = {"shape": list(shape), "cfg": list(cfg), "tag": tag}
+        ng = shape[1] // 8
+        idx[nm] = [rng.integers(0, 1 << 16, (shape[0], ng)).astype(np.int64)]
+        if len(cfg) > 1:
+            idx[nm].append(rng.integers(0, 256, (shape[0], ng)).astype(np.int64))
+        scales[nm] = torch.from_numpy((0.02 * np.exp(0.1 * rng.standard_normal(shape[0]))).astype(np.float16))
+    streams = {}
+    for key, stage, bits in (("16", 0, 16), ("16_8", 1, 8)):
+        owners = [nm for nm in names if len(meta[nm]["cfg"]) > stage]
+        sym = np.concatenate([idx[nm][stage].reshape(-1) for nm in owners])
+        streams[key] = {"bits": bits, "sizes": [int(idx[nm][stage].size) for nm in owners], "mode": "fixed",
+                        "fixed": torch.from_numpy(np.asarray(ex.pack_fixed(sym, bits)))}
+    # placeholder codebooks (index decoding never reads them; full-size ones would bloat the file)
+    cbs = {"16": torch.zeros(4, 8), "16_8": torch.zeros(4, 8)}
+    C = {"names": names, "meta": meta, "streams": streams, "scales": scales, "codebooks": cbs,
+         "codebooks_embed": cbs, "dense": {}}
+    path = os.path.join(HERE, "vq2_small.pt")
+    torch.save(C, path)
+    import vq2.runtime as rt
+    D = rt.read_container(path)
+    for nm in names:
+        for i, t in enumerate(D["idx"][nm]):
+            res[f"ctr_{nm}_{i}"] = t.numpy()
+    np.savez_compressed(os.path.join(HERE, "fixed.npz"), **res)
+
+
 STAGES = dict(codebooks=stage_codebooks, rot=stage_rot, gemv=stage_gemv, moe=stage_moe,
-              lru=stage_lru, vq2m=stage_vq2m)
+              lru=stage_lru, vq2m=stage_vq2m, lru_cache=stage_lru_cache, fixed=stage_fixed)
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())

@@ -137,3 +137,64 @@ def test_promoted_3bit_experts_in_container(tmp_path):
     with pytest.raises(ValueError):   # promoted experts need the residual codebook
         paged_runtime.PagedMoEExpert(1, st, torch.zeros(65536, 8, dtype=torch.float16), capacity=3, device="cpu")
     st.close()
+
+
+# ---------------------------------------------------------------- fixed-width streams, .vq2 read
+@pytest.mark.parametrize("bits", [4, 8, 12, 16])
+@pytest.mark.parametrize("n", [1, 2, 7, 1000, 1001])
+def test_unpack_fixed_matches_reference(bits, n):
+    """runtime.unpack_fixed on the reference's own pack_fixed output equals the reference's
+    unpack_fixed (vq2/export.py:39-70), odd counts included."""
+    from compressai_b200 import runtime
+    d = golden("fixed.npz")
+    out = runtime.unpack_fixed(d[f"b{bits}_n{n}_buf"], bits, n)
+    assert np.array_equal(out, d[f"b{bits}_n{n}_out"])
+    assert np.array_equal(out, d[f"b{bits}_n{n}_sym"])
+
+
+def test_read_container_matches_reference():
+    """read_container / decode_indices on a fixed-width .vq2 built in the reference's stream layout
+    give the reference read_container's index tensors (dtype and bits)."""
+    from compressai_b200 import runtime
+    from tests.conftest import GOLDEN
+    d = golden("fixed.npz")
+    C = runtime.read_container(os.path.join(GOLDEN, "vq2_small.pt"))
+    assert C["format"] == "vq2r"
+    for nm in C["names"]:
+        for i, t in enumerate(C["idx"][nm]):
+            ref = d[f"ctr_{nm}_{i}"]
+            assert t.dtype == (torch.int16 if i == 0 else torch.uint8)
+            assert t.shape == ref.shape and np.array_equal(t.numpy(), ref), (nm, i)
+
+
+# ---------------------------------------------------------------- LRUExpertCache (older API)
+class _RecordingStore:
+    def __init__(self):
+        self.loads = []
+
+    def get_expert_weights(self, layer_idx, expert_id, device="cpu"):
+        self.loads.append((layer_idx, expert_id))
+        t = torch.tensor([layer_idx, expert_id])
+        return t, t + 1, t + 2, t + 3
+
+
+@pytest.mark.parametrize("case", ["c3", "c16", "c0"])
+def test_lru_expert_cache_matches_reference(case):
+    """Hit flags, store loads, counters and the final recency order equal those of the reference
+    LRUExpertCache (vq2/paged_runtime.py:287-313) on the same (layer, expert) sequence."""
+    d = golden("lru_cache.npz")
+    hits_ref, loads_ref = d[f"{case}_hits"], d[f"{case}_loads"]
+    c_hits, c_misses, cap = (int(v) for v in d[f"{case}_counters"])
+    st = _RecordingStore()
+    c = paged_runtime.LRUExpertCache(capacity=cap, device="cpu")
+    hits = []
+    for ln, e in d[f"{case}_keys"]:
+        h0 = c.hits
+        w = c.get(st, int(ln), int(e))
+        assert int(w[0][0]) == ln and int(w[0][1]) == e
+        hits.append(c.hits - h0)
+    assert np.array_equal(np.array(hits, dtype=np.uint8), hits_ref)
+    assert np.array_equal(np.array(st.loads, dtype=np.int64).reshape(-1, 2), loads_ref)
+    assert (c.hits, c.misses) == (c_hits, c_misses)
+    assert np.array_equal(np.array(list(c.cache.keys()), dtype=np.int64).reshape(-1, 2), d[f"{case}_final"])
+    assert len(c) == len(d[f"{case}_final"]) <= cap

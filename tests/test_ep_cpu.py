@@ -1,6 +1,6 @@
 """Expert-parallel host logic on CPU ranks (gloo, world size 2 and 4): partitioning, local id
-mapping, shared expert on rank 0, all_reduce of the partials -- against the single-process
-oracle. The per-rank expert compute is a test stand-in built from the oracle (the product's
+mapping, the shared expert's tokens spread over the ranks (token t on rank t % N), all_reduce of
+the partials -- against the single-process oracle. The per-rank expert compute is a test stand-in built from the oracle (the product's
 compute is the CUDA expert FFN)."""
 import os
 import socket
@@ -60,9 +60,7 @@ def _worker(rank, world, port, results):
         r2048, r512 = O.rot_params("moe_expert_2048", 2048), O.rot_params("moe_expert_512", 512)
         lo, hi = ep.partition(E, world, rank)
         experts = [synth.synth_expert(SEED, e) for e in range(lo, hi)]
-        shared = synth.synth_expert(SEED + 1, 0)
-        if rank == 0:
-            experts.append(shared)
+        experts.append(synth.synth_expert(SEED + 1, 0))   # every rank holds the shared expert
         gate = torch.from_numpy((0.05 * np.random.default_rng(1).standard_normal(2048)).astype(np.float32))
         blk = ep.ExpertParallelMoEBlock(None, None, E, None, None, shared_gate=gate, top_k=K,
                                         ffn=_oracle_ffn_factory(experts, cbs["16"], r2048, r512), router=_router)
@@ -103,3 +101,9 @@ def test_partition_and_local_ids():
     loc, lw = ep.local_problems(ids, w, 8, 16, shared_id=8, shared_w=torch.tensor([0.3, 0.7]))
     assert loc.tolist() == [[-1, -1, 1, 7, 8], [0, -1, -1, 4, 8]]
     assert torch.allclose(lw[:, 4], torch.tensor([0.3, 0.7]))
+    # the shared expert's problem of token t is local on rank t % world only
+    ids3 = torch.tensor([[0, 9], [9, 1], [2, 12]])
+    for rank in range(2):
+        loc, _ = ep.local_problems(ids3, torch.rand(3, 2), 8 * rank, 8 * rank + 8, shared_id=8,
+                                   shared_w=torch.rand(3), rank=rank, world=2)
+        assert loc[:, 2].tolist() == [8 if t % 2 == rank else -1 for t in range(3)]

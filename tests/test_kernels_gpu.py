@@ -390,9 +390,14 @@ def test_lm_head_fused_greedy_argmax(cbs, M, bits, ties):
     got = lin.greedy(x)
     y = torch.empty(M, out, device=DEV, dtype=torch.float32)
     got2 = lin.greedy(x, logits=y)
-    # the fused kernel's own fp32 logits decide; lin(x) may run on tensor cores (another sum order)
+    # the fused kernel's own fp32 logits decide; lin(x) may run on tensor cores (another sum order;
+    # at this height the tcgen05 kernel, whose fp16 activation operand errs by ~2^-12 of each
+    # row's |w| |x|: the three rows scaled x100 are compared through the argmax only)
     assert torch.equal(got, torch.argmax(y, dim=-1)) and torch.equal(got2, got)
-    assert (y - logits).abs().max() <= 1e-3 * logits.abs().max()
+    keep = torch.ones(out, dtype=torch.bool, device=DEV)
+    if ties:
+        keep[[123, 7000, 19999]] = False
+    assert (y - logits)[:, keep].abs().max() <= 1e-3 * logits[:, keep].abs().max()
     assert torch.equal(got, torch.argmax(logits, dim=-1))
     if ties:
         assert (got == 123).all()

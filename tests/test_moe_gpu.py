@@ -99,6 +99,83 @@ def test_moe_block_with_shared_expert(cbs, T):
     assert rel_err(y, ref) < TOL
 
 
+def test_moe_layer_matches_reference_golden(cbs):
+    """vq2_moe_layer (router + experts in one call) on the golden logits reproduces the reference's
+    own routed-expert outputs (no shared expert)."""
+    d = golden("moe.npz")
+    pool = resident_pool(int(d["t1_seed"]), 256)
+    ex = moe.PackedMoEExpertUniversal(pool, cb16_dev(cbs), DEV)
+    for nm in ("t1", "t4"):
+        y = moe.moe_layer(torch.from_numpy(d[f"{nm}_h"]).to(DEV), torch.from_numpy(d[f"{nm}_logits"]).to(DEV),
+                          pool, ex.cb16, ex.rot_2048, ex.rot_512, 8)
+        assert rel_err(y.float().cpu().numpy(), d[f"{nm}_y"]) < TOL, nm
+
+
+@pytest.mark.parametrize("T", [1, 7, 32])
+def test_moe_layer_equals_route_plus_expert_ffn(cbs, T):
+    """The one-call layer (RHT in the router kernel, combine in the down GEMV's epilogue) agrees
+    with route + expert_ffn (RHT in the gate_up prologue, separate combine kernel) to fp32
+    rounding, with and without the shared expert."""
+    shared = synth.synth_expert(98, 0)
+    pool = resident_pool(12, 256, extra=shared)
+    ex = moe.PackedMoEExpertUniversal(pool, cb16_dev(cbs), DEV, shared=True)
+    g = torch.from_numpy((0.05 * np.random.default_rng(5).standard_normal(2048)).astype(np.float32)).to(DEV)
+    h = torch.from_numpy(np.random.default_rng(6 + T).standard_normal((T, 2048)).astype(np.float16)).to(DEV)
+    lg = torch.randn(T, 256, device=DEV)
+    for gate in (None, g):
+        y = moe.moe_layer(h, lg, pool, ex.cb16, ex.rot_2048, ex.rot_512, 8, shared_gate=gate, hi=256,
+                          out_dtype=torch.float32)
+        if gate is None:
+            ids, w = moe.route(lg, 8)
+            k = 8
+        else:
+            ids, w, sw = moe.route(lg, 8, h, gate)
+            ids = torch.cat([ids, torch.full((T, 1), 256, dtype=torch.int32, device=DEV)], 1)
+            w = torch.cat([w, sw[:, None]], 1)
+            k = 9
+        ref = moe.expert_ffn(h, ids.reshape(-1).contiguous(), w, pool, ex.cb16, ex.rot_2048, ex.rot_512, k,
+                             out_dtype=torch.float32)
+        assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("T", [1, 5, 32])
+def test_moe_layer_rank_partials_sum_to_full_layer(cbs, world, T):
+    """Expert parallelism emulated on one GPU: each rank's layer over its expert slice (+ its
+    share of the shared expert's tokens) gives an fp32 partial; tokens with nothing local get zero
+    rows; the partials sum to the single-GPU layer and to the fp64 oracle."""
+    shared = synth.synth_expert(97, 0)
+    full = resident_pool(13, 256, extra=shared)
+    ex = moe.PackedMoEExpertUniversal(full, cb16_dev(cbs), DEV, shared=True)
+    g_np = (0.05 * np.random.default_rng(7).standard_normal(2048)).astype(np.float32)
+    g = torch.from_numpy(g_np).to(DEV)
+    h_np = np.random.default_rng(8 + T).standard_normal((T, 2048)).astype(np.float16)
+    lg_np = np.random.default_rng(9 + T).standard_normal((T, 256)).astype(np.float32)
+    h, lg = torch.from_numpy(h_np).to(DEV), torch.from_numpy(lg_np).to(DEV)
+    whole = moe.moe_layer(h, lg, full, ex.cb16, ex.rot_2048, ex.rot_512, 8, shared_gate=g, hi=256,
+                          out_dtype=torch.float32)
+    parts = []
+    for rank in range(world):
+        lo, hi = rank * 256 // world, (rank + 1) * 256 // world
+        pool = moe.ExpertRecordPool(hi - lo + 1, DEV)
+        pool.raw[: hi - lo].copy_(full.raw[lo:hi])
+        pool.raw[hi - lo].copy_(full.raw[256])
+        parts.append(moe.moe_layer(h, lg, pool, ex.cb16, ex.rot_2048, ex.rot_512, 8, shared_gate=g, lo=lo, hi=hi,
+                                   rank=rank, world=world, out_dtype=torch.float32))
+    total = torch.stack(parts).sum(0)
+    assert rel_err(total.cpu().numpy(), whole.cpu().numpy()) < 1e-5
+    ids, w = O.router_ref(lg_np, 8)
+    if T == 1:  # a rank holding none of the token's experts and not its shared problem returns zeros
+        for rank in range(world):
+            lo, hi = rank * 256 // world, (rank + 1) * 256 // world
+            if rank != 0 and not any(lo <= e < hi for e in ids[0]):
+                assert not parts[rank].abs().any()
+    sw = 1 / (1 + np.exp(-(h_np.astype(np.float64) @ g_np.astype(np.float64))))
+    ref = O.moe_layer_ref(h_np, ids, w, lambda e: synth.synth_expert(13, e), cbs["16"], ROT2048, ROT512,
+                          shared=shared, shared_w=sw)
+    assert rel_err(total.cpu().numpy(), ref) < TOL
+
+
 @pytest.mark.parametrize("mode", ["image_pinned", "offset", "mmap"])
 @pytest.mark.parametrize("T,cap", [(1, 12), (3, 10), (4, 8)])
 def test_paged_experts_outputs_and_lru(cbs, tmp_path, mode, T, cap):
