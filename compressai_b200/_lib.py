@@ -60,12 +60,13 @@ SIGNATURES = {
                                _i64, _f32, _p, _p, _i64, _f32, _p, _p, _i64, _p, _i32, _p],
     "vq2_moe_peer_buffer_bytes": [_i64, _i64, _i64],
     "vq2_moe_expert_ffn_ep": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
-                              _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _p, _i32, _p],
+                              _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _i64, _p, _i32, _p],
     "vq2_moe_layer_workspace": [_i64, _i64, _i32, _i64, _i64, _i64],
     "vq2_moe_layer": [_p, _i32, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p, _i64, _i64, _i64, _i64, _i64,
                       _p, _i32, _p, _p, _i64, _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _p],
     "vq2_moe_layer_ep": [_p, _i32, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32,
-                         _p, _p, _i64, _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _p, _i32, _p],
+                         _p, _p, _i64, _f32, _p, _p, _i64, _f32, _p, _i64, _p, _i32, _i32, _i64, _p, _p, _i64, _p, _i32,
+                         _p],
     "vq2_lru_state_ints": [_i64, _i64],
     "vq2_lru_step": [_p, _p, _i64, _p, _p, _p],
     "vq2_fetch_records": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _p],
@@ -83,7 +84,7 @@ class PagedLayer(ctypes.Structure):
                 ("status", _p), ("stage_turn", _p), ("decode_stream", _p), ("stage_ready", _p), ("stage_free0", _p),
                 ("stage_free1", _p), ("ids_host", _p), ("ids_dev", _p), ("ids_cap", _i64), ("copy_stream", _p),
                 ("copy_done", _p), ("compute_done", _p), ("ids_done", _p)]
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lib = None
 _lock = threading.Lock()

@@ -40,7 +40,7 @@ int sm_count() {
 }
 }  // namespace vq2
 
-extern "C" int vq2_abi_version(void) { return 1; }
+extern "C" int vq2_abi_version(void) { return 2; }
 
 extern "C" int vq2_last_cuda_error(void) { return vq2::g_last_cuda_error.load(); }
 

@@ -145,6 +145,7 @@ struct PeerReduce {
   int64_t part_bytes;     // bytes of one (parity, rank) slot (>= T x H fp32)
   int32_t* epochs;        // local device state {sequence number, finished CTAs}, zero at first use
   int32_t* err;           // optional status word (timeouts)
+  int max_polls;          // polls of a peer flag before giving up (<= 0: about a second)
 };
 int run_combine_peer(const float* y, const float* w, int64_t T, int top_k, int64_t H, const int32_t* ids,
                      int64_t num_experts, const PeerReduce& pr, void* out, int out_dtype, cudaStream_t st);

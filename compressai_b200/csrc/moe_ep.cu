@@ -43,7 +43,8 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
                                                                int T, int K, int H, uint8_t* const* __restrict__ peers,
                                                                int rank, int world, int64_t part_off,
                                                                int64_t slot_bytes, int32_t* __restrict__ state,
-                                                               int32_t* err, void* out, int out_dtype) {
+                                                               int32_t* err, int max_polls, void* out,
+                                                               int out_dtype) {
   __shared__ uint32_t s_e;
   pdl_wait();
   const int b = blockIdx.x, nb = gridDim.x, tid = threadIdx.x;
@@ -80,11 +81,11 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
     for (int q = 0; q < world; ++q) {
       if (q == rank) continue;
       int it = 0;
-      while ((int)(ld_acquire_sys(flags + q * kPeerMaxBlocks + b) - e) < 0 && it < kPeerWaitPolls) {
+      while ((int)(ld_acquire_sys(flags + q * kPeerMaxBlocks + b) - e) < 0 && it < max_polls) {
         if (it >= kPeerTightPolls) __nanosleep(64);
         ++it;
       }
-      if (it == kPeerWaitPolls) ok = false;
+      if (it == max_polls) ok = false;
     }
     if (!ok && err) atomicMax(err, kPeerTimeout);
   }
@@ -135,8 +136,9 @@ int run_combine_peer(const float* y, const float* w, int64_t T, int top_k, int64
   if (!aligned(out, 16) || !aligned(y, 16)) return VQ2_ERR_ALIGN;
   const int64_t nv = T * H / 4;
   const int nb = (int)std::min<int64_t>(kPeerMaxBlocks, std::max<int64_t>(1, (nv + 255) / 256));
+  const int polls = pr.max_polls > 0 ? pr.max_polls : kPeerWaitPolls;
   return launch_kernel(moe_combine_peer_kernel, dim3(nb), dim3(256), 0, st, y, w, ids, num_experts, (int)T, top_k,
-                       (int)H, pr.peers, pr.rank, pr.world, pr.part_off, pr.part_bytes, pr.epochs, pr.err, out,
+                       (int)H, pr.peers, pr.rank, pr.world, pr.part_off, pr.part_bytes, pr.epochs, pr.err, polls, out,
                        out_dtype);
 }
 
@@ -153,8 +155,8 @@ extern "C" int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int6
                                      const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in,
                                      const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid,
                                      void* workspace, int64_t workspace_bytes, void* const* peers_dev, int rank,
-                                     int world, int64_t max_tokens, uint32_t* epochs, int32_t* err, void* out,
-                                     int out_dtype, void* stream) {
+                                     int world, int64_t max_tokens, uint32_t* epochs, int32_t* err,
+                                     int64_t max_polls, void* out, int out_dtype, void* stream) {
   if (T <= 0 || top_k <= 0 || gu_rows <= 0 || dn_rows <= 0 || T > max_tokens) return VQ2_ERR_SHAPE;
   if (workspace_bytes < vq2::moe_ffn_workspace(T * top_k, gu_rows, dn_rows)) return VQ2_ERR_ARG;
   if (!peers_dev || !epochs || world < 2 || world > 64) return VQ2_ERR_ARG;
@@ -166,6 +168,7 @@ extern "C" int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int6
   pr.part_bytes = vq2::peer_slot_bytes(max_tokens, gu_cols * 8);
   pr.epochs = reinterpret_cast<int32_t*>(epochs);
   pr.err = err;
+  pr.max_polls = (int)std::min<int64_t>(std::max<int64_t>(max_polls, 0), INT32_MAX);
   return vq2::moe_expert_ffn(h, h_dtype, T, top_k, ids, w, pool, num_experts, gu_rows, gu_cols, dn_rows, dn_cols,
                              cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
                              scale_mid, workspace, out, out_dtype, static_cast<cudaStream_t>(stream), false, false,
@@ -179,7 +182,7 @@ extern "C" int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const flo
                                 int64_t hb_in, float scale_in, const int32_t* perm_mid, const int8_t* sign_mid,
                                 int64_t hb_mid, float scale_mid, void* workspace, int64_t workspace_bytes,
                                 void* const* peers_dev, int rank, int world, int64_t max_tokens, uint32_t* epochs,
-                                int32_t* err, void* out, int out_dtype, void* stream) {
+                                int32_t* err, int64_t max_polls, void* out, int out_dtype, void* stream) {
   if (T <= 0 || T > max_tokens) return VQ2_ERR_SHAPE;
   if (!peers_dev || !epochs || world < 2 || world > 64) return VQ2_ERR_ARG;
   vq2::PeerReduce pr;
@@ -190,6 +193,7 @@ extern "C" int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const flo
   pr.part_bytes = vq2::peer_slot_bytes(max_tokens, gu_cols * 8);
   pr.epochs = reinterpret_cast<int32_t*>(epochs);
   pr.err = err;
+  pr.max_polls = (int)std::min<int64_t>(std::max<int64_t>(max_polls, 0), INT32_MAX);
   return vq2::moe_layer(h, h_dtype, T, logits, E, top_k, shared_gate, expert_lo, expert_hi, rank, world, pool,
                         pool_rows, gu_rows, gu_cols, dn_rows, dn_cols, cb0, val_dtype, perm_in, sign_in, hb_in,
                         scale_in, perm_mid, sign_mid, hb_mid, scale_mid, workspace, workspace_bytes, out, out_dtype,

@@ -54,35 +54,40 @@ __device__ __forceinline__ void stage_tile(const ActSrc& a, int64_t xoff, int mc
   else stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
 }
 
-// Fused combine after an item of expert-indexed problem o, row block rb (RPC rows) is written:
+// Fused combine (the COMB kernel variants only) after an item of expert-indexed problem o, row
+// block rb (RPC rows) is written:
 // arrival count per (token, row block); the CTA that brings it to the token's problem count sums
 // the token's problems over the block's rows in problem order (the fmaf chain of
 // moe_combine_kernel, so the result is bit-identical) and writes comb_out. Called by all
 // threads of the CTA at the same point of the item sequence.
-__device__ __noinline__ void combine_tail(const GemvArgs& a, int o, int rb, int rpc) {
+__device__ __forceinline__ void combine_tail(const float* __restrict__ comb_w, const int32_t* __restrict__ tstart,
+                                         const int32_t* __restrict__ tcnt, int32_t* ctr,
+                                         const int32_t* __restrict__ prob_map, const float* y, int64_t y_k_stride,
+                                         void* comb_out, int comb_dtype, int comb_ks, int row_blocks, int out, int o,
+                                         int rb, int rpc) {
   __shared__ int s_last;
   __threadfence();  // this thread's output rows are visible GPU-wide before the arrival
   __syncthreads();
-  const int t = o / a.comb_ks;
+  const int t = o / comb_ks;
   if (threadIdx.x == 0) {
-    const int old = atomicAdd(a.comb_ctr + (int64_t)t * a.row_blocks + rb, 1);
-    s_last = (old == a.comb_tcnt[t] - 1) ? 1 : 0;
+    const int old = atomicAdd(ctr + (int64_t)t * row_blocks + rb, 1);
+    s_last = (old == tcnt[t] - 1) ? 1 : 0;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const int r = rb * rpc + (int)threadIdx.x;
-  if ((int)threadIdx.x < rpc && r < a.out) {
-    const int c0 = a.comb_tstart[t], cn = a.comb_tcnt[t];
+  if ((int)threadIdx.x < rpc && r < out) {
+    const int c0 = tstart[t], cn = tcnt[t];
     float s = 0.f;
     for (int c = c0; c < c0 + cn; ++c) {
-      const int oo = a.prob_map ? a.prob_map[c] : c;
-      s = fmaf(a.comb_w[oo], __ldcg(static_cast<const float*>(a.y) + (int64_t)oo * a.y_k_stride + r), s);
+      const int oo = prob_map ? prob_map[c] : c;
+      s = fmaf(comb_w[oo], __ldcg(y + (int64_t)oo * y_k_stride + r), s);
     }
-    const int64_t i = (int64_t)t * a.out + r;
-    if (a.comb_dtype == VQ2_F16) static_cast<__half*>(a.comb_out)[i] = __float2half_rn(s);
-    else if (a.comb_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(a.comb_out)[i] = __float2bfloat16_rn(s);
-    else static_cast<float*>(a.comb_out)[i] = s;
+    const int64_t i = (int64_t)t * out + r;
+    if (comb_dtype == VQ2_F16) static_cast<__half*>(comb_out)[i] = __float2half_rn(s);
+    else if (comb_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(comb_out)[i] = __float2bfloat16_rn(s);
+    else static_cast<float*>(comb_out)[i] = s;
   }
 }
 
@@ -91,7 +96,7 @@ __device__ __noinline__ void combine_tail(const GemvArgs& a, int o, int rb, int 
 template <int RW, bool RES, bool XREG>
 constexpr bool variant_fast_stage() { return !(RES && XREG && RW == 2); }
 
-template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, bool COMB = false>
 __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   static_assert(!XREG || (LPR == 32 && MT == 1), "register activations need one 256-group chunk, M tile 1");
   constexpr int RPL = 32 / LPR;   // rows per warp-load
@@ -364,7 +369,9 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
           if (lane == 0 && mi < mcount && b) atomicMax(a.argmax + m0 + mi, b);
         }
       }
-      if (!multi && a.comb_w != nullptr) combine_tail(a, cur.o, cur.rb, RPC);  // uniform over the CTA
+      if constexpr (COMB)  // uniform over the CTA
+        combine_tail(a.comb_w, a.comb_tstart, a.comb_tcnt, a.comb_ctr, a.prob_map, static_cast<const float*>(a.y),
+                     a.y_k_stride, a.comb_out, a.comb_dtype, a.comb_ks, a.row_blocks, a.out, cur.o, cur.rb, RPC);
     }
     item = nitem;
     chunk = nchunk;
@@ -383,7 +390,7 @@ constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the 
 constexpr int kTcMinRows = 4;           // activation rows from which the tensor-core path is used
 constexpr int64_t kTcTallRows = 16384;  // ...or from 2 rows when the matrices have this many rows
 
-template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV>
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, bool COMB = false>
 static int launch_cfg(GemvArgs a, cudaStream_t st) {
   constexpr int RPC = 8 * RW * (32 / LPR);
   a.mtiles = (a.M + MT - 1) / MT;
@@ -405,7 +412,7 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
                        (variant_fast_stage<RW, RES, XREG>() ? fast_stage_floats(MT, a.n, a.x_mode) : 0)) *
                           sizeof(float) +
                       (RES ? 256 * sizeof(uint4) : 0);
-  auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV>;
+  auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV, COMB>;
   // Per-device one-time attributes: dynamic shared memory opt-in and, for the small-tile
   // variants, a small shared-memory carveout so most of the SM's 256 KB serves as L1.
   static std::atomic<uint64_t> done{0};
@@ -469,6 +476,16 @@ static int launch_lpr(const GemvArgs& a, int64_t total_rows, int lpr, int mt, cu
   }
 }
 
+template <int RW, typename TV>
+static int launch_comb(const GemvArgs& a, int lpr, cudaStream_t st) {
+  switch (lpr) {
+    case 4: return launch_cfg<4, RW, 1, false, false, TV, true>(a, st);
+    case 8: return launch_cfg<8, RW, 1, false, false, TV, true>(a, st);
+    case 16: return launch_cfg<16, RW, 1, false, false, TV, true>(a, st);
+    default: return launch_cfg<32, RW, 1, false, false, TV, true>(a, st);
+  }
+}
+
 // Largest M tile (1, 2, 4, 8) whose fp32 activation tile fits kMaxXsBytes of shared memory.
 static int pick_mt(int64_t M, int64_t n) {
   int mt = M >= 8 ? 8 : M >= 4 ? 4 : M >= 2 ? 2 : 1;
@@ -510,6 +527,15 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
     if (r != -1) return r;
     r = run_gemm_tc(a, res, val_dtype, ws, st);
     if (r != -1) return r;
+  }
+  if (a.comb_w != nullptr) {  // fused combine: expert-indexed, 2 bpw, one activation row (MoE down)
+    if (a.nprob > 0 || res || a.M != 1 || a.argmax) return VQ2_ERR_ARG;
+    // two rows per warp once the rows fill every SM's warps twice over (as launch_rw chooses)
+    const bool rw2 = total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / lpr);
+    if (val_dtype == VQ2_F16) return rw2 ? launch_comb<2, __half>(a, lpr, st) : launch_comb<1, __half>(a, lpr, st);
+    if (val_dtype == VQ2_BF16)
+      return rw2 ? launch_comb<2, __nv_bfloat16>(a, lpr, st) : launch_comb<1, __nv_bfloat16>(a, lpr, st);
+    return VQ2_ERR_DTYPE;
   }
   const int mt = pick_mt(a.M, a.n);
   if (val_dtype == VQ2_F16)

@@ -32,11 +32,12 @@ class PeerReduceContext:
     local epochs and status word of vq2_moe_expert_ffn_ep; one per (group, device), shared by
     all layers (their calls are ordered on one stream)."""
 
-    def __init__(self, group, device, max_tokens, hidden):
+    def __init__(self, group, device, max_tokens, hidden, max_polls=0):
         import torch.distributed._symmetric_memory as symm_mem
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.max_tokens, self.hidden = max_tokens, hidden
+        self.max_polls = max_polls   # polls of a peer's flag before a wait gives up (0: about a second)
         lib = _lib.load()
         nbytes = lib.vq2_moe_peer_buffer_bytes(max_tokens, hidden, self.world)
         if nbytes < 0:

@@ -166,8 +166,10 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
             raise ValueError("residual indices must be uint8 [out, n/8]")
         i0s.append(_c(i0)); i1s.append(_c(i1)); scs.append(_c(sc)); outs.append(i0.shape[0])
     out_dtype = out_dtype or cb0.dtype
+    lead = x.shape[:-1]
+    shaped = ys is None
     if ys is None:
-        ys = [torch.empty(*x.shape[:-1], o, dtype=out_dtype, device=x.device) for o in outs]
+        ys = [torch.empty(M, o, dtype=out_dtype, device=x.device) for o in outs]
         y_row_stride = None
     if y_row_stride is None:
         if M > 1 and len(set(outs)) > 1:
@@ -191,6 +193,8 @@ def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=No
               _lib.ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), _lib.dtype_code(ys[0]),
               int(y_row_stride), n, float(rs), _lib.ptr(ws), ws.numel() if ws is not None else 0,
               _lib.stream_ptr(x.device))
+    if shaped:
+        ys = [y.reshape(*lead, y.shape[-1]) for y in ys]
     return ys
 
 

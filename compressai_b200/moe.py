@@ -222,7 +222,8 @@ def moe_layer(hidden, logits, pool, cb16, rot_in, rot_mid, top_k=8, shared_gate=
         import ctypes
         _lib.call("vq2_moe_layer_ep", _lib.ptr(h), _lib.dtype_code(h), T, _lib.ptr(lg), E, top_k, _lib.ptr(g), lo, hi,
                   *common, ctypes.c_void_p(peer.peers_dev), peer.rank, peer.world, peer.max_tokens,
-                  _lib.ptr(peer.epochs), _lib.ptr(peer.err), _lib.ptr(out), _lib.dtype_code(out),
+                  _lib.ptr(peer.epochs), _lib.ptr(peer.err), int(getattr(peer, "max_polls", 0)), _lib.ptr(out),
+                  _lib.dtype_code(out),
                   _lib.stream_ptr(h.device))
     return out
 

@@ -326,7 +326,8 @@ VQ2_API int vq2_moe_layer(const void* h, int h_dtype, int64_t T, const float* lo
  * bytes, zeroed before first use); epochs: local device uint32 [2] (sequence number, finished
  * CTAs), zeroed before first use.
  * Every rank must make the same sequence of calls (T <= max_tokens); a wait for a peer that
- * gives up (about a second) raises *err (code 0x200). The output is identical on every rank.
+ * gives up (after max_polls polls of its flag; <= 0: about a second) raises *err (code 0x200)
+ * and the kernel finishes with what it has. The output is identical on every rank.
  */
 VQ2_API int64_t vq2_moe_peer_buffer_bytes(int64_t max_tokens, int64_t hidden, int64_t world);
 VQ2_API int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int64_t top_k,
@@ -338,7 +339,7 @@ VQ2_API int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int64_t
                                   int64_t hb_mid, float scale_mid, void* workspace,
                                   int64_t workspace_bytes, void* const* peers_dev, int rank,
                                   int world, int64_t max_tokens, uint32_t* epochs, int32_t* err,
-                                  void* out, int out_dtype, void* stream);
+                                  int64_t max_polls, void* out, int out_dtype, void* stream);
 
 /*
  * Expert-parallel vq2_moe_layer: the same route / gate_up / down sequence on this rank's
@@ -356,7 +357,8 @@ VQ2_API int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const float*
                              const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid,
                              float scale_mid, void* workspace, int64_t workspace_bytes,
                              void* const* peers_dev, int rank, int world, int64_t max_tokens,
-                             uint32_t* epochs, int32_t* err, void* out, int out_dtype,
+                             uint32_t* epochs, int32_t* err, int64_t max_polls, void* out,
+                             int out_dtype,
                              void* stream);
 
 /* Workspace bytes vq2_moe_expert_ffn needs for T tokens x top_k experts (-1 on bad sizes). */

@@ -107,3 +107,45 @@ def test_partition_and_local_ids():
         loc, _ = ep.local_problems(ids3, torch.rand(3, 2), 8 * rank, 8 * rank + 8, shared_id=8,
                                    shared_w=torch.rand(3), rank=rank, world=2)
         assert loc[:, 2].tolist() == [8 if t % 2 == rank else -1 for t in range(3)]
+
+
+# ------------------------------------------------------------------------ a rank that leaves
+def _leaving_worker(rank, world, port, results):
+    """Step 0 runs on every rank; then the last rank leaves between steps (no collective of its
+    in flight) and the others' next all_reduce must end with an error within the group timeout."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    cbs = _cbs()
+    r2048, r512 = O.rot_params("moe_expert_2048", 2048), O.rot_params("moe_expert_512", 512)
+    lo, hi = ep.partition(E, world, rank)
+    experts = [synth.synth_expert(SEED, e) for e in range(lo, hi)]
+    blk = ep.ExpertParallelMoEBlock(None, None, E, None, None, top_k=K,
+                                    ffn=_oracle_ffn_factory(experts, cbs["16"], r2048, r512), router=_router)
+    h = torch.from_numpy(np.random.default_rng(2).standard_normal((1, 2048)).astype(np.float32))
+    lg = torch.from_numpy(np.random.default_rng(3).standard_normal((1, E)).astype(np.float32))
+    blk(h, lg)
+    if rank == world - 1:
+        results[rank] = "left"
+        return  # leaves without destroying the group: its peers must notice on their own
+    t0 = time.time()
+    try:
+        blk(h, lg)
+        results[rank] = "no error"
+    except Exception as exc:  # gloo reports the lost peer / the timeout as a RuntimeError
+        results[rank] = (type(exc).__name__, round(time.time() - t0, 1))
+
+
+def test_rank_leaving_between_steps_is_detected_by_the_others():
+    world = 4
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_leaving_worker, args=(world, _free_port(), results), nprocs=world, join=True,
+                       start_method="spawn")
+    assert results[world - 1] == "left"
+    for r in range(world - 1):
+        res = results[r]
+        assert isinstance(res, tuple), (r, res)
+        assert res[1] < 30, (r, res)   # ended by the error, not by hanging
