@@ -104,10 +104,11 @@ def _ids32(ids):
     return ids.contiguous()
 
 
-def gemv_argmax(x, mat, cb0, cb1=None, rot=None, mode=None, rs=1.0, y=None):
+def gemv_argmax(x, mat, cb0, cb1=None, rot=None, mode=None, rs=1.0, y=None, keys=False):
     """Greedy argmax over the rows of one VQ matrix, fused into its GEMV (vq2_gemv_argmax):
     returns int64 [M] row indices (ties to the smaller row); with ``y`` (a [M, out] tensor) the
-    logits are written too. M <= 64."""
+    logits are written too; with ``keys`` the raw 64-bit (value, row) keys are returned instead
+    (for a cross-rank maximum). M <= 64."""
     i0, i1, sc = mat
     _lib.require_cuda(x, i0, i1, sc, cb0, cb1)
     if mode is None:
@@ -129,7 +130,7 @@ def gemv_argmax(x, mat, cb0, cb1=None, rot=None, mode=None, rs=1.0, y=None):
               _lib.ptr(cb1) if i1 is not None else None, _lib.ptr(sc), _lib.dtype_code(cb0), out, n,
               float(rs), _lib.ptr(y) if y is not None else None, _lib.dtype_code(y) if y is not None else 0, out,
               _lib.ptr(best), _lib.stream_ptr(x.device))
-    return 0xFFFFFFFF - (best & 0xFFFFFFFF)
+    return best if keys else 0xFFFFFFFF - (best & 0xFFFFFFFF)
 
 
 def gemv_multi(x, mats, cb0, cb1=None, rot=None, mode=None, rs=1.0, out_dtype=None, ys=None, y_row_stride=None):

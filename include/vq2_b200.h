@@ -319,6 +319,27 @@ VQ2_API int vq2_moe_layer(const void* h, int h_dtype, int64_t T, const float* lo
                           int out_dtype, void* stream);
 
 /*
+ * One small exchange among the ranks of a node over NVLink peer memory, one kernel (the
+ * row-sharded lm_head's all-gather of hidden states and its cross-rank argmax):
+ *   mode 0 (gather): dst = concat over ranks of each rank's `bytes` from src (rank order);
+ *   mode 1 (argmax keys): src holds bytes/8 greedy keys of this rank's rows (as written by
+ *     vq2_gemv_argmax); they are rebased to global rows (+ row_offset) and dst receives the
+ *     elementwise maximum over ranks (global argmax, ties to the smaller row).
+ * peers_dev: device array of `world` addresses of identical buffers of
+ * vq2_peer_exchange_buffer_bytes(max_bytes, world) bytes (one per rank, peer-mapped, zeroed
+ * before first use); state: local device int32 [1], zeroed before first use. bytes % 8 == 0,
+ * bytes <= max_bytes. Every rank makes the same calls; a wait for a peer that gives up (after
+ * max_polls polls; <= 0: about a second) raises *err (0x400) and the kernel uses what it has.
+ * No counterpart in the reference (single GPU only); replaces the all_gather of logits or a
+ * (max, idx) all-reduce of a row-sharded PackedLMHead (vq2/runtime.py:136-144).
+ */
+VQ2_API int64_t vq2_peer_exchange_buffer_bytes(int64_t max_bytes, int64_t world);
+VQ2_API int vq2_peer_exchange(const void* src, int64_t bytes, int mode, int64_t row_offset,
+                              void* const* peers_dev, int rank, int world, int64_t max_bytes,
+                              int32_t* state, int32_t* err, int64_t max_polls, void* dst,
+                              void* stream);
+
+/*
  * Expert-parallel vq2_moe_expert_ffn whose combine also sums over the ranks of a group, in one
  * kernel over NVLink peer memory (instead of combine -> NCCL all_reduce -> cast). ids: this
  * rank's local pool rows (-1 for experts of other ranks). peers_dev: device array of `world`

@@ -79,7 +79,24 @@ def _worker(rank, world, port, results):
         graph_equal = bool(torch.equal(x, eager))
         blk.peer.check()
         del g
-        results[rank] = (out, graph_equal)
+        # row-sharded greedy lm_head: every rank gets the full matrix's greedy ids of every rank's token
+        from compressai_b200 import runtime, shard
+        V, n = 20000, 2048
+        idx, scale = synth.random_matrix(123, V, n)
+        cbd = {"16": cb}
+        full = runtime.PackedLinear((V, n), (16,), "lm_head", [torch.from_numpy(idx[0])], torch.from_numpy(scale),
+                                    cbd, dev)
+        lo, hi = shard.shard_rows(V, world, rank)
+        sh = runtime.PackedLinear((hi - lo, n), (16,), "lm_head", [torch.from_numpy(idx[0][lo:hi])],
+                                  torch.from_numpy(scale[lo:hi]), cbd, dev)
+        ex = shard.PeerExchange(None, dev, max_bytes=4 * n * 2)
+        head = shard.ShardedLMHead(sh, lo, V, ex)
+        xs = torch.from_numpy(np.random.default_rng(77).standard_normal((world, 2, n)).astype(np.float16)).to(dev)
+        ids = head.greedy(xs[rank])
+        want = full.greedy(xs.reshape(-1, n)).reshape(world, 2)
+        ex.check()
+        sharded_ok = bool(torch.equal(ids, want))
+        results[rank] = (out, graph_equal, sharded_ok)
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
@@ -94,7 +111,8 @@ def test_expert_parallel_matches_single_gpu():
     results = mgr.dict()
     mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, join=True, start_method="spawn")
     for r in range(world):
-        out, graph_equal = results[r]
+        out, graph_equal, sharded_ok = results[r]
+        assert sharded_ok, r
         for t_, (err_peer, err_nccl, _) in out.items():
             assert err_peer < 2e-3 and err_nccl < 2e-3, (r, t_, err_peer, err_nccl)  # fp16 outputs
         assert graph_equal, r
