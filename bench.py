@@ -523,6 +523,85 @@ def run_moe(args, dev, dist, world, steps, warmup, tokens=MOE_TOKENS):
     return summary
 
 
+# ------------------------------------------------------------------------------ config 5 stack
+def run_stack(args, dev, dist, world, batches=(1, 8, 64)):
+    """the 35B-A3B-shaped Qwen3.5-MoE text model (40 layers: 30 Gated-DeltaNet
+    + 10 full-attention, hidden 2048, 256 experts + 1 shared, top-8, expert inter 512, vocab
+    248320), random-init, every linear VQ 2 bpw, attention / DeltaNet / norms the transformers
+    modules (torch fallback path: no fla / causal-conv1d kernels in the image), the MoE blocks
+    on this library's kernels -- expert-parallel across the N ranks at N > 1 (every rank runs
+    the same batch; experts split; rank sum over NVLink peer memory). Greedy decode through the
+    HF cache, eager (no graph); tokens/s of the whole group."""
+    from compressai_b200 import stack
+    group = dist.group.WORLD if dist is not None else None
+    t0 = time.perf_counter()
+    model = stack.build_vq2_moe_model(None, dev, seed=11, group=group, max_tokens=max(batches))
+    build_s = time.perf_counter() - t0
+    res = {"model": "Qwen3.5-MoE 35B-A3B shape, random-init, VQ 2 bpw", "build_s": round(build_s, 1),
+           "parallelism": f"expert-parallel x{world}" if world > 1 else "single GPU", "per_batch": []}
+    for B in batches:
+        barrier(dist)
+        t, ids = stack.decode(model, batch=B, prompt_len=4, steps=args.stack_steps, warmup=2, seed=B)
+        t = max_over_ranks(t, dist)
+        entry = {"batch": B, "ms_per_step": round(t * 1e3, 3), "tok_s": round(B / t, 2)}
+        if world > 1:
+            allv = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(allv, ids.contiguous())
+            entry["ranks_identical"] = all(bool(torch.equal(allv[0], v)) for v in allv[1:])
+        res["per_batch"].append(entry)
+    del model
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------------ row-sharded lm_head (N > 1)
+def run_sharded_head(args, dev, dist, world):
+    """Greedy lm_head (151936 x 2048, 2 bpw) for one token per rank: every rank running the full
+    matrix on its own token (replicas) against the row-sharded head (all-gather of the N hidden
+    rows over peer memory, the fused-argmax GEMV over this rank's V/N rows for all N tokens, the
+    cross-rank key maximum). Both in CUDA graphs; ids checked against the full matrix."""
+    from compressai_b200 import runtime, shard, synth
+    rank = dist.get_rank()
+    g = torch.Generator(device=dev).manual_seed(77)          # the same matrix on every rank
+    cbs = {k: torch.from_numpy(v).to(dev) for k, v in synth.random_codebooks(1).items()}
+    idx = torch.randint(-32768, 32768, (VOCAB, HIDDEN // 8), generator=g, device=dev, dtype=torch.int16)
+    scale = (0.02 * torch.exp(0.1 * torch.randn(VOCAB, generator=g, device=dev))).half()
+    full = runtime.PackedLinear((VOCAB, HIDDEN), (16,), "lm_head", [idx], scale, cbs, dev)
+    lo, hi = shard.shard_rows(VOCAB, world, rank)
+    sh = runtime.PackedLinear((hi - lo, HIDDEN), (16,), "lm_head", [idx[lo:hi].clone()], scale[lo:hi].clone(), cbs,
+                              dev)
+    ex = shard.PeerExchange(None, dev, max_bytes=8 * HIDDEN * 2)
+    head = shard.ShardedLMHead(sh, lo, VOCAB, ex)
+    gx = torch.Generator(device=dev).manual_seed(5)
+    xs = torch.randn(world, 1, HIDDEN, generator=gx, device=dev).half()   # every rank's token, known to all
+    x = xs[rank].clone()
+    stream = torch.cuda.Stream(dev)
+    res = {"vocab": VOCAB, "rows_per_rank": hi - lo}
+    for name, fn in (("replicated", lambda: full.greedy(x)), ("sharded", lambda: head.greedy(x))):
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            out = fn()
+        barrier(dist)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                gr.replay()
+        barrier(dist)
+        t = max_over_ranks(time_graph(gr, args.steps, stream), dist)
+        res[f"us_{name}"] = round(t / args.steps * 1e6, 2)
+        if name == "sharded":
+            want = full.greedy(xs.reshape(world, HIDDEN))
+            res["ids_equal_full_matrix"] = bool(torch.equal(out.reshape(-1), want))
+        del gr
+    res["tok_s_replicated"] = round(world / (res["us_replicated"] * 1e-6), 1)
+    res["tok_s_sharded"] = round(world / (res["us_sharded"] * 1e-6), 1)
+    ex.check()
+    return res
+
+
 # ------------------------------------------------------------------------------ paging (config 4)
 def run_paged(args, dev, coding="raw"):
     """40 MoE layers x 256 experts in a pinned host .vq2m image (8.12 GB raw); one PagedMoEExpert
@@ -753,6 +832,8 @@ def main():
     ap.add_argument("--paged-steps", type=int, default=512)
     ap.add_argument("--dense-only", action="store_true")
     ap.add_argument("--sweep-json", default=None, help="write the full config-2 sweep here")
+    ap.add_argument("--stack-steps", type=int, default=6, help="timed decode steps of the config-5 stack")
+    ap.add_argument("--no-stack", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -792,6 +873,10 @@ def main():
                         json.dump(sweep, f, indent=1)
                 res["paged"] = run_paged(args, dev)
                 res["paged_ans"] = run_paged(args, dev, coding="vq2a")
+            if world > 1:
+                res["lm_head_sharded"] = run_sharded_head(args, dev, dist, world)
+            if not args.no_stack:
+                res["stack35b"] = run_stack(args, dev, dist, world)
             res["moe"] = run_moe(args, dev, dist, world, args.steps, args.warmup)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)

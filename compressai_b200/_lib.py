@@ -36,6 +36,7 @@ SIGNATURES = {
                        _i32, _i64, _i64, _f32, _p, _i64, _p],
     "vq2_gemv_workspace": [_i64, _i64],
     "vq2_tc_status": [_i32],
+    "vq2_router_logits": [_p, _i32, _i64, _p, _i32, _i64, _i64, _p, _p],
     "vq2_peer_exchange_buffer_bytes": [_i64, _i64],
     "vq2_peer_exchange": [_p, _i64, _i32, _i64, _p, _i32, _i32, _i64, _p, _p, _i64, _p, _p],
     "vq2_fixed_stream_bytes": [_i32, _i64],

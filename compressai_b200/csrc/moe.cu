@@ -335,3 +335,57 @@ extern "C" int vq2_moe_route(const float* logits, int64_t T, int64_t E, int64_t 
   r.ids = ids; r.w = w; r.ks = (int)K; r.shared_w = shared_w; r.layer = false;
   return run_route(r, static_cast<cudaStream_t>(stream));
 }
+
+// ---- router logits ------------------------------------------------------------------------
+// logits[t, e] = sum_i h[t, i] * W[e, i] with the dense router weight W [E, H] (bf16 or fp16, as
+// the reference keeps it unquantized), fp32 accumulation: one warp per expert, 16-byte loads of
+// the weight row (L1-resident across tokens) and of each token's hidden row, a shuffle reduction.
+// Replaces the F.linear of Qwen3_5MoeTopKRouter.forward (modeling_qwen3_5_moe.py:762-764).
+namespace vq2 {
+__device__ __forceinline__ void load8(const void* p, int dtype, int64_t off, float (&f)[8]) {
+  if (dtype == VQ2_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + off);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + off + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else if (dtype == VQ2_F16) {
+    decode8<__half>(*reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + off), f);
+  } else {
+    decode8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + off), f);
+  }
+}
+
+__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ h, int h_dtype,
+                                                            const void* __restrict__ W, int w_dtype, int T, int E,
+                                                            int H, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_wait();
+  if (e >= E) return;
+  const int nc = H >> 3;
+  for (int t = 0; t < T; ++t) {
+    float acc = 0.f;
+    for (int c = lane; c < nc; c += 32) {
+      float w[8], x[8];
+      load8(W, w_dtype, (int64_t)e * H + 8 * c, w);
+      load8(h, h_dtype, (int64_t)t * H + 8 * c, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(w[i], x[i], acc);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) out[(int64_t)t * E + e] = acc;
+  }
+}
+}  // namespace vq2
+
+extern "C" int vq2_router_logits(const void* h, int h_dtype, int64_t T, const void* W, int w_dtype, int64_t E,
+                                 int64_t H, float* logits, void* stream) {
+  using namespace vq2;
+  if (!h || !W || !logits) return VQ2_ERR_ARG;
+  if (T <= 0 || T > (1 << 20) || E <= 0 || E > (1 << 20) || H <= 0 || H % 8 != 0 || H > (1 << 24)) return VQ2_ERR_SHAPE;
+  if (h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (w_dtype != VQ2_F16 && w_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (!aligned(h, 16) || !aligned(W, 16)) return VQ2_ERR_ALIGN;
+  return launch_kernel(router_logits_kernel, dim3((unsigned)((E + 7) / 8)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), h, h_dtype, W, w_dtype, (int)T, (int)E, (int)H, logits);
+}

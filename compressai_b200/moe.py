@@ -228,6 +228,21 @@ def moe_layer(hidden, logits, pool, cb16, rot_in, rot_mid, top_k=8, shared_gate=
     return out
 
 
+def router_logits_fn(hidden, weight, out=None):
+    """logits fp32 [T, E] = hidden [T, H] . weight [E, H]^T with the dense router weight
+    (vq2_router_logits; Qwen3_5MoeTopKRouter's F.linear)."""
+    _lib.require_cuda(hidden, weight)
+    h = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+    w = weight.contiguous()
+    T, H = h.shape
+    E = w.shape[0]
+    if out is None:
+        out = torch.empty(T, E, dtype=torch.float32, device=h.device)
+    _lib.call("vq2_router_logits", _lib.ptr(h), _lib.dtype_code(h), T, _lib.ptr(w), _lib.dtype_code(w), E, H,
+              _lib.ptr(out), _lib.stream_ptr(h.device))
+    return out
+
+
 class MoEBlock(nn.Module):
     """Sparse MoE block (Qwen3_5MoeSparseMoeBlock math) on VQ experts: router from logits (or a
     dense router weight), top-k routed experts + the always-on shared expert weighted by
@@ -242,7 +257,7 @@ class MoEBlock(nn.Module):
 
     def forward(self, hidden_states, router_logits=None):
         if router_logits is None:
-            router_logits = torch.nn.functional.linear(hidden_states.to(self.router_weight.dtype), self.router_weight)
+            router_logits = router_logits_fn(hidden_states, self.router_weight)
         ex = self.experts
         gate = self.shared_gate if (self.shared_gate is not None and ex.shared) else None
         return moe_layer(hidden_states, router_logits, ex.pool, ex.cb16, ex.rot_2048, ex.rot_512, self.top_k,

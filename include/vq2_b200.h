@@ -287,6 +287,16 @@ VQ2_API int vq2_moe_expert_ffn_res(const void* h, int h_dtype, int64_t T, int64_
                                    int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
 /*
+ * Router logits with the dense (unquantized) router weight: logits[t, e] = sum_i h[t, i] W[e, i],
+ * fp32 accumulation. h: [T, H] in h_dtype; W: [E, H] in w_dtype (fp16/bf16); logits fp32
+ * [T, E]; H % 8 == 0, h and W 16-byte aligned (rows of 16-byte multiples).
+ * Replaces: the F.linear of Qwen3_5MoeTopKRouter.forward (installed transformers
+ * modeling_qwen3_5_moe.py:762-764); the reference keeps the router dense (vq2/quantize_35b.py:139).
+ */
+VQ2_API int vq2_router_logits(const void* h, int h_dtype, int64_t T, const void* W, int w_dtype, int64_t E,
+                              int64_t H, float* logits, void* stream);
+
+/*
  * One sparse MoE layer from router logits, three launches on `stream`:
  *   1. one CTA: router (softmax over E, top_k by logit with ties to the lower id, weights
  *      renormalised over the selected), the shared expert's sigmoid gate, the mapping of expert
