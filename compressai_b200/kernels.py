@@ -28,6 +28,21 @@ HAVE_CUDA_KERNELS = HAVE_TRITON
 FUSED_KERNELS_ENABLED = True
 
 
+def patch_transformers_kernels():
+    """Kept so the reference's callers import unchanged (vq2/kernels.py:572): the reference swaps
+    its Triton kernels into the transformers attention / DeltaNet / norm blocks here. Those blocks
+    are outside this library's decode path (they run as the transformers modules), so this leaves
+    them untouched and returns False."""
+    return False
+
+
+def optimize_deltanet_layers(model):
+    """Kept for import compatibility (vq2/kernels.py:443): the reference fuses the DeltaNet input
+    projections for its Triton path; with VQ weights those projections are PackedLinear modules
+    already, so the model is returned unchanged."""
+    return model
+
+
 def set_fused_kernels_enabled(enabled: bool):
     """Kept for API compatibility (vq2/kernels.py:16-20); the CUDA kernels are always used."""
     global FUSED_KERNELS_ENABLED

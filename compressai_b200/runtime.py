@@ -384,3 +384,17 @@ def load_packed(path, device="cuda", config=None, cb_dtype=torch.float16):
     if emb is not None and getattr(config.get_text_config(), "tie_word_embeddings", True):
         model.lm_head = PackedLMHead(emb)
     return model.to(device)
+
+
+def packed_bytes(model):
+    """Bytes of the compressed weights (PackedLinear buffers) held by ``model``."""
+    return sum(m.nbytes() for m in model.modules() if isinstance(m, PackedLinear))
+
+
+def report_memory(model, tag=""):
+    """Print allocated / peak device memory and the packed weight bytes (vq2/runtime.py:258-263)."""
+    if not torch.cuda.is_available():
+        return
+    torch.cuda.synchronize()
+    print(f"[mem{tag}] allocated {torch.cuda.memory_allocated() / 2**20:.0f} MiB | peak "
+          f"{torch.cuda.max_memory_allocated() / 2**20:.0f} MiB | packed weights {packed_bytes(model) / 2**20:.0f} MiB")
