@@ -482,7 +482,9 @@ def run_moe(args, dev, dist, world, steps, warmup, tokens=MOE_TOKENS):
         e1.synchronize()
         t = max_over_ranks(e0.elapsed_time(e1) / 1e3, dist)
         ach = sbytes * steps / t / 1e9
-        per_layer = 4 if (world > 1 and blocks[0].reduce_kind == "peer") else 3
+        # router kernel, gate_up, down (+ the peer combine at N > 1, or the separate combine kernel
+        # above 64 (token, expert) problems)
+        per_layer = 4 if (world > 1 and blocks[0].reduce_kind == "peer") or T * 9 > 64 else 3
         res = {"T": T, "tok_s": round(T * steps / t, 2), "ms_per_step": round(t / steps * 1e3, 4),
                "us_per_layer": round(t / steps / L * 1e6, 2), "distinct_experts_per_layer": round(distinct / L, 2),
                "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak * world, "unit": "GB/s",

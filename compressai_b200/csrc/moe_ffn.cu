@@ -182,8 +182,10 @@ int64_t moe_layer_workspace(int64_t T, int64_t ks, int64_t H, int64_t gu_rows, i
 }
 
 // Router + routed (and shared) expert FFN + combine of one MoE layer: three launches (route,
-// gate_up, down with the combine in its epilogue), or four with the cross-rank sum over peer
-// memory (route, gate_up, down, peer combine).
+// gate_up, down with the combine in its epilogue) up to kFuseCombineMaxP (token, expert)
+// problems, else four (a separate combine kernel); with the cross-rank sum over peer memory the
+// fourth is the peer combine.
+constexpr int64_t kFuseCombineMaxP = 64;
 int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E, int64_t K,
               const float* shared_gate, int64_t lo, int64_t hi, int rank, int world, const void* pool,
               int64_t pool_rows, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0,
@@ -217,7 +219,10 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
   r.lo = (int)lo; r.hi = (int)hi; r.shared_row = (int)shared_row; r.rank = rank; r.world = world;
   r.perm = perm_in; r.sign = sign_in; r.hb = (int)hb_in; r.rot_scale = scale_in; r.xrot = L.xrot;
   r.c_ids = L.c_ids; r.c_map = L.c_map; r.c_cnt = L.c_cnt; r.tstart = L.tstart; r.tcnt = L.tcnt;
-  r.zero = peer ? nullptr : L.ctr; r.zero_n = peer ? 0 : L.ctr_n;
+  // the combine rides in the down GEMV's epilogue for decode-sized batches (it saves a launch on
+  // the critical path); past that its per-item fence and barriers cost more than the launch
+  const bool fuse_combine = !peer && P <= kFuseCombineMaxP;
+  r.zero = fuse_combine ? L.ctr : nullptr; r.zero_n = fuse_combine ? L.ctr_n : 0;
   r.out = peer ? nullptr : out; r.out_dtype = out_dtype;
   int s = run_route(r, st);
   if (s != VQ2_OK) return s;
@@ -239,12 +244,13 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
   b.perm = perm_mid; b.sign = sign_mid; b.hb = (int)hb_mid; b.rot_scale = scale_mid;
   b.idx0 = reinterpret_cast<const int16_t*>(base + R.dn_idx); b.scale = base + R.dn_scale;
   b.y = L.yd; b.y_k_stride = dn_rows; b.out = (int)dn_rows; b.n = (int)I;
-  if (!peer) {  // the routing-weighted sum of each token's problems in the down GEMV's epilogue
+  if (fuse_combine) {  // the routing-weighted sum of each token's problems in the down GEMV's epilogue
     b.comb_w = L.w; b.comb_tstart = L.tstart; b.comb_tcnt = L.tcnt; b.comb_ctr = L.ctr;
     b.comb_out = out; b.comb_dtype = out_dtype; b.comb_ks = (int)ks;
   }
   if ((s = run_gemv(b, dn_rows * P, false, val_dtype, st)) != VQ2_OK) return s;
   if (peer) return run_combine_peer(L.yd, L.w, T, (int)ks, H, L.ids, pool_rows, *peer, out, out_dtype, st);
+  if (!fuse_combine) return run_combine(L.yd, L.w, T, (int)ks, H, nullptr, out, out_dtype, st, L.ids, pool_rows);
   return VQ2_OK;
 }
 
