@@ -132,6 +132,7 @@ struct RouteArgs {
   int64_t zero_n;
   void* out;             // layer mode: [T, H] rows of tokens without local problems are zeroed, or null
   int out_dtype;
+  int32_t* arrive;       // layer mode, expert parallel: arrival counter (zero at entry, left at zero)
 };
 
 int run_route(const RouteArgs& r, cudaStream_t st);

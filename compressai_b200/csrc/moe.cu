@@ -205,6 +205,211 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RouteArg
   }
 }
 
+// Router, one CTA of 1024 threads per token (layer mode). Used when every problem of the layer
+// is local to this GPU (the problem list is then the identity: nothing to compact) or when a
+// persistent arrival counter is given (expert parallelism: the last CTA to finish compacts the
+// layer's problems and resets the counter). All global loads a token needs -- its logits, its
+// hidden row (16-byte vectors), the shared gate -- are issued together after the dependency
+// wait; the rotation table is staged in shared memory before it (constant). Each of the TPT
+// logit slots has PARTS = 1024 / TPT threads that split the rank count.
+constexpr int kRouteMaxH = 4096;
+
+template <int TPT>
+__global__ void __launch_bounds__(1024) moe_route_token_kernel(const RouteArgs r) {
+  constexpr int PARTS = 1024 / TPT;
+  __shared__ float sl[TPT];
+  __shared__ int sel_e[32];
+  __shared__ float sel_v[32];
+  __shared__ float red[32];
+  __shared__ __align__(16) float hs[kRouteMaxH];
+  __shared__ uint16_t ps[kRouteMaxH];
+  __shared__ float sc[kRouteMaxH + kRouteMaxH / 32];  // segments x (hb + hb / 32) floats
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t = blockIdx.x;
+  const int H = r.H, nv = H >> 3;
+  // rotation table (constant): perm with the sign in bit 15
+  for (int j = tid; j < H; j += 1024) ps[j] = static_cast<uint16_t>(r.perm[j] | (r.sign[j] < 0 ? 0x8000 : 0));
+  pdl_trigger();
+  pdl_wait();
+  // ---- all loads of this token at once: logit slot, hidden row (8 values per thread), gate
+  const int i = tid / PARTS, part = tid % PARTS;
+  float l = -FLT_MAX;
+  if (part == 0 && i < r.E) l = r.logits[(int64_t)t * r.E + i];
+  float hv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float gv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (tid < nv) {
+    const int64_t off = (int64_t)t * H + 8 * tid;
+    if (r.h_dtype == VQ2_F32) {
+      const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(r.h) + off);
+      const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(r.h) + off + 4);
+      hv[0] = a.x; hv[1] = a.y; hv[2] = a.z; hv[3] = a.w; hv[4] = b.x; hv[5] = b.y; hv[6] = b.z; hv[7] = b.w;
+    } else if (r.h_dtype == VQ2_F16) {
+      decode8<__half>(*reinterpret_cast<const uint4*>(static_cast<const __half*>(r.h) + off), hv);
+    } else {
+      decode8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(r.h) + off), hv);
+    }
+    if (r.gate) {
+      const float4 a = *reinterpret_cast<const float4*>(r.gate + 8 * tid);
+      const float4 b = *reinterpret_cast<const float4*>(r.gate + 8 * tid + 4);
+      gv[0] = a.x; gv[1] = a.y; gv[2] = a.z; gv[3] = a.w; gv[4] = b.x; gv[5] = b.y; gv[6] = b.z; gv[7] = b.w;
+    }
+  }
+  if (part == 0 && i < TPT) sl[i] = l;
+  float d = 0.f;
+  if (tid < nv) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      hs[8 * tid + k] = hv[k];
+      d = fmaf(hv[k], gv[k], d);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+  if (lane == 0) red[warp] = d;
+  for (int64_t z = tid; r.zero && z < r.zero_n / r.T; z += 1024) r.zero[(int64_t)t * (r.zero_n / r.T) + z] = 0;
+  __syncthreads();
+  // ---- rank of each logit: PARTS threads count interleaved slices of the others
+  {
+    const float li = i < r.E ? sl[i] : -FLT_MAX;
+    int rank = 0;
+    for (int j = part; j < r.E; j += PARTS) {
+      const float o = sl[j];
+      rank += (o > li || (o == li && j < i)) ? 1 : 0;
+    }
+#pragma unroll
+    for (int off = 1; off < PARTS; off <<= 1) rank += __shfl_xor_sync(0xffffffffu, rank, off);
+    if (part == 0 && i < r.E && rank < r.K) {
+      sel_e[rank] = i;
+      sel_v[rank] = li;
+    }
+  }
+  __syncthreads();
+  const int64_t row = (int64_t)t * r.ks;
+  if (tid < r.K) {
+    const float mx = sel_v[0];
+    float sum = 0.f;
+    for (int k = 0; k < r.K; ++k) sum += expf(sel_v[k] - mx);
+    const int e = sel_e[tid];
+    r.ids[row + tid] = (e >= r.lo && e < r.hi) ? e - r.lo : -1;
+    r.w[row + tid] = expf(sel_v[tid] - mx) / sum;
+  }
+  if (r.gate && tid == 32) {
+    float dd = 0.f;
+    for (int wv = 0; wv < 32; ++wv) dd += red[wv];
+    r.ids[row + r.K] = (t % r.world == r.rank) ? r.shared_row : -1;
+    r.w[row + r.K] = 1.f / (1.f + expf(-dd));
+  }
+  // ---- forward RHT of the hidden row from shared memory into xrot
+  {
+    const int TS = r.hb >> 3, nb = H / r.hb;
+    const int sg = tid / TS, ts = tid % TS;
+    const bool act = sg < nb;
+    float* scr = sc + (act ? sg : 0) * (r.hb + (r.hb >> 5));
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float val = 0.f;
+      if (act) {
+        const uint32_t pq = ps[sg * r.hb + ts + TS * q];
+        const float x = hs[pq & 0x7fffu];
+        val = (pq & 0x8000u) ? -x : x;
+      }
+      v[q] = val;
+    }
+    fwht8(v);
+    if (act) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int e = ts + TS * q;
+        scr[e + (e >> 5)] = v[q];
+      }
+    }
+    __syncthreads();
+    if (act) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int e = 8 * ts + q;
+        v[q] = scr[e + (e >> 5)];
+      }
+    }
+    fwht8(v);
+    for (int td = 1; td <= (TS >> 4); td <<= 1) {
+      const bool upper = (ts & td) != 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float o = __shfl_xor_sync(0xffffffffu, v[q], td);
+        v[q] = upper ? (o - v[q]) : (v[q] + o);
+      }
+    }
+    if (act) {
+      float* o = r.xrot + (int64_t)t * H + sg * r.hb + 8 * ts;
+      reinterpret_cast<float4*>(o)[0] = make_float4(v[0] * r.rot_scale, v[1] * r.rot_scale, v[2] * r.rot_scale,
+                                                    v[3] * r.rot_scale);
+      reinterpret_cast<float4*>(o)[1] = make_float4(v[4] * r.rot_scale, v[5] * r.rot_scale, v[6] * r.rot_scale,
+                                                    v[7] * r.rot_scale);
+    }
+  }
+  // ---- the problem list
+  if (r.arrive == nullptr) {  // every problem is local: the identity list
+    if (tid < r.ks) {
+      r.c_ids[row + tid] = r.ids[row + tid];
+      r.c_map[row + tid] = static_cast<int32_t>(row + tid);
+    }
+    if (tid == 0) {
+      r.tstart[t] = static_cast<int32_t>(row);
+      r.tcnt[t] = r.ks;
+      if (t == 0) *r.c_cnt = r.T * r.ks;
+    }
+    return;
+  }
+  // expert parallel: the last CTA compacts all tokens' problems in order and resets the counter
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(r.arrive, 1) == r.T - 1) ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  const int P = r.T * r.ks;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < P; c0 += 1024) {
+    const int p = c0 + tid;
+    const int32_t id = p < P ? __ldcg(r.ids + p) : -1;
+    const bool keep = id >= 0;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int off = base;
+    for (int wv = 0; wv < warp; ++wv) off += warp_tot[wv];
+    if (keep) {
+      const int pos = off + __popc(m & ((1u << lane) - 1u));
+      r.c_ids[pos] = id;
+      r.c_map[pos] = p;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int wv = 0; wv < 32; ++wv) tot += warp_tot[wv];
+      base += tot;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    *r.c_cnt = base;
+    *r.arrive = 0;
+  }
+  for (int tt = tid; tt < r.T; tt += 1024) {
+    int before = 0, mine = 0;
+    for (int p = 0; p < tt * r.ks; ++p) before += __ldcg(r.ids + p) >= 0 ? 1 : 0;
+    for (int k = 0; k < r.ks; ++k) mine += __ldcg(r.ids + tt * r.ks + k) >= 0 ? 1 : 0;
+    r.tstart[tt] = before;
+    r.tcnt[tt] = mine;
+  }
+}
+
 int run_route(const RouteArgs& r, cudaStream_t st) {
   if (r.T <= 0 || r.E <= 0 || r.E > kRouteThreads || r.K <= 0 || r.K > 32 || r.K > r.E) return VQ2_ERR_SHAPE;
   if (r.layer) {
@@ -213,6 +418,19 @@ int run_route(const RouteArgs& r, cudaStream_t st) {
     if (!aligned(r.xrot, 16) || r.world <= 0 || r.rank < 0 || r.rank >= r.world) return VQ2_ERR_ARG;
   }
   const int tpt = r.E <= 32 ? 32 : r.E <= 64 ? 64 : r.E <= 128 ? 128 : r.E <= 256 ? 256 : r.E <= 512 ? 512 : 1024;
+  const bool all_local = r.lo == 0 && r.hi == r.E && r.world == 1;
+  if (r.layer && (all_local || r.arrive) && r.H <= kRouteMaxH && r.H % 256 == 0 && r.out == nullptr) {
+    // one CTA per token (the per-token work in parallel)
+    const dim3 g((unsigned)r.T);
+    switch (tpt) {
+      case 32: return launch_kernel(moe_route_token_kernel<32>, g, dim3(1024), 0, st, r);
+      case 64: return launch_kernel(moe_route_token_kernel<64>, g, dim3(1024), 0, st, r);
+      case 128: return launch_kernel(moe_route_token_kernel<128>, g, dim3(1024), 0, st, r);
+      case 256: return launch_kernel(moe_route_token_kernel<256>, g, dim3(1024), 0, st, r);
+      case 512: return launch_kernel(moe_route_token_kernel<512>, g, dim3(1024), 0, st, r);
+      default: return launch_kernel(moe_route_token_kernel<1024>, g, dim3(1024), 0, st, r);
+    }
+  }
   switch (tpt) {
     case 32: return launch_kernel(moe_route_kernel<32>, dim3(1), dim3(kRouteThreads), 0, st, r);
     case 64: return launch_kernel(moe_route_kernel<64>, dim3(1), dim3(kRouteThreads), 0, st, r);

@@ -223,7 +223,9 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
   // the critical path); past that its per-item fence and barriers cost more than the launch
   const bool fuse_combine = !peer && P <= kFuseCombineMaxP;
   r.zero = fuse_combine ? L.ctr : nullptr; r.zero_n = fuse_combine ? L.ctr_n : 0;
-  r.out = peer ? nullptr : out; r.out_dtype = out_dtype;
+  const bool all_local = lo == 0 && hi == E && world == 1;
+  r.out = (peer || all_local) ? nullptr : out; r.out_dtype = out_dtype;
+  r.arrive = peer ? peer->epochs + 2 : nullptr;  // the peer state's third word: route arrivals
   int s = run_route(r, st);
   if (s != VQ2_OK) return s;
 

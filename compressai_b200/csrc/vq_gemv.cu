@@ -64,9 +64,9 @@ __device__ __forceinline__ void combine_tail(const float* __restrict__ comb_w, c
                                          const int32_t* __restrict__ tcnt, int32_t* ctr,
                                          const int32_t* __restrict__ prob_map, const float* y, int64_t y_k_stride,
                                          void* comb_out, int comb_dtype, int comb_ks, int row_blocks, int out, int o,
-                                         int rb, int rpc) {
+                                         int rb, int rpc, bool wrote) {
   __shared__ int s_last;
-  __threadfence();  // this thread's output rows are visible GPU-wide before the arrival
+  if (wrote) __threadfence();  // this thread's output rows are visible GPU-wide before the arrival
   __syncthreads();
   const int t = o / comb_ks;
   if (threadIdx.x == 0) {
@@ -80,9 +80,20 @@ __device__ __forceinline__ void combine_tail(const float* __restrict__ comb_w, c
   if ((int)threadIdx.x < rpc && r < out) {
     const int c0 = tstart[t], cn = tcnt[t];
     float s = 0.f;
-    for (int c = c0; c < c0 + cn; ++c) {
-      const int oo = prob_map ? prob_map[c] : c;
-      s = fmaf(comb_w[oo], __ldcg(y + (int64_t)oo * y_k_stride + r), s);
+    int c = c0;
+    for (; c < c0 + cn; c += 8) {  // 8 problems' loads in flight, summed in problem order
+      int oo[8];
+      float wv[8], yv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) oo[k] = (c + k < c0 + cn) ? (prob_map ? prob_map[c + k] : c + k) : -1;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        wv[k] = oo[k] >= 0 ? comb_w[oo[k]] : 0.f;
+        yv[k] = oo[k] >= 0 ? __ldcg(y + (int64_t)oo[k] * y_k_stride + r) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (oo[k] >= 0) s = fmaf(wv[k], yv[k], s);
     }
     const int64_t i = (int64_t)t * out + r;
     if (comb_dtype == VQ2_F16) static_cast<__half*>(comb_out)[i] = __float2half_rn(s);
@@ -371,7 +382,8 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
       }
       if constexpr (COMB)  // uniform over the CTA
         combine_tail(a.comb_w, a.comb_tstart, a.comb_tcnt, a.comb_ctr, a.prob_map, static_cast<const float*>(a.y),
-                     a.y_k_stride, a.comb_out, a.comb_dtype, a.comb_ks, a.row_blocks, a.out, cur.o, cur.rb, RPC);
+                     a.y_k_stride, a.comb_out, a.comb_dtype, a.comb_ks, a.row_blocks, a.out, cur.o, cur.rb, RPC,
+                     li == 0);
     }
     item = nitem;
     chunk = nchunk;
@@ -455,10 +467,11 @@ static int launch_mt(const GemvArgs& a, int mt, bool xreg, cudaStream_t st) {
 
 template <int LPR, bool RES, typename TV>
 static int launch_rw(const GemvArgs& a, int64_t total_rows, int mt, bool xreg, cudaStream_t st) {
-  // Few rows (small matrices, MoE problems) or wide M tiles: one row per warp-load keeps many
-  // CTAs busy within the register budget; many rows at M tile 1: two rows per warp amortise
-  // activation reads over more gathers.
-  if (mt == 1 && total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / LPR)) {
+  // Few rows (small matrices) or wide M tiles: one row per warp-load keeps many CTAs busy within
+  // the register budget. Many rows at M tile 1, and expert-indexed problems at any count: two
+  // rows per warp put twice the gathers in flight per lane (for MoE problems the rows are known
+  // only after the routing kernel, so the CTAs should finish their shares in fewer rounds).
+  if (mt == 1 && (a.nprob == 0 || total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / LPR))) {
     if (xreg && LPR == 32) return launch_cfg<LPR, 2, 1, RES, LPR == 32, TV>(a, st);
     return launch_cfg<LPR, 2, 1, RES, false, TV>(a, st);
   }
@@ -530,11 +543,9 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
   }
   if (a.comb_w != nullptr) {  // fused combine: expert-indexed, 2 bpw, one activation row (MoE down)
     if (a.nprob > 0 || res || a.M != 1 || a.argmax) return VQ2_ERR_ARG;
-    // two rows per warp once the rows fill every SM's warps twice over (as launch_rw chooses)
-    const bool rw2 = total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / lpr);
-    if (val_dtype == VQ2_F16) return rw2 ? launch_comb<2, __half>(a, lpr, st) : launch_comb<1, __half>(a, lpr, st);
-    if (val_dtype == VQ2_BF16)
-      return rw2 ? launch_comb<2, __nv_bfloat16>(a, lpr, st) : launch_comb<1, __nv_bfloat16>(a, lpr, st);
+    // two rows per warp (as launch_rw chooses for expert-indexed problems)
+    if (val_dtype == VQ2_F16) return launch_comb<2, __half>(a, lpr, st);
+    if (val_dtype == VQ2_BF16) return launch_comb<2, __nv_bfloat16>(a, lpr, st);
     return VQ2_ERR_DTYPE;
   }
   const int mt = pick_mt(a.M, a.n);

@@ -47,7 +47,8 @@ class PeerReduceContext:
         self.buf.zero_()
         self.handle = symm_mem.rendezvous(self.buf, name)
         self.peers_dev = self.handle.buffer_ptrs_dev
-        self.epochs = torch.zeros(2, dtype=torch.int32, device=device)   # sequence number, finished CTAs
+        # sequence number, finished CTAs (peer combine), router arrivals, spare
+        self.epochs = torch.zeros(4, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group)  # every rank's flags are zero before any rank writes into them

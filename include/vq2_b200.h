@@ -375,9 +375,10 @@ VQ2_API int vq2_moe_expert_ffn_ep(const void* h, int h_dtype, int64_t T, int64_t
 /*
  * Expert-parallel vq2_moe_layer: the same route / gate_up / down sequence on this rank's
  * experts, then the routing-weighted combine and the sum over the ranks in one kernel over
- * NVLink peer memory (peers_dev, epochs, err and max_tokens as vq2_moe_expert_ffn_ep). Every
- * rank makes the same calls with the same logits and hidden states; the output is identical
- * on every rank.
+ * NVLink peer memory (peers_dev, err and max_tokens as vq2_moe_expert_ffn_ep; epochs: local
+ * device int32 [4], zeroed before first use -- the combine's sequence number and CTA count and
+ * the router's arrival counter). Every rank makes the same calls with the same logits and hidden
+ * states; the output is identical on every rank.
  */
 VQ2_API int vq2_moe_layer_ep(const void* h, int h_dtype, int64_t T, const float* logits, int64_t E,
                              int64_t top_k, const float* shared_gate, int64_t expert_lo,

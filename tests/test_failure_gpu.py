@@ -25,7 +25,7 @@ class _LoneRankPeers:
         self.ptrs = torch.tensor([b.data_ptr() for b in self.bufs], dtype=torch.int64, device=DEV)
         self.peers_dev = self.ptrs.data_ptr()
         self.rank, self.world, self.max_tokens, self.max_polls = 0, 2, max_tokens, max_polls
-        self.epochs = torch.zeros(2, dtype=torch.int32, device=DEV)
+        self.epochs = torch.zeros(4, dtype=torch.int32, device=DEV)
         self.err = torch.zeros(1, dtype=torch.int32, device=DEV)
 
 
