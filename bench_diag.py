@@ -3,10 +3,10 @@ behind the launch lists and captures summarised in profiles/. Not part of the pa
 
   python bench_diag.py gather
       random codebook-row gather rates (global / shared / cluster-shared memory)
-  python bench_diag.py gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3 [--swiglu]
+  python bench_diag.py gemv --out 151936 --n 2048 --M 1 --bpw 2 --reps 3 [--swiglu | --argmax]
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
       with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
-      prologue (the MLP down projection)
+      prologue (the MLP down projection); with --argmax the fused greedy argmax (keys only)
   python bench_diag.py moe --T 1 --reps 3
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts
   python bench_diag.py rans --n 16777216 --reps 2
@@ -14,6 +14,10 @@ behind the launch lists and captures summarised in profiles/. Not part of the pa
       ANS-coded expert record (vq2_rans_decode_segments)
   python bench_diag.py paged --layers 2 --experts 64 --steps 8 --T 1 [--coding vq2a]
       native paged MoE steps (vq2_paged_moe_step) over a pinned synthetic .vq2m image
+  python bench_diag.py reftriton --reps 50
+      the reference's own Triton kernels (vq2/kernels.py, from the offline install under
+      baseline/_ref) beside this library's drop-ins of the same functions: same arguments, same
+      rotating weight copies (at least 4x L2 of indices per shape), both timed in CUDA graphs
 
 Each prints one JSON line with the measured device time per launch/layer.
 """
@@ -65,7 +69,12 @@ def cmd_gemv(a):
     idx, scale = synth.random_matrix(a.seed, a.out, a.n, bits)
     lin = runtime.PackedLinear((a.out, a.n), bits, "diag", [torch.from_numpy(i) for i in idx],
                                torch.from_numpy(scale), cbs, dev)
-    if a.swiglu:
+    if a.argmax:  # fused greedy argmax (no logits written), keys as the row-sharded head uses them
+        x = torch.randn(a.M, a.n, device=dev).half()
+        cb0, cb1 = lin.codebooks()
+        t = _time(lambda: kernels.gemv_argmax(x, lin.mat(), cb0, cb1, rot=lin.rot, keys=True), a.reps)
+        xbytes = 2 * a.M * a.n
+    elif a.swiglu:
         from compressai_b200 import _lib
         x = torch.randn(a.M, 2 * a.n, device=dev)
         cb0, cb1 = lin.codebooks()
@@ -161,6 +170,84 @@ def cmd_paged(a):
                       "ms_per_step": round(wall / a.steps * 1e3, 3), "finite": bool(torch.isfinite(h).all())}))
 
 
+def _rotating(fn, copies, reps):
+    """Device time per call of fn(c), c cycling over the weight copies, from a CUDA graph of
+    `copies` calls replayed `reps` times (no host launch cost in the measurement)."""
+    for c in range(copies):  # warm-up (Triton autotuning, first-call set-up) outside the capture
+        fn(c)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for c in range(copies):
+            fn(c)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / (reps * copies)
+
+
+def cmd_reftriton(a):
+    ref_root = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_root, "vq2", "kernels.py")):
+        print(json.dumps({"reference_triton": "unavailable", "why": "the reference is not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, ref_root)
+    import vq2.kernels as RK  # the reference package, unmodified
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(a.seed)
+    cb = _cbs(dev)["16"].to(torch.bfloat16)
+    budget = 4 * 126 * 2 ** 20
+    out = []
+    for rows, n in ((2048, 2048), (6144, 2048), (2048, 6144), (151936, 2048)):
+        ng = n // 8
+        copies = max(2, -(-budget // (rows * ng * 2)))
+        idx = torch.randint(-32768, 32768, (copies, rows, ng), generator=g, device=dev, dtype=torch.int16)
+        sc = (0.02 * torch.ones(copies, rows, device=dev)).to(torch.bfloat16)
+        x = torch.randn(n, generator=g, device=dev).to(torch.bfloat16)
+        y_ref = RK.vq_gemv_16(x, idx[0], cb, sc[0], rows, n)
+        y_own = kernels.vq_gemv_16(x, idx[0], cb, sc[0], rows, n)
+        err = float((y_own.float() - y_ref.float()).abs().max() / y_ref.float().abs().max())
+        reps = max(1, a.reps * 8 // copies)
+        t_ref = _rotating(lambda c: RK.vq_gemv_16(x, idx[c], cb, sc[c], rows, n), copies, reps)
+        t_own = _rotating(lambda c: kernels.vq_gemv_16(x, idx[c], cb, sc[c], rows, n), copies, reps)
+        out.append({"vq_gemv_16": [rows, n], "copies": copies, "ref_us": round(t_ref * 1e6, 2),
+                    "own_us": round(t_own * 1e6, 2), "speedup": round(t_ref / t_own, 2), "max_rel_diff": err})
+        del idx, sc
+    # one top-8 MoE layer's two expert GEMVs (gate_up on the shared input, down on 8 activations)
+    E, copies = 256, 2
+    gu = torch.randint(-32768, 32768, (copies, E, 1024, 256), generator=g, device=dev, dtype=torch.int16)
+    dn = torch.randint(-32768, 32768, (copies, E, 2048, 64), generator=g, device=dev, dtype=torch.int16)
+    gus = (0.02 * torch.ones(copies, E, 1024, device=dev)).to(torch.bfloat16)
+    dns = (0.02 * torch.ones(copies, E, 2048, device=dev)).to(torch.bfloat16)
+    sets = [torch.randperm(E, generator=g, device=dev)[:8].to(torch.int32) for _ in range(64)]
+    x = torch.randn(2048, generator=g, device=dev).to(torch.bfloat16)
+    act = torch.randn(8, 512, generator=g, device=dev).to(torch.bfloat16)
+    y_gu = torch.empty(8, 1024, device=dev, dtype=torch.bfloat16)
+    y_dn = torch.empty(8, 2048, device=dev, dtype=torch.bfloat16)
+    own_gu, own_dn = torch.empty_like(y_gu), torch.empty_like(y_dn)
+
+    def ref_layer(c, mod=RK, a_gu=y_gu, a_dn=y_dn):
+        ids = sets[c % 64]
+        w = c % copies
+        mod.vq_moe_parallel_gate_up(x, ids, gu[w], cb, gus[w], a_gu)
+        mod.vq_moe_parallel_down(act, ids, dn[w], cb, dns[w], a_dn)
+    ref_layer(0)
+    ref_layer(0, kernels, own_gu, own_dn)
+    err = max(float((own_gu.float() - y_gu.float()).abs().max() / y_gu.float().abs().max()),
+              float((own_dn.float() - y_dn.float()).abs().max() / y_dn.float().abs().max()))
+    t_ref = _rotating(ref_layer, 128, max(1, a.reps // 10))
+    t_own = _rotating(lambda c: ref_layer(c, kernels, own_gu, own_dn), 128, max(1, a.reps // 10))
+    out.append({"moe_gate_up_plus_down_top8": [E, 1024, 2048], "ref_us": round(t_ref * 1e6, 2),
+                "own_us": round(t_own * 1e6, 2), "speedup": round(t_ref / t_own, 2), "max_rel_diff": err})
+    print(json.dumps({"reference_triton": out, "triton": __import__("triton").__version__}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -173,6 +260,7 @@ def main(argv=None):
     g.add_argument("--reps", type=int, default=3)
     g.add_argument("--seed", type=int, default=0)
     g.add_argument("--swiglu", action="store_true")
+    g.add_argument("--argmax", action="store_true")
     m = sub.add_parser("moe")
     m.add_argument("--T", type=int, default=1)
     m.add_argument("--E", type=int, default=256)
@@ -190,8 +278,12 @@ def main(argv=None):
     pg.add_argument("--T", type=int, default=1)
     pg.add_argument("--coding", choices=("raw", "vq2a"), default="raw")
     pg.add_argument("--seed", type=int, default=0)
+    rt = sub.add_parser("reftriton")
+    rt.add_argument("--reps", type=int, default=50)
+    rt.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
-    {"gather": cmd_gather, "gemv": cmd_gemv, "moe": cmd_moe, "rans": cmd_rans, "paged": cmd_paged}[a.cmd](a)
+    {"gather": cmd_gather, "gemv": cmd_gemv, "moe": cmd_moe, "rans": cmd_rans, "paged": cmd_paged,
+     "reftriton": cmd_reftriton}[a.cmd](a)
 
 
 if __name__ == "__main__":

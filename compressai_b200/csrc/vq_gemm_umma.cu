@@ -181,19 +181,11 @@ __device__ __forceinline__ bool um_drain(uint32_t bar, uint32_t parity) {
   return true;
 }
 
-// The CTA's contiguous range of items: with an even grid, CTAs b and b + G/2 (the two CTAs of one
-// SM) split one SM-sized share, so per-SM totals differ by at most one item.
+// The CTA's contiguous range of items (one CTA per SM): a floor / ceil split.
 __device__ __forceinline__ void um_items(int64_t items, int64_t& lo, int64_t& hi) {
   const int64_t G = gridDim.x, b = blockIdx.x;
-  if (G % 2 == 0) {
-    const int64_t half = G / 2, pr = b % half;
-    const int64_t p0 = pr * items / half, p1 = (pr + 1) * items / half, mid = p0 + (p1 - p0 + 1) / 2;
-    lo = b < half ? p0 : mid;
-    hi = b < half ? mid : p1;
-  } else {
-    lo = b * items / G;
-    hi = (b + 1) * items / G;
-  }
+  lo = b * items / G;
+  hi = (b + 1) * items / G;
 }
 
 struct UmItem {
@@ -214,7 +206,7 @@ __device__ __forceinline__ UmItem um_decode(const GemvArgs& a, int64_t it, int N
 }
 
 template <int NT, int S, bool RES, bool LO, typename TV>
-__global__ void __launch_bounds__(kUmThreads, 2) vq_umma_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap xmap,
+__global__ void __launch_bounds__(kUmThreads, 1) vq_umma_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap xmap,
                                                                  const __grid_constant__ CUtensorMap lmap) {
   constexpr int A_BYTES = kUmRows * 128;
   constexpr int B_BYTES = NT * 128;
@@ -308,19 +300,20 @@ __global__ void __launch_bounds__(kUmThreads, 2) vq_umma_kernel(const GemvArgs a
         const uint32_t gc = (uint32_t)il * chunks + c;
         const int s = (int)(gc % S);
         const uint32_t u = gc / S;
-        if (!um_wait(su32(&ctl->empty[s]), (u & 1) ^ 1, ctl)) goto producer_exit;
-        if (leader) {
-          mbar_arrive_tx(su32(&ctl->tma[s]), B_BYTES * (LO ? 2 : 1));
-          tma_load_2d(su32(stage_b(s)), &xmap, c * kUmKC, w.m0, su32(&ctl->tma[s]));
-          if (LO) tma_load_2d(su32(stage_bl(s)), &lmap, c * kUmKC, w.m0, su32(&ctl->tma[s]));
-          issued_use[s] = u + 1;
-        }
+        // the gathers go out first: their L2 round trip overlaps the wait for the stage
         uint4 cw[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t w32 = (&iv.x)[j >> 1];
           const uint32_t code = (j & 1) ? (w32 >> 16) : (w32 & 0xffffu);
           cw[j] = row_ok ? ld_cb_u4(cb0 + code, pol_c) : make_uint4(0, 0, 0, 0);
+        }
+        if (!um_wait(su32(&ctl->empty[s]), (u & 1) ^ 1, ctl)) goto producer_exit;
+        if (leader) {
+          mbar_arrive_tx(su32(&ctl->tma[s]), B_BYTES * (LO ? 2 : 1));
+          tma_load_2d(su32(stage_b(s)), &xmap, c * kUmKC, w.m0, su32(&ctl->tma[s]));
+          if (LO) tma_load_2d(su32(stage_bl(s)), &lmap, c * kUmKC, w.m0, su32(&ctl->tma[s]));
+          issued_use[s] = u + 1;
         }
         if (RES) {  // 3 bpw: cb0 + cb1 summed in fp32 and rounded once to the operand type
 #pragma unroll
@@ -484,7 +477,7 @@ constexpr size_t umma_smem() {
 template <int NT, bool RES, typename TV>
 int launch_umma(GemvArgs a, const void* xh, const void* xl, cudaStream_t st) {
   constexpr bool LO = std::is_same<TV, __nv_bfloat16>::value;
-  constexpr int S = NT * 128 * (LO ? 2 : 1) <= 8192 ? 4 : 2;  // two CTAs per SM either way
+  constexpr int S = NT * 128 * (LO ? 2 : 1) <= 8192 ? 4 : 2;  // stages of <= 24 KB (A 16 KB + B)
   constexpr size_t smem = umma_smem<NT, S, RES, LO>();
   auto kern = vq_umma_kernel<NT, S, RES, LO, TV>;
   static std::atomic<uint64_t> done{0};
@@ -498,9 +491,33 @@ int launch_umma(GemvArgs a, const void* xh, const void* xl, cudaStream_t st) {
       set_last_cuda_error(e);
       return VQ2_ERR_LAUNCH;
     }
-    int nb = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kUmThreads, smem);
-    blocks_per_sm.store(nb > 2 ? 2 : (nb > 0 ? nb : 1));  // TMEM: 2 CTAs x 2 x NT <= 512 columns
+    // One CTA per SM, and a shared-memory carveout just covering it. The gathers are served
+    // through L1, and every codeword in flight holds an L1 line until it returns: with the SM's
+    // whole shared memory configured (what the driver picked for this kernel when it ran two
+    // CTAs per SM) only ~28 KB of L1 remained, which capped the gathers in flight per SM below
+    // what the L2 round trip needs -- two CTAs per SM measured no faster than one.
+    cudaFuncAttributes fa{};
+    int smem_sm = 0, reserved = 0;
+    e = cudaFuncGetAttributes(&fa, kern);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return VQ2_ERR_LAUNCH;
+    }
+    const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;       // allocation granularity
+    const int by_regs = 65536 / (regs_warp * (kUmThreads / 32));
+    const int by_smem = smem_sm / ((int)smem + reserved);
+    if (by_regs < 1 || by_smem < 1) return VQ2_ERR_LAUNCH;
+    const int nb = 1;
+    // a hint: the driver rounds up to a supported configuration that holds the launch
+    const int pct = (int)((((int64_t)smem + reserved) * nb * 100) / smem_sm);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct > 100 ? 100 : pct);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return VQ2_ERR_LAUNCH;
+    }
+    blocks_per_sm.store(nb);
     done.fetch_or(bit);
   }
   CUtensorMap xmap, lmap;

@@ -54,7 +54,7 @@ __device__ __forceinline__ void stage_tile(const ActSrc& a, int64_t xoff, int mc
   else stage_activations<MT>(a, xoff, mcount, xs, xl, scratch, raw, ps);
 }
 
-// Fused combine (the COMB kernel variants only) after an item of expert-indexed problem o, row
+// Fused combine (the kEpiComb kernel variants only) after an item of expert-indexed problem o, row
 // block rb (RPC rows) is written:
 // arrival count per (token, row block); the CTA that brings it to the token's problem count sums
 // the token's problems over the block's rows in problem order (the fmaf chain of
@@ -102,12 +102,15 @@ __device__ __forceinline__ void combine_tail(const float* __restrict__ comb_w, c
   }
 }
 
+// Epilogue of a kernel variant: plain stores, + the fused MoE combine, or the greedy argmax.
+constexpr int kEpiPlain = 0, kEpiComb = 1, kEpiArgmax = 2;
+
 // Variants that stage the fast way: all but the 3 bpw two-row register variant, whose
 // registers are taken by its two rows of residual indices.
 template <int RW, bool RES, bool XREG>
 constexpr bool variant_fast_stage() { return !(RES && XREG && RW == 2); }
 
-template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, bool COMB = false>
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, int EPI = kEpiPlain>
 __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   static_assert(!XREG || (LPR == 32 && MT == 1), "register activations need one 256-group chunk, M tile 1");
   constexpr int RPL = 32 / LPR;   // rows per warp-load
@@ -247,6 +250,16 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
   }
   pdl_trigger();
 
+  // greedy argmax: each warp's running best key per activation row of its current M tile
+  __shared__ unsigned long long s_best[EPI == kEpiArgmax ? 8 : 1][MT];
+  __shared__ int s_tile[EPI == kEpiArgmax ? 8 : 1];
+  if constexpr (EPI == kEpiArgmax) {
+    if (lane == 0) {
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) s_best[warp][mi] = 0ull;
+      s_tile[warp] = -1;
+    }
+  }
   int64_t cur_xoff = -1;
   float xreg[XREG ? 64 : 1];
   float acc[RW][MT];
@@ -337,11 +350,12 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
         for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
           for (int off = LPR / 2; off > 0; off >>= 1) acc[rw][mi] += __shfl_xor_sync(0xffffffffu, acc[rw][mi], off);
-      // greedy argmax (one matrix): per activation row, the warp's best (value, row) key, one atomic
-      // per warp
-      unsigned long long best[MT];
+      // greedy argmax (one matrix): per activation row, the warp's best (value, row) key
+      unsigned long long best[EPI == kEpiArgmax ? MT : 1];
+      if constexpr (EPI == kEpiArgmax) {
 #pragma unroll
-      for (int mi = 0; mi < MT; ++mi) best[mi] = 0ull;
+        for (int mi = 0; mi < MT; ++mi) best[mi] = 0ull;
+      }
       if (li == 0) {
         void* ybase = multi ? a.p_y[cur.k] : a.y;
         const int64_t yk = multi ? 0 : (int64_t)cur.o * a.y_k_stride;
@@ -355,11 +369,11 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
               if (mi < mcount) {
                 const int64_t o = yk + (int64_t)(m0 + mi) * a.y_row_stride + r;
                 const float v = acc[rw][mi] * s;
-                if (a.argmax) {  // global row of the concatenated outputs: problem offset + r
+                if constexpr (EPI == kEpiArgmax) {
                   const unsigned long long key = argmax_key(v, r);
                   best[mi] = key > best[mi] ? key : best[mi];
+                  if (a.no_y) continue;
                 }
-                if (a.no_y) continue;
                 if (a.y_dtype == VQ2_F16) static_cast<__half*>(ybase)[o] = __float2half_rn(v);
                 else if (a.y_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(ybase)[o] = __float2bfloat16_rn(v);
                 else static_cast<float*>(ybase)[o] = v;
@@ -368,7 +382,20 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
           }
         }
       }
-      if (a.argmax) {
+      if constexpr (EPI == kEpiArgmax) {
+        // the warp's best of this item joins its running best; the running bests go out (one
+        // atomic per row) only when the warp moves to another M tile and at the end of the
+        // CTA's items, not once per item: 64-bit atomics on one address serialise in L2
+        if (lane == 0 && s_tile[warp] != m0) {
+          if (s_tile[warp] >= 0) {
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+              if (s_best[warp][mi]) atomicMax(a.argmax + s_tile[warp] + mi, s_best[warp][mi]);
+          }
+#pragma unroll
+          for (int mi = 0; mi < MT; ++mi) s_best[warp][mi] = 0ull;
+          s_tile[warp] = m0;
+        }
 #pragma unroll
         for (int mi = 0; mi < MT; ++mi) {
           unsigned long long b = best[mi];
@@ -377,10 +404,10 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
             const unsigned long long q = __shfl_xor_sync(0xffffffffu, b, off);
             b = q > b ? q : b;
           }
-          if (lane == 0 && mi < mcount && b) atomicMax(a.argmax + m0 + mi, b);
+          if (lane == 0 && mi < mcount && b > s_best[warp][mi]) s_best[warp][mi] = b;
         }
       }
-      if constexpr (COMB)  // uniform over the CTA
+      if constexpr (EPI == kEpiComb)  // uniform over the CTA
         combine_tail(a.comb_w, a.comb_tstart, a.comb_tcnt, a.comb_ctr, a.prob_map, static_cast<const float*>(a.y),
                      a.y_k_stride, a.comb_out, a.comb_dtype, a.comb_ks, a.row_blocks, a.out, cur.o, cur.rb, RPC,
                      li == 0);
@@ -395,6 +422,13 @@ __global__ void __launch_bounds__(256, 2) vq_gemv_kernel(const GemvArgs a) {
       sv[rw] = nsv[rw];
     }
   }
+  if constexpr (EPI == kEpiArgmax) {
+    if (lane == 0 && s_tile[warp] >= 0) {
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi)
+        if (s_best[warp][mi]) atomicMax(a.argmax + s_tile[warp] + mi, s_best[warp][mi]);
+    }
+  }
 }
 
 // ---- host dispatch ------------------------------------------------------------------------
@@ -402,7 +436,7 @@ constexpr int kMaxXsBytes = 80 * 1024;  // activation tile cap; the rest of the 
 constexpr int kTcMinRows = 4;           // activation rows from which the tensor-core path is used
 constexpr int64_t kTcTallRows = 16384;  // ...or from 2 rows when the matrices have this many rows
 
-template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, bool COMB = false>
+template <int LPR, int RW, int MT, bool RES, bool XREG, typename TV, int EPI = kEpiPlain>
 static int launch_cfg(GemvArgs a, cudaStream_t st) {
   constexpr int RPC = 8 * RW * (32 / LPR);
   a.mtiles = (a.M + MT - 1) / MT;
@@ -424,7 +458,7 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
                        (variant_fast_stage<RW, RES, XREG>() ? fast_stage_floats(MT, a.n, a.x_mode) : 0)) *
                           sizeof(float) +
                       (RES ? 256 * sizeof(uint4) : 0);
-  auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV, COMB>;
+  auto kern = vq_gemv_kernel<LPR, RW, MT, RES, XREG, TV, EPI>;
   // Per-device one-time attributes: dynamic shared memory opt-in and, for the small-tile
   // variants, a small shared-memory carveout so most of the SM's 256 KB serves as L1.
   static std::atomic<uint64_t> done{0};
@@ -452,50 +486,56 @@ static int launch_cfg(GemvArgs a, cudaStream_t st) {
   return launch_kernel(kern, dim3((unsigned)grid), dim3(256), smem, st, a);
 }
 
-template <int LPR, int RW, bool RES, typename TV>
+template <int LPR, int RW, bool RES, typename TV, int EPI>
 static int launch_mt(const GemvArgs& a, int mt, bool xreg, cudaStream_t st) {
   if constexpr (LPR == 32) {
-    if (xreg && mt == 1) return launch_cfg<LPR, RW, 1, RES, true, TV>(a, st);
+    if (xreg && mt == 1) return launch_cfg<LPR, RW, 1, RES, true, TV, EPI>(a, st);
   }
   switch (mt) {
-    case 1: return launch_cfg<LPR, RW, 1, RES, false, TV>(a, st);
-    case 2: return launch_cfg<LPR, RW, 2, RES, false, TV>(a, st);
-    case 4: return launch_cfg<LPR, RW, 4, RES, false, TV>(a, st);
-    default: return launch_cfg<LPR, RW, 8, RES, false, TV>(a, st);
+    case 1: return launch_cfg<LPR, RW, 1, RES, false, TV, EPI>(a, st);
+    case 2: return launch_cfg<LPR, RW, 2, RES, false, TV, EPI>(a, st);
+    case 4: return launch_cfg<LPR, RW, 4, RES, false, TV, EPI>(a, st);
+    default: return launch_cfg<LPR, RW, 8, RES, false, TV, EPI>(a, st);
   }
 }
 
-template <int LPR, bool RES, typename TV>
+template <int LPR, bool RES, typename TV, int EPI>
 static int launch_rw(const GemvArgs& a, int64_t total_rows, int mt, bool xreg, cudaStream_t st) {
   // Few rows (small matrices) or wide M tiles: one row per warp-load keeps many CTAs busy within
   // the register budget. Many rows at M tile 1, and expert-indexed problems at any count: two
   // rows per warp put twice the gathers in flight per lane (for MoE problems the rows are known
   // only after the routing kernel, so the CTAs should finish their shares in fewer rounds).
   if (mt == 1 && (a.nprob == 0 || total_rows >= (int64_t)sm_count() * 8 * 2 * 8 * (32 / LPR))) {
-    if (xreg && LPR == 32) return launch_cfg<LPR, 2, 1, RES, LPR == 32, TV>(a, st);
-    return launch_cfg<LPR, 2, 1, RES, false, TV>(a, st);
+    if (xreg && LPR == 32) return launch_cfg<LPR, 2, 1, RES, LPR == 32, TV, EPI>(a, st);
+    return launch_cfg<LPR, 2, 1, RES, false, TV, EPI>(a, st);
   }
-  return launch_mt<LPR, 1, RES, TV>(a, mt, xreg, st);
+  return launch_mt<LPR, 1, RES, TV, EPI>(a, mt, xreg, st);
 }
 
-template <bool RES, typename TV>
+template <bool RES, typename TV, int EPI>
 static int launch_lpr(const GemvArgs& a, int64_t total_rows, int lpr, int mt, cudaStream_t st) {
   const bool xreg = (a.n == 2048);
   switch (lpr) {
-    case 4: return launch_rw<4, RES, TV>(a, total_rows, mt, false, st);
-    case 8: return launch_rw<8, RES, TV>(a, total_rows, mt, false, st);
-    case 16: return launch_rw<16, RES, TV>(a, total_rows, mt, false, st);
-    default: return launch_rw<32, RES, TV>(a, total_rows, mt, xreg, st);
+    case 4: return launch_rw<4, RES, TV, EPI>(a, total_rows, mt, false, st);
+    case 8: return launch_rw<8, RES, TV, EPI>(a, total_rows, mt, false, st);
+    case 16: return launch_rw<16, RES, TV, EPI>(a, total_rows, mt, false, st);
+    default: return launch_rw<32, RES, TV, EPI>(a, total_rows, mt, xreg, st);
   }
+}
+
+template <bool RES, typename TV>
+static int launch_epi(const GemvArgs& a, int64_t total_rows, int lpr, int mt, cudaStream_t st) {
+  if (a.argmax) return launch_lpr<RES, TV, kEpiArgmax>(a, total_rows, lpr, mt, st);
+  return launch_lpr<RES, TV, kEpiPlain>(a, total_rows, lpr, mt, st);
 }
 
 template <int RW, typename TV>
 static int launch_comb(const GemvArgs& a, int lpr, cudaStream_t st) {
   switch (lpr) {
-    case 4: return launch_cfg<4, RW, 1, false, false, TV, true>(a, st);
-    case 8: return launch_cfg<8, RW, 1, false, false, TV, true>(a, st);
-    case 16: return launch_cfg<16, RW, 1, false, false, TV, true>(a, st);
-    default: return launch_cfg<32, RW, 1, false, false, TV, true>(a, st);
+    case 4: return launch_cfg<4, RW, 1, false, false, TV, kEpiComb>(a, st);
+    case 8: return launch_cfg<8, RW, 1, false, false, TV, kEpiComb>(a, st);
+    case 16: return launch_cfg<16, RW, 1, false, false, TV, kEpiComb>(a, st);
+    default: return launch_cfg<32, RW, 1, false, false, TV, kEpiComb>(a, st);
   }
 }
 
@@ -550,10 +590,10 @@ int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream
   }
   const int mt = pick_mt(a.M, a.n);
   if (val_dtype == VQ2_F16)
-    return res ? launch_lpr<true, __half>(a, total_rows, lpr, mt, st) : launch_lpr<false, __half>(a, total_rows, lpr, mt, st);
+    return res ? launch_epi<true, __half>(a, total_rows, lpr, mt, st) : launch_epi<false, __half>(a, total_rows, lpr, mt, st);
   if (val_dtype == VQ2_BF16)
-    return res ? launch_lpr<true, __nv_bfloat16>(a, total_rows, lpr, mt, st)
-               : launch_lpr<false, __nv_bfloat16>(a, total_rows, lpr, mt, st);
+    return res ? launch_epi<true, __nv_bfloat16>(a, total_rows, lpr, mt, st)
+               : launch_epi<false, __nv_bfloat16>(a, total_rows, lpr, mt, st);
   return VQ2_ERR_DTYPE;
 }
 
