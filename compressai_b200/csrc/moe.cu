@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(1024) moe_route_token_kernel(const RouteArgs r
   {
     const float li = i < r.E ? sl[i] : -FLT_MAX;
     int rank = 0;
+#pragma unroll 8
     for (int j = part; j < r.E; j += PARTS) {
       const float o = sl[j];
       rank += (o > li || (o == li && j < i)) ? 1 : 0;
@@ -294,11 +295,14 @@ __global__ void __launch_bounds__(1024) moe_route_token_kernel(const RouteArgs r
     r.ids[row + tid] = (e >= r.lo && e < r.hi) ? e - r.lo : -1;
     r.w[row + tid] = expf(sel_v[tid] - mx) / sum;
   }
-  if (r.gate && tid == 32) {
-    float dd = 0.f;
-    for (int wv = 0; wv < 32; ++wv) dd += red[wv];
-    r.ids[row + r.K] = (t % r.world == r.rank) ? r.shared_row : -1;
-    r.w[row + r.K] = 1.f / (1.f + expf(-dd));
+  if (r.gate && warp == 1) {  // the 32 warp sums of the shared-gate dot product, by shuffles
+    float dd = red[lane];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dd += __shfl_xor_sync(0xffffffffu, dd, off);
+    if (lane == 0) {
+      r.ids[row + r.K] = (t % r.world == r.rank) ? r.shared_row : -1;
+      r.w[row + r.K] = 1.f / (1.f + expf(-dd));
+    }
   }
   // ---- forward RHT of the hidden row from shared memory into xrot
   {

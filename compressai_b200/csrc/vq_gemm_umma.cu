@@ -123,6 +123,34 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z)
       : "memory");
 }
+// The same MMA with the A operand read from tensor memory (lane = row, 16-bit K values packed two
+// per 32-bit column, K = 16 per instruction = 8 columns).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z)
+      : "memory");
+}
+
+// This thread's 32 consecutive 32-bit TMEM columns of its lane (32x32b shape; warp-collective),
+// waited for before returning.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint4 (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr), "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z),
+        "r"(v[1].w), "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z),
+        "r"(v[3].w), "r"(v[4].x), "r"(v[4].y), "r"(v[4].z), "r"(v[4].w), "r"(v[5].x), "r"(v[5].y), "r"(v[5].z),
+        "r"(v[5].w), "r"(v[6].x), "r"(v[6].y), "r"(v[6].z), "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z),
+        "r"(v[7].w)
+      : "memory");
+}
+
 // Arrive on `bar` once every MMA this thread issued so far has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -205,14 +233,26 @@ __device__ __forceinline__ UmItem um_decode(const GemvArgs& a, int64_t it, int N
   return w;
 }
 
-template <int NT, int S, bool RES, bool LO, typename TV>
+// Columns of a TMEM allocation: a power of two from 32 to 512.
+constexpr uint32_t tmem_cols(uint32_t need) {
+  return need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+}
+
+// AT: the decoded weight tile (MMA operand A) is written to tensor memory by the producers
+// (tcgen05.st) instead of to shared memory. Stage s's A tile then occupies TMEM columns
+// [2 NT + 32 s, +32) of all 128 lanes, and shared memory only carries the activation tiles.
+template <int NT, int S, bool RES, bool LO, typename TV, bool AT>
 __global__ void __launch_bounds__(kUmThreads, 1) vq_umma_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap xmap,
                                                                  const __grid_constant__ CUtensorMap lmap) {
-  constexpr int A_BYTES = kUmRows * 128;
+  constexpr int A_BYTES = AT ? 0 : kUmRows * 128;
   constexpr int B_BYTES = NT * 128;
   constexpr int STAGE = A_BYTES + B_BYTES * (LO ? 2 : 1);
-  constexpr uint32_t TMEM_COLS = 2 * NT < 32 ? 32 : 2 * NT;
+  constexpr uint32_t ACC_COLS = 2 * NT;                 // two accumulators of NT fp32 columns
+  constexpr uint32_t A_COL0 = ACC_COLS;                 // AT: first column of the A stages
+  constexpr uint32_t NEED_COLS = ACC_COLS + (AT ? 32u * S : 0u);
+  constexpr uint32_t TMEM_COLS = tmem_cols(NEED_COLS);
   constexpr uint32_t IDESC = umma_idesc<NT, std::is_same<TV, __nv_bfloat16>::value>();
+  static_assert(NEED_COLS <= 512, "accumulators and A stages exceed tensor memory");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzled tiles must stay 1024-byte aligned");
   static_assert(S % 2 == 0, "each producer group owns every other stage");
   extern __shared__ unsigned char um_raw[];
@@ -308,7 +348,10 @@ __global__ void __launch_bounds__(kUmThreads, 1) vq_umma_kernel(const GemvArgs a
           const uint32_t code = (j & 1) ? (w32 >> 16) : (w32 & 0xffffu);
           cw[j] = row_ok ? ld_cb_u4(cb0 + code, pol_c) : make_uint4(0, 0, 0, 0);
         }
-        if (!um_wait(su32(&ctl->empty[s]), (u & 1) ^ 1, ctl)) goto producer_exit;
+        {
+          const bool ok = um_wait(su32(&ctl->empty[s]), (u & 1) ^ 1, ctl);
+          if (!__all_sync(0xffffffffu, ok)) goto producer_exit;  // warp-uniform (tcgen05.st is collective)
+        }
         if (leader) {
           mbar_arrive_tx(su32(&ctl->tma[s]), B_BYTES * (LO ? 2 : 1));
           tma_load_2d(su32(stage_b(s)), &xmap, c * kUmKC, w.m0, su32(&ctl->tma[s]));
@@ -328,10 +371,17 @@ __global__ void __launch_bounds__(kUmThreads, 1) vq_umma_kernel(const GemvArgs a
             cw[j] = row_ok ? *reinterpret_cast<const uint4*>(o) : make_uint4(0, 0, 0, 0);
           }
         }
-        unsigned char* A = stage_a(s) + (r >> 3) * 1024 + (r & 7) * 128;
+        if constexpr (AT) {
+          // row r -> TMEM lane r (this warp's lane quarter), K values 2c, 2c+1 -> column c
+          tc_fence_after();
+          tmem_st32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + A_COL0 + 32u * s, cw);
+          tc_fence_before();
+        } else {
+          unsigned char* A = stage_a(s) + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(A + ((j ^ (r & 7)) << 4)) = cw[j];
-        fence_proxy_async();
+          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(A + ((j ^ (r & 7)) << 4)) = cw[j];
+          fence_proxy_async();
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(su32(&ctl->full[s]));
         iv = niv;
@@ -367,14 +417,25 @@ __global__ void __launch_bounds__(kUmThreads, 1) vq_umma_kernel(const GemvArgs a
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_desc(su32(stage_a(s)));
           const uint64_t bd = sw128_desc(su32(stage_b(s)));
+          if constexpr (AT) {
+            const uint32_t at = tmem + A_COL0 + 32u * s;
 #pragma unroll
-          for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16(d, ad + 2 * kk, bd + 2 * kk, IDESC, (c | kk) != 0);
-          if (LO) {
-            const uint64_t bl = sw128_desc(su32(stage_bl(s)));
+            for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16_ts(d, at + 8 * kk, bd + 2 * kk, IDESC, (c | kk) != 0);
+            if (LO) {
+              const uint64_t bl = sw128_desc(su32(stage_bl(s)));
 #pragma unroll
-            for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16(d, ad + 2 * kk, bl + 2 * kk, IDESC, 1);
+              for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16_ts(d, at + 8 * kk, bl + 2 * kk, IDESC, 1);
+            }
+          } else {
+            const uint64_t ad = sw128_desc(su32(stage_a(s)));
+#pragma unroll
+            for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16(d, ad + 2 * kk, bd + 2 * kk, IDESC, (c | kk) != 0);
+            if (LO) {
+              const uint64_t bl = sw128_desc(su32(stage_bl(s)));
+#pragma unroll
+              for (int kk = 0; kk < kUmKC / 16; ++kk) umma_f16(d, ad + 2 * kk, bl + 2 * kk, IDESC, 1);
+            }
           }
           umma_commit(su32(&ctl->empty[s]));
         }
@@ -469,17 +530,28 @@ bool make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, int S, bool RES, bool LO>
+template <int NT, int S, bool RES, bool LO, bool AT>
 constexpr size_t umma_smem() {
-  return 1024 + (size_t)S * (kUmRows * 128 + NT * 128 * (LO ? 2 : 1)) + (RES ? 4096 : 0) + sizeof(UmCtl<S>);
+  return 1024 + (size_t)S * ((AT ? 0 : kUmRows * 128) + NT * 128 * (LO ? 2 : 1)) + (RES ? 4096 : 0) +
+         sizeof(UmCtl<S>);
 }
 
-template <int NT, bool RES, typename TV>
+// Where the decoded weight tile goes: tensor memory (default) or shared memory (VQ2_UMMA_A=smem).
+bool umma_a_in_tmem() {
+  static const bool on = [] {
+    const char* v = std::getenv("VQ2_UMMA_A");
+    return !(v && std::strcmp(v, "smem") == 0);
+  }();
+  return on;
+}
+
+template <int NT, bool RES, typename TV, bool AT>
 int launch_umma(GemvArgs a, const void* xh, const void* xl, cudaStream_t st) {
   constexpr bool LO = std::is_same<TV, __nv_bfloat16>::value;
-  constexpr int S = NT * 128 * (LO ? 2 : 1) <= 8192 ? 4 : 2;  // stages of <= 24 KB (A 16 KB + B)
-  constexpr size_t smem = umma_smem<NT, S, RES, LO>();
-  auto kern = vq_umma_kernel<NT, S, RES, LO, TV>;
+  // four stages (two per producer group) of at most 24 KB of shared memory each
+  constexpr int S = AT || NT * 128 * (LO ? 2 : 1) <= 8192 ? 4 : 2;
+  constexpr size_t smem = umma_smem<NT, S, RES, LO, AT>();
+  auto kern = vq_umma_kernel<NT, S, RES, LO, TV, AT>;
   static std::atomic<uint64_t> done{0};
   static std::atomic<int> blocks_per_sm{0};
   int dev = 0;
@@ -530,12 +602,18 @@ int launch_umma(GemvArgs a, const void* xh, const void* xl, cudaStream_t st) {
   return launch_kernel(kern, dim3((unsigned)grid), dim3(kUmThreads), smem, st, a, xmap, lmap);
 }
 
+template <bool RES, typename TV, bool AT>
+int launch_umma_tile(const GemvArgs& a, const void* xh, const void* xl, cudaStream_t st) {
+  if (a.M <= 16) return launch_umma<16, RES, TV, AT>(a, xh, xl, st);
+  if (a.M <= 32) return launch_umma<32, RES, TV, AT>(a, xh, xl, st);
+  if (a.M <= 64) return launch_umma<64, RES, TV, AT>(a, xh, xl, st);
+  return launch_umma<128, RES, TV, AT>(a, xh, xl, st);
+}
+
 template <bool RES, typename TV>
 int launch_umma_nt(const GemvArgs& a, const void* xh, const void* xl, cudaStream_t st) {
-  if (a.M <= 16) return launch_umma<16, RES, TV>(a, xh, xl, st);
-  if (a.M <= 32) return launch_umma<32, RES, TV>(a, xh, xl, st);
-  if (a.M <= 64) return launch_umma<64, RES, TV>(a, xh, xl, st);
-  return launch_umma<128, RES, TV>(a, xh, xl, st);
+  return umma_a_in_tmem() ? launch_umma_tile<RES, TV, true>(a, xh, xl, st)
+                          : launch_umma_tile<RES, TV, false>(a, xh, xl, st);
 }
 
 int token_tile(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }

@@ -365,6 +365,33 @@ def test_tensor_core_path_without_workspace_falls_back_exactly(cbs):
     assert rel_err(y_cc.cpu().numpy(), y_tc.cpu().numpy()) < 3e-5
 
 
+def test_greedy_argmax_matches_reference_on_golden(cbs):
+    """vq2_gemv_argmax (keys and ids) on every golden case -- matrices quantized by the
+    reference's own quantizer, y computed by the reference's dequantize + fp64 matmul -- picks the
+    reference's argmax row for every activation row; a row whose reference logit is within the
+    GEMV tolerance of the maximum counts as a tie."""
+    from compressai_b200 import runtime
+    d = golden("gemv.npz")
+    cbd = dev_cbs(cbs)
+    names = sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_meta")})
+    checked = 0
+    for nm in names:
+        out, n, nst, M = (int(v) for v in d[f"{nm}_meta"])
+        bits = (16, 8) if nst > 1 else (16,)
+        idx = [d[f"{nm}_idx0"]] + ([d[f"{nm}_idx1"]] if nst > 1 else [])
+        lin = runtime.PackedLinear((out, n), bits, str(d[f"{nm}_tag"]),
+                                   [torch.from_numpy(np.ascontiguousarray(a)) for a in idx],
+                                   torch.from_numpy(np.asarray(d[f"{nm}_scale"])), cbd, DEV)
+        x = torch.from_numpy(np.asarray(d[f"{nm}_x"])).to(DEV)
+        got = lin.greedy(x).cpu().numpy()
+        ref = np.asarray(d[f"{nm}_y"], dtype=np.float64).reshape(M, out)
+        tol = TOL_F16 * np.abs(ref).max()
+        for m in range(M):
+            assert ref[m, got[m]] >= ref[m].max() - tol, (nm, m, int(got[m]), int(ref[m].argmax()))
+            checked += 1
+    assert checked >= len(names)
+
+
 @pytest.mark.parametrize("M,bits,ties", [(1, (16,), False), (3, (16, 8), False), (2, (16,), True)])
 def test_lm_head_fused_greedy_argmax(cbs, M, bits, ties):
     """vq2_gemv_argmax: the argmax of each activation row equals torch.argmax of the GEMV's own
