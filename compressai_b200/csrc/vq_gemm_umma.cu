@@ -9,11 +9,15 @@
 // walked in chunks of 64 (one 128-byte swizzle row of 16-bit values, 8 index groups). Roles:
 //   * warps 0-7, two groups of four (even / odd chunks): each thread owns one weight row of its
 //     group's chunks -- one 16-byte index load (prefetched one chunk ahead), 8 random 16-byte
-//     codebook gathers (L2 evict-last), 8 bank-conflict-free 16-byte stores into the A stage, a
-//     proxy fence and one mbarrier arrival per warp. The group's first thread also starts the
-//     TMA copy of the chunk's activation tile (NT x 64) into the B half of the same stage;
-//   * warp 8 allocates 2 x NT TMEM columns (two accumulators: the epilogue of one item runs
-//     while the next item accumulates) and its lane 0 issues the MMAs, 4 x (K = 16) per chunk,
+//     codebook gathers (L2 evict-last, issued before the wait for the stage), then the row's 64
+//     decoded values into the stage's A operand: by default one tcgen05.st into tensor memory
+//     (row -> TMEM lane, two 16-bit K values per 32-bit column), else 8 bank-conflict-free
+//     16-byte stores into a 128-byte-swizzled shared-memory tile and a proxy fence; then one
+//     mbarrier arrival per warp. The group's first thread also starts the TMA copy of the
+//     chunk's activation tile (NT x 64) into the stage's B tile in shared memory;
+//   * warp 8 allocates the TMEM columns (two accumulators of NT columns: the epilogue of one
+//     item runs while the next item accumulates; plus the A stages when A lives in TMEM) and its
+//     lane 0 issues the MMAs, 4 x (K = 16) per chunk,
 //     once the stage's gathers and its TMA copy have landed, then commits the stage back to its
 //     producers (tcgen05.commit -> mbarrier);
 //   * warps 9-12: epilogue -- tcgen05.ld of their 32-lane quarter of the accumulator (one weight
