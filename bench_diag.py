@@ -7,8 +7,9 @@ behind the launch lists and captures summarised in profiles/. Not part of the pa
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
       with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
       prologue (the MLP down projection); with --argmax the fused greedy argmax (keys only)
-  python bench_diag.py moe --T 1 --reps 3
-      `reps` MoE layers (router + expert FFN) over 256 resident seeded experts
+  python bench_diag.py moe --T 1 --reps 3 [--graph --layers 40]
+      `reps` MoE layers (router + expert FFN) over 256 resident seeded experts; with --graph,
+      `reps` replays of a CUDA graph of `layers` chained layers (each its own router logits)
   python bench_diag.py rans --n 16777216 --reps 2
       `reps` GPU decodes of one VQ2A stream of n skewed index bytes, then `reps` decodes of one
       ANS-coded expert record (vq2_rans_decode_segments)
@@ -102,6 +103,24 @@ def cmd_moe(a):
     blk = moe.MoEBlock(ex)
     h = torch.randn(a.T, 2048, device=dev).half()
     logits = torch.randn(a.T, a.E, device=dev)
+    if a.graph:  # `layers` chained layers, each with its own router logits, in one CUDA graph
+        lg = [torch.randn(a.T, a.E, device=dev) for _ in range(a.layers)]
+
+        def step():
+            x = h
+            for li in range(a.layers):
+                x = blk(x, lg[li])
+            return x
+        step()
+        torch.cuda.synchronize()
+        st = torch.cuda.Stream(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            step()
+        t = _time(g.replay, a.reps) / a.layers
+        print(json.dumps({"moe_T": a.T, "graph_layers": a.layers, "us_per_layer": round(t * 1e6, 2),
+                          "tok_s": round(a.T / (t * a.layers), 1)}))
+        return
     t = _time(lambda: blk(h, logits), a.reps)
     ids, _ = moe.route(logits, 8)
     distinct = int(torch.unique(ids).numel())
@@ -266,6 +285,8 @@ def main(argv=None):
     m.add_argument("--E", type=int, default=256)
     m.add_argument("--reps", type=int, default=3)
     m.add_argument("--seed", type=int, default=0)
+    m.add_argument("--graph", action="store_true")
+    m.add_argument("--layers", type=int, default=40)
     r = sub.add_parser("rans")
     r.add_argument("--n", type=int, default=1 << 24)
     r.add_argument("--reps", type=int, default=2)
