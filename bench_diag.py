@@ -55,7 +55,9 @@ def cmd_gather(a):
     clk = torch.cuda.get_device_properties(dev)
     sms = clk.multi_processor_count
     rows = [("global, 65536 rows (L2)", 0, 65536), ("global, 4096 rows (L1)", 0, 4096),
-            ("shared memory, 12288 rows", 1, 65536), ("cluster shared memory (8 CTAs)", 2, 65536)]
+            ("shared memory, 12288 rows", 1, 65536), ("cluster shared memory (8 CTAs)", 2, 65536),
+            ("bucketed entry: codeword + fp32 x from shared memory", 3, 65536),
+            ("bucketed entry: codeword + fp16 x from shared memory", 4, 65536)]
     out = []
     for name, mode, r in rows:
         g = kernels.gather_rate(cb, mode=mode, rows=r)

@@ -459,10 +459,23 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restric
   if (i >= T * H) return;
   const int64_t t = i / H, h = i - t * H;
   float s = add ? add[i] : 0.f;
-  for (int j = 0; j < top_k; ++j) {
-    const int64_t p = t * top_k + j;
-    if (ids && (ids[p] < 0 || ids[p] >= num_experts)) continue;  // problem not computed here
-    s = fmaf(w[p], y[p * H + h], s);
+  for (int j0 = 0; j0 < top_k; j0 += 8) {  // 8 problems' loads in flight, summed in problem order
+    bool ok[8];
+    float wp[8], yv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t p = t * top_k + j0 + k;
+      ok[k] = j0 + k < top_k && (!ids || (ids[p] >= 0 && ids[p] < num_experts));  // else not computed here
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t p = t * top_k + j0 + k;
+      wp[k] = ok[k] ? w[p] : 0.f;
+      yv[k] = ok[k] ? y[p * H + h] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (ok[k]) s = fmaf(wp[k], yv[k], s);
   }
   if (out_dtype == VQ2_F16) static_cast<__half*>(out)[i] = __float2half_rn(s);
   else if (out_dtype == VQ2_BF16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(s);

@@ -57,15 +57,30 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
   for (int64_t v = v0 + tid; v < v1; v += blockDim.x) {
     const int64_t el = v * 4, t = el / H, c = el - t * H;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < K; ++j) {
-      const int64_t p = t * K + j;
-      if (ids[p] < 0 || ids[p] >= num_experts) continue;  // problem computed on another rank
-      const float wp = w[p];
-      const float4 yv = *reinterpret_cast<const float4*>(y + p * H + c);
-      s.x = fmaf(wp, yv.x, s.x);
-      s.y = fmaf(wp, yv.y, s.y);
-      s.z = fmaf(wp, yv.z, s.z);
-      s.w = fmaf(wp, yv.w, s.w);
+    for (int j0 = 0; j0 < K; j0 += 8) {  // 8 problems' loads in flight, summed in problem order
+      bool ok[8];
+      float wp[8];
+      float4 yv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t p = t * K + j0 + k;
+        const int32_t id = j0 + k < K ? ids[p] : -1;
+        ok[k] = id >= 0 && id < num_experts;  // else computed on another rank
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t p = t * K + j0 + k;
+        wp[k] = ok[k] ? w[p] : 0.f;
+        yv[k] = ok[k] ? *reinterpret_cast<const float4*>(y + p * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (!ok[k]) continue;
+        s.x = fmaf(wp[k], yv[k].x, s.x);
+        s.y = fmaf(wp[k], yv[k].y, s.y);
+        s.z = fmaf(wp[k], yv[k].z, s.z);
+        s.w = fmaf(wp[k], yv[k].w, s.w);
+      }
     }
     for (int r = 0; r < world; ++r)
       reinterpret_cast<float4*>(peers[r] + part_off + (par * world + rank) * slot_bytes)[v] = s;

@@ -297,11 +297,14 @@ def moe_combine(y, w, top_k, add=None, out=None, out_dtype=torch.float16):
 
 def gather_rate(cb, mode=0, rows=None, iters=256, blocks_per_sm=8, reps=5):
     """Measured random 16-byte codebook-row gathers per second on cb's device (diagnostic;
-    mode 0 global memory, 1 shared memory, 2 cluster distributed shared memory)."""
+    mode 0 global memory, 1 shared memory, 2 cluster distributed shared memory; modes 3 / 4:
+    bucketed GEMV entries per second -- codeword and fp32 / fp16 activation both from shared
+    memory, one 1024-thread CTA per SM)."""
     _lib.require_cuda(cb)
     dev = cb.device
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    blocks = sms * blocks_per_sm if mode == 0 else (sms if mode == 1 else sms // 8 * 8)
+    blocks = sms * blocks_per_sm if mode == 0 else (sms // 8 * 8 if mode == 2 else sms)
+    threads = 1024 if mode in (3, 4) else 256
     rows = rows or cb.shape[0]
     sink = torch.zeros(1, dtype=torch.int32, device=dev)
     st = _lib.stream_ptr(dev)
@@ -313,4 +316,4 @@ def gather_rate(cb, mode=0, rows=None, iters=256, blocks_per_sm=8, reps=5):
         _lib.call("vq2_gather_probe", *args)
     e1.record()
     e1.synchronize()
-    return reps * blocks * 256 * iters * 8 / (e0.elapsed_time(e1) / 1e3)
+    return reps * blocks * threads * iters * 8 / (e0.elapsed_time(e1) / 1e3)

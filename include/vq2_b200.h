@@ -434,7 +434,10 @@ VQ2_API int vq2_moe_expert_ffn_noalloc(const void* h, int h_dtype, int64_t T, in
  * of a [65536, 8] fp16/bf16 codebook cb, with uniform random row indices, through
  *   mode 0: global memory (the GEMV's load form); rows <= 65536 limits the rows touched;
  *   mode 1: shared memory (each CTA stages the first 12,288 rows; rows must be 65536);
- *   mode 2: distributed shared memory of an 8-CTA cluster holding the whole table (rows 65536).
+ *   mode 2: distributed shared memory of an 8-CTA cluster holding the whole table (rows 65536);
+ *   modes 3 / 4: `blocks` x 1024 threads, each CTA holding one 8192-row bucket of the table and a
+ *           2048-value activation row (fp32 / fp16) in shared memory; each of the 8 * iters steps
+ *           is one bucketed GEMV entry (codeword read + activation read + 8-wide dot product).
  * Timing it gives the random codebook-gather rate that bounds the M = 1 VQ GEMV.
  * sink: one uint32 of device memory. No reference counterpart (measurement aid).
  */
