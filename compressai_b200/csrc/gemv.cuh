@@ -172,6 +172,18 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
               const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid, void* ws,
               int64_t ws_bytes, void* out, int out_dtype, cudaStream_t st, const PeerReduce* peer);
 
+// One-token MoE layer in two launches (moe_decode.cu): routing recomputed per CTA, gate_up rows
+// into `gu` ([K + 1, 1024] fp32), then the down rows over all problems with the combine, into
+// `out` (out_dtype; fp32 for a rank's partial). Returns -1 when the shapes are not the
+// specialisation's (hidden 2048, intermediate 512, top-k <= 8, E <= 256, 2 bpw) or VQ2_MOE_T1=0.
+int run_moe_t1(const void* h, int h_dtype, const float* logits, int64_t E, int64_t K, const float* shared_gate,
+               int64_t lo, int64_t hi, int rank, int world, const void* pool, int64_t pool_rows, int64_t gu_rows,
+               int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
+               const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in, const int32_t* perm_mid,
+               const int8_t* sign_mid, int64_t hb_mid, float scale_mid, int64_t rec, int64_t off_gu_idx,
+               int64_t off_gu_scale, int64_t off_dn_idx, int64_t off_dn_scale, float* gu, void* out, int out_dtype,
+               cudaStream_t st);
+
 // Fused single-launch expert FFN for T * top_k <= 64 (moe_fused.cu).
 struct MoeFusedArgs {
   const void* h;

@@ -64,13 +64,13 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int64_t p = t * K + j0 + k;
-        const int32_t id = j0 + k < K ? ids[p] : -1;
+        const int32_t id = j0 + k < K ? (ids ? ids[p] : 0) : -1;  // ids null: every problem local
         ok[k] = id >= 0 && id < num_experts;  // else computed on another rank
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int64_t p = t * K + j0 + k;
-        wp[k] = ok[k] ? w[p] : 0.f;
+        wp[k] = ok[k] ? (w ? w[p] : 1.f) : 0.f;  // w null: weight 1 (y is an already combined partial)
         yv[k] = ok[k] ? *reinterpret_cast<const float4*>(y + p * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll

@@ -212,6 +212,18 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
   if (ws_bytes < L.bytes) return VQ2_ERR_ARG;
   const int64_t P = T * ks;
 
+  if (T == 1) {  // one token: routing recomputed inside two launches (moe_decode.cu)
+    const int s1 = run_moe_t1(h, h_dtype, logits, E, K, shared_gate, lo, hi, rank, world, pool, pool_rows, gu_rows,
+                              gu_cols, dn_rows, dn_cols, cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid,
+                              sign_mid, hb_mid, scale_mid, R.bytes, R.gu_idx, R.gu_scale, R.dn_idx, R.dn_scale, L.gu,
+                              peer ? static_cast<void*>(L.yd) : out, peer ? VQ2_F32 : out_dtype, st);
+    if (s1 != -1) {
+      if (s1 != VQ2_OK || !peer) return s1;
+      // the partial is already combined: one "problem" per token, weight 1, all local
+      return run_combine_peer(L.yd, nullptr, 1, 1, H, nullptr, 1, *peer, out, out_dtype, st);
+    }
+  }
+
   RouteArgs r{};
   r.logits = logits; r.T = (int)T; r.E = (int)E; r.K = (int)K;
   r.h = h; r.h_dtype = h_dtype; r.H = (int)H; r.gate = shared_gate;

@@ -138,6 +138,36 @@ def test_moe_layer_equals_route_plus_expert_ffn(cbs, T):
         assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
 
 
+@pytest.mark.parametrize("K,shared", [(8, True), (8, False), (4, True)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_moe_layer_one_token_path_bitwise(cbs, monkeypatch, K, shared, out_dtype):
+    """A one-token layer runs in two launches that each route the token themselves
+    (moe_decode.cu); routing keys, weights, shared gate, staging, FMA, shuffle and combine order
+    are those of the router kernel + GEMVs, so the outputs are bit-identical to that path
+    (VQ2_MOE_T1=0), for the whole layer and for a rank's expert slice."""
+    sh = synth.synth_expert(96, 0)
+    full = resident_pool(14, 256, extra=sh)
+    ex = moe.PackedMoEExpertUniversal(full, cb16_dev(cbs), DEV, shared=True)
+    g = torch.from_numpy((0.05 * np.random.default_rng(11).standard_normal(2048)).astype(np.float32)).to(DEV)
+    h = torch.from_numpy(np.random.default_rng(12).standard_normal((1, 2048)).astype(np.float16)).to(DEV)
+    slice_pool = moe.ExpertRecordPool(64 + 1, DEV)
+    slice_pool.raw[:64].copy_(full.raw[64:128])
+    slice_pool.raw[64].copy_(full.raw[256])
+    for trial in range(3):
+        lg = torch.randn(1, 256, device=DEV)
+        lg[0, 64:128] += 1.5 * trial  # from a few of the slice's experts to most of them
+        cases = [dict(pool=full, hi=256), dict(pool=slice_pool, lo=64, hi=128, rank=1, world=4)]
+        for kw in cases:
+            pool = kw.pop("pool")
+            outs = []
+            for env in ("1", "0"):
+                monkeypatch.setenv("VQ2_MOE_T1", env)
+                outs.append(moe.moe_layer(h, lg, pool, ex.cb16, ex.rot_2048, ex.rot_512, K,
+                                          shared_gate=g if shared else None, out_dtype=out_dtype, **kw))
+            assert torch.equal(outs[0], outs[1]), (trial, kw)
+            assert torch.isfinite(outs[0].float()).all()
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("T", [1, 5, 32])
 def test_moe_layer_rank_partials_sum_to_full_layer(cbs, world, T):
