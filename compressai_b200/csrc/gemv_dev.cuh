@@ -55,7 +55,10 @@ __device__ __forceinline__ void fwht8(float v[8]) {
   }
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+// silu(g) = g * sigmoid(g). Fast division (reciprocal + multiply): the IEEE-exact divide is a
+// multi-instruction sequence, and the staging of a SwiGLU row evaluates thousands of these.
+// 1 + exp(-g) beyond 2^126 (g < -87) gives 0, the limit of g * sigmoid(g).
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
 // Shared-memory ("fast") staging, used by the GEMV kernels: the rotation table is loaded into
 // shared memory before the dependency wait (it is constant), the activation rows are read after

@@ -42,7 +42,10 @@ __device__ __forceinline__ float ldx(const void* x, int64_t i) {
   return to_f32<TX>(static_cast<const TX*>(x)[i]);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+// silu(g) = g * sigmoid(g). Fast division (reciprocal + multiply): the IEEE-exact divide is a
+// multi-instruction sequence, and the staging of a SwiGLU row evaluates thousands of these.
+// 1 + exp(-g) beyond 2^126 (g < -87) gives 0, the limit of g * sigmoid(g).
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
 // TO = float: fp32 result in xr. TO = __half / __nv_bfloat16 (forward modes only): the result w
 // stored as hi = TO(w) in xr and lo = TO(w - float(hi)) in xl, both [M, n] with row stride
