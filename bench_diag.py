@@ -7,7 +7,7 @@ behind the launch lists and captures summarised in profiles/. Not part of the pa
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
       with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
       prologue (the MLP down projection); with --argmax the fused greedy argmax (keys only)
-  python bench_diag.py moe --T 1 --reps 3 [--graph --layers 40]
+  python bench_diag.py moe --T 1 --reps 3 [--graph --layers 40] [--shared]
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts; with --graph,
       `reps` replays of a CUDA graph of `layers` chained layers (each its own router logits)
   python bench_diag.py rans --n 16777216 --reps 2
@@ -101,8 +101,12 @@ def cmd_moe(a):
                                                    device=dev, dtype=torch.int16))
     pool.gu_scale.copy_(0.02 * torch.ones_like(pool.gu_scale))
     pool.dn_scale.copy_(0.02 * torch.ones_like(pool.dn_scale))
-    ex = moe.PackedMoEExpertUniversal(pool, cbs["16"], dev)
-    blk = moe.MoEBlock(ex)
+    if a.shared:  # the last pool row serves as the shared expert, with a seeded gate vector
+        ex = moe.PackedMoEExpertUniversal(pool, cbs["16"], dev, shared=True)
+        blk = moe.MoEBlock(ex, shared_gate=0.02 * torch.randn(2048, device=dev))
+    else:
+        ex = moe.PackedMoEExpertUniversal(pool, cbs["16"], dev)
+        blk = moe.MoEBlock(ex)
     h = torch.randn(a.T, 2048, device=dev).half()
     logits = torch.randn(a.T, a.E, device=dev)
     if a.graph:  # `layers` chained layers, each with its own router logits, in one CUDA graph
@@ -289,6 +293,7 @@ def main(argv=None):
     m.add_argument("--seed", type=int, default=0)
     m.add_argument("--graph", action="store_true")
     m.add_argument("--layers", type=int, default=40)
+    m.add_argument("--shared", action="store_true", help="the last pool row as a shared expert (9 problems)")
     r = sub.add_parser("rans")
     r.add_argument("--n", type=int, default=1 << 24)
     r.add_argument("--reps", type=int, default=2)

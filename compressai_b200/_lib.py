@@ -55,6 +55,9 @@ SIGNATURES = {
     "vq2_moe_expert_ffn_workspace": [_i64, _i64, _i64, _i64],
     "vq2_moe_expert_ffn_noalloc": [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p,
                                    _i64, _f32, _p, _p, _i64, _f32, _p, _i32, _p],
+    "vq2_paged_moe_t1_workspace": [_i64],
+    "vq2_paged_moe_t1": [_p, _i32, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i32, _p, _p, _i64,
+                         _f32, _p, _p, _i64, _f32, _p, _p, _i64, _p, _i64, _p, _i32, _p],
     "vq2_rans_bound": [_i64],
     "vq2_rans_encode": [_p, _i64, _p, _i64, _p],
     "vq2_rans_decode": [_p, _i64, _i64, _p, _i64, _p, _p],

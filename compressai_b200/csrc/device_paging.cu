@@ -16,66 +16,85 @@ namespace vq2 {
 
 constexpr int kLruHdr = 8;
 
-__global__ void lru_step_kernel(int32_t* __restrict__ st, const int32_t* __restrict__ ids, int K,
-                                int32_t* __restrict__ slots, int32_t* __restrict__ miss) {
+// The decision itself is serial (one thread). The CTA first copies the layer's state into
+// shared memory with coalesced loads (when it fits kLruSmemInts), so the ~5 dependent accesses per
+// id are shared-memory round trips instead of L2 ones, and copies it back at the end.
+constexpr int kLruSmemInts = 12288;  // 48 KB: E up to ~4000 experts per layer
+
+__global__ void __launch_bounds__(256) lru_step_kernel(int32_t* __restrict__ gst, const int32_t* __restrict__ ids,
+                                                       int K, int32_t* __restrict__ slots,
+                                                       int32_t* __restrict__ miss) {
+  extern __shared__ int32_t sst[];
   pdl_wait();
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const int cap = st[5], E = st[6];
-  int32_t* e2s = st + kLruHdr;
-  int32_t* prv = e2s + E;
-  int32_t* nxt = prv + E;
-  int32_t* fre = nxt + E;
-  int head = st[0], tail = st[1], nfree = st[2], hits = st[3], misses = st[4], err = st[7];
-  auto unlink = [&](int x) {
-    const int p = prv[x], n = nxt[x];
-    if (p >= 0) nxt[p] = n; else head = n;
-    if (n >= 0) prv[n] = p; else tail = p;
-  };
-  auto append = [&](int x) {
-    prv[x] = tail;
-    nxt[x] = -1;
-    if (tail >= 0) nxt[tail] = x; else head = x;
-    tail = x;
-  };
-  int nm = 0;
-  for (int k = 0; k < K; ++k) {
-    const int e = ids[k];
-    if (e < 0 || e >= E) {  // not an expert of this pool: contributes nothing
-      slots[k] = -1;
-      continue;
-    }
-    int s = e2s[e];
-    if (s >= 0) {
-      ++hits;
-      unlink(e);
-      append(e);
-    } else {
-      ++misses;
-      if (nfree > 0) {
-        s = fre[--nfree];
-      } else if (head >= 0) {
-        const int old = head;
-        unlink(old);
-        s = e2s[old];
-        e2s[old] = -1;
-        for (int j = 0; j < k; ++j)  // a slot still needed by this step must not be reused
-          if (slots[j] == s) err = 1;
-      } else {
-        err = 1;  // capacity 0
+  const int64_t nints = kLruHdr + 3 * (int64_t)gst[6] + gst[5];  // header: capacity, experts
+  const bool in_smem = nints <= kLruSmemInts;
+  int32_t* st = gst;
+  if (in_smem) {
+    for (int i = threadIdx.x; i < nints; i += blockDim.x) sst[i] = gst[i];
+    __syncthreads();
+    st = sst;
+  }
+  if (threadIdx.x == 0) {
+    const int E = st[6];
+    int32_t* e2s = st + kLruHdr;
+    int32_t* prv = e2s + E;
+    int32_t* nxt = prv + E;
+    int32_t* fre = nxt + E;
+    int head = st[0], tail = st[1], nfree = st[2], hits = st[3], misses = st[4], err = st[7];
+    auto unlink = [&](int x) {
+      const int p = prv[x], n = nxt[x];
+      if (p >= 0) nxt[p] = n; else head = n;
+      if (n >= 0) prv[n] = p; else tail = p;
+    };
+    auto append = [&](int x) {
+      prv[x] = tail;
+      nxt[x] = -1;
+      if (tail >= 0) nxt[tail] = x; else head = x;
+      tail = x;
+    };
+    int nm = 0;
+    for (int k = 0; k < K; ++k) {
+      const int e = ids[k];
+      if (e < 0 || e >= E) {  // not an expert of this pool: contributes nothing
         slots[k] = -1;
         continue;
       }
-      e2s[e] = s;
-      append(e);
-      miss[1 + nm] = e;
-      miss[1 + K + nm] = s;
-      ++nm;
+      int s = e2s[e];
+      if (s >= 0) {
+        ++hits;
+        unlink(e);
+        append(e);
+      } else {
+        ++misses;
+        if (nfree > 0) {
+          s = fre[--nfree];
+        } else if (head >= 0) {
+          const int old = head;
+          unlink(old);
+          s = e2s[old];
+          e2s[old] = -1;
+          for (int j = 0; j < k; ++j)  // a slot still needed by this step must not be reused
+            if (slots[j] == s) err = 1;
+        } else {
+          err = 1;  // capacity 0
+          slots[k] = -1;
+          continue;
+        }
+        e2s[e] = s;
+        append(e);
+        miss[1 + nm] = e;
+        miss[1 + K + nm] = s;
+        ++nm;
+      }
+      slots[k] = s;
     }
-    slots[k] = s;
+    miss[0] = nm;
+    st[0] = head; st[1] = tail; st[2] = nfree; st[3] = hits; st[4] = misses; st[7] = err;
   }
-  miss[0] = nm;
-  st[0] = head; st[1] = tail; st[2] = nfree; st[3] = hits; st[4] = misses; st[7] = err;
-  (void)cap;
+  if (in_smem) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < nints; i += blockDim.x) gst[i] = sst[i];
+  }
 }
 
 // Copy the missed records (miss list of lru_step_kernel) from the host image into their slots:
@@ -107,8 +126,17 @@ extern "C" int vq2_lru_step(int32_t* state, const int32_t* ids, int64_t K, int32
                             void* stream) {
   if (!state || !ids || !slots || !miss) return VQ2_ERR_ARG;
   if (K <= 0 || K > 64) return VQ2_ERR_SHAPE;
-  return vq2::launch_kernel(vq2::lru_step_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), state,
-                            ids, static_cast<int>(K), slots, miss);
+  static int attr_done[64] = {};  // per device: 48 KB of dynamic shared memory for the state copy
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    const cudaError_t e = cudaFuncSetAttribute(vq2::lru_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               vq2::kLruSmemInts * 4);
+    if (e != cudaSuccess) { vq2::set_last_cuda_error(e); return VQ2_ERR_LAUNCH; }
+    attr_done[dev & 63] = 1;
+  }
+  return vq2::launch_kernel(vq2::lru_step_kernel, dim3(1), dim3(256), (size_t)vq2::kLruSmemInts * 4,
+                            static_cast<cudaStream_t>(stream), state, ids, static_cast<int>(K), slots, miss);
 }
 
 extern "C" int vq2_fetch_records(const void* image_dev, const int64_t* rec_off, int64_t rec_bytes, void* pool,

@@ -138,11 +138,50 @@ struct RouteArgs {
 int run_route(const RouteArgs& r, cudaStream_t st);
 
 // Cross-GPU reduction of the expert-parallel combine over peer memory (moe_ep.cu).
-constexpr int kPeerMaxBlocks = 128;  // CTAs (output ranges) of the peer combine, at most
+constexpr int kPeerMaxBlocks = 128;    // CTAs (output ranges) of the peer combine, at most
+constexpr int kPeerFlagStride = 512;   // flags per rank in the symmetric buffer: CTAs of one exchange, at most
+constexpr int kPeerWaitPolls = 1 << 22;  // default poll limit of a peer wait, ~1 s at 64 ns naps
+constexpr int kPeerTimeout = 0x200;      // status word of a wait that gave up
+constexpr int kPeerTightPolls = 2048;    // polls before napping between them
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// One thread of CTA b, after a CTA barrier that follows the CTA's peer stores: a system-scope
+// fence, sequence number e into flag [rank][b] of every peer's buffer (release stores), then a
+// bounded wait (max_polls polls per peer, napping after the first kPeerTightPolls) until flag
+// [q][b] of the local buffer has reached e for every peer q. A wait that gives up raises *err
+// (kPeerTimeout) and returns false; nothing traps.
+__device__ inline bool peer_flags_exchange(uint8_t* const* peers, int rank, int world, int b, uint32_t e,
+                                           int max_polls, int32_t* err) {
+  fence_acq_rel_sys();
+  for (int q = 0; q < world; ++q)
+    if (q != rank) st_release_sys(reinterpret_cast<uint32_t*>(peers[q]) + rank * kPeerFlagStride + b, e);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers[rank]);
+  bool ok = true;
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    int it = 0;
+    while ((int)(ld_acquire_sys(flags + q * kPeerFlagStride + b) - e) < 0 && it < max_polls) {
+      if (it >= kPeerTightPolls) __nanosleep(64);
+      ++it;
+    }
+    if (it == max_polls) ok = false;
+  }
+  if (!ok && err) atomicMax(err, kPeerTimeout);
+  return ok;
+}
 struct PeerReduce {
   uint8_t* const* peers;  // device array [world] of the symmetric buffers' base addresses
   int rank, world;
-  int64_t part_off;       // bytes: flags region (world x kPeerMaxBlocks uint32) padded
+  int64_t part_off;       // bytes: flags region (world x kPeerFlagStride uint32) padded
   int64_t part_bytes;     // bytes of one (parity, rank) slot (>= T x H fp32)
   int32_t* epochs;        // local device state {sequence number, finished CTAs}, zero at first use
   int32_t* err;           // optional status word (timeouts)
@@ -174,8 +213,8 @@ int moe_layer(const void* h, int h_dtype, int64_t T, const float* logits, int64_
 
 // One-token MoE layer in two launches (moe_decode.cu): routing recomputed per CTA, gate_up rows
 // into `gu` ([K + 1, 1024] fp32), then the down rows over all problems with the combine, into
-// `out` (out_dtype; fp32 for a rank's partial). Returns -1 when the shapes are not the
-// specialisation's (hidden 2048, intermediate 512, top-k <= 8, E <= 256, 2 bpw) or VQ2_MOE_T1=0.
+// `out` (out_dtype; fp32 for a rank's partial). Returns -1 when the shapes are not the specialisation's (hidden
+// 2048, intermediate 512, top-k <= 8, E <= 256, 2 bpw) or VQ2_MOE_T1=0.
 int run_moe_t1(const void* h, int h_dtype, const float* logits, int64_t E, int64_t K, const float* shared_gate,
                int64_t lo, int64_t hi, int rank, int world, const void* pool, int64_t pool_rows, int64_t gu_rows,
                int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,

@@ -12,7 +12,7 @@
 //      problem's gate_up row, and each warp computes one output row over ALL problems and sums
 //      them with the routing weights in problem order -- the combine needs no second pass and no
 //      cross-CTA counters. The output is the layer's hidden row, or (expert parallelism) this
-//      rank's fp32 partial for the peer combine.
+//      rank's fp32 partial, which the peer combine kernel sums over the ranks.
 //
 // Why: a single token's routing on one 1024-thread CTA (the general router) costs ~6 us of
 // serial work on one SM while the other 147 wait (rank counting ~2.3 us, the RHT of the hidden
@@ -64,6 +64,17 @@ struct MoeT1Args {
   float* gu;                // [K + 1, 1024] fp32 gate_up rows by original problem index
   void* out;                // [H] out_dtype
   int out_dtype;
+  // paged mode (ids_in != null): the token's experts, weights and pool slots come from the device
+  // LRU step, and a record missed in this step is read from the pinned host image by the kernels
+  // that use it, which write it into its slot on the way (gate_up rows by launch 1, down rows by
+  // launch 2: together the whole record)
+  const int32_t* ids_in;    // [K] expert ids of the layer (image offsets)
+  const int32_t* slots;     // [K] pool slots, -1: skipped
+  const int32_t* miss;      // LRU miss list {count, expert[K], slot[K]}
+  const float* w_in;        // [K] routing weights
+  const uint8_t* image;     // device address of the page-locked image
+  const int64_t* rec_off;   // [num_experts] record offsets in the image
+  int64_t num_experts;
 };
 
 // The routing of one token as every CTA computes it.
@@ -74,6 +85,8 @@ struct T1Route {
   float sel_v[kT1MaxK];
   int pid[kT1MaxP];   // pool row of compacted problem c
   int pmap[kT1MaxP];  // its original problem index (0..K-1 routed, K shared)
+  const uint8_t* src[kT1MaxP];  // record to read: the pool row, or (paged miss) the image's copy
+  uint8_t* dst[kT1MaxP];        // paged miss: the pool slot the record is written to; else null
   int P;
 };
 
@@ -127,12 +140,52 @@ __device__ __forceinline__ void t1_route(const MoeT1Args& a, T1Route& s) {
       if (id >= 0 && id < a.pool_rows) {
         s.pid[P] = id;
         s.pmap[P] = j;
+        s.src[P] = a.pool + id * a.rec;
+        s.dst[P] = nullptr;
         ++P;
       }
     }
     s.P = P;
   }
   __syncthreads();
+}
+
+// Paged mode: the problem list from the LRU step's slots (in k order, skipping -1), the record
+// of a slot on the step's miss list read from the image. All 256 threads; ends with a barrier.
+__device__ __forceinline__ void t1_problems_paged(const MoeT1Args& a, T1Route& s) {
+  if (threadIdx.x == 0) {
+    const int nm = min(max(__ldcg(a.miss), 0), a.K);
+    int P = 0;
+    for (int j = 0; j < a.K; ++j) {
+      const int sl = __ldcg(a.slots + j), e = __ldcg(a.ids_in + j);
+      if (sl < 0 || sl >= a.pool_rows || e < 0 || e >= a.num_experts) continue;
+      bool missed = false;
+      for (int m = 0; m < nm; ++m) missed |= __ldcg(a.miss + 1 + a.K + m) == sl;
+      uint8_t* slot = const_cast<uint8_t*>(a.pool) + sl * a.rec;
+      s.pid[P] = sl;
+      s.pmap[P] = j;
+      s.src[P] = missed ? a.image + __ldcg(a.rec_off + e) : slot;
+      s.dst[P] = missed ? slot : nullptr;
+      ++P;
+    }
+    s.P = P;
+  }
+  __syncthreads();
+}
+
+// 16 bytes of a record: from the pool (streaming load), or from the host image (plain load),
+// then written into the slot.
+__device__ __forceinline__ uint4 t1_rec_u4(const uint8_t* src, uint8_t* dst, int64_t off, uint64_t pol) {
+  if (dst == nullptr) return ld_stream_u4(src + off, pol);
+  const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+  *reinterpret_cast<uint4*>(dst + off) = v;
+  return v;
+}
+template <typename TV>
+__device__ __forceinline__ float t1_rec_scale(const uint8_t* src, uint8_t* dst, int64_t off, bool store) {
+  const TV v = *reinterpret_cast<const TV*>(src + off);
+  if (dst != nullptr && store) *reinterpret_cast<TV*>(dst + off) = v;
+  return to_f32<TV>(v);
 }
 
 // Forward RHT (blocks of HB = the row length) of `rows` rows of the tile in place: raw values at
@@ -228,7 +281,8 @@ __global__ void __launch_bounds__(256, 2) moe_t1_gate_up_kernel(const MoeT1Args 
   pdl_trigger();
   float hv[8];
   t1_load8(a.h, a.h_dtype, 8 * tid, hv);  // in flight with the logits of the routing
-  t1_route(a, rt);
+  if (a.ids_in) t1_problems_paged(a, rt);
+  else t1_route(a, rt);
   const int P = rt.P;
   const int64_t R = (int64_t)P * kT1GuRows;
   const int64_t lo = blockIdx.x * R / gridDim.x, hi = (blockIdx.x + 1) * R / gridDim.x;
@@ -242,9 +296,8 @@ __global__ void __launch_bounds__(256, 2) moe_t1_gate_up_kernel(const MoeT1Args 
       sv[rw] = 0.f;
       if (q < npairs && g < hi) {
         const int c = (int)(g / kT1GuRows), r = (int)(g % kT1GuRows);
-        const uint8_t* rec = a.pool + rt.pid[c] * a.rec;
-        iv[rw] = ld_stream_u4(rec + a.off_gu_idx + ((int64_t)r * (kT1H / 8) + lane * 8) * 2, pol_s);
-        if (lane == 0) sv[rw] = to_f32<TV>(reinterpret_cast<const TV*>(rec + a.off_gu_scale)[r]);
+        iv[rw] = t1_rec_u4(rt.src[c], rt.dst[c], a.off_gu_idx + ((int64_t)r * (kT1H / 8) + lane * 8) * 2, pol_s);
+        if (lane == 0) sv[rw] = t1_rec_scale<TV>(rt.src[c], rt.dst[c], a.off_gu_scale + 2 * r, true);
       }
     }
   };
@@ -338,12 +391,15 @@ __global__ void __launch_bounds__(256, 2) moe_t1_down_kernel(const MoeT1Args a) 
 #pragma unroll
     for (int k = 0; k < 8; ++k) d = fmaf(hv[k], gv[k], d);
   }
-  t1_route(a, rt);
+  if (a.ids_in) t1_problems_paged(a, rt);
+  else t1_route(a, rt);
   const int P = rt.P;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
   if (lane == 0) s_red[warp] = d;
-  if (tid < a.K) {
+  if (a.ids_in) {
+    if (tid < a.K) s_wj[tid] = __ldcg(a.w_in + tid);
+  } else if (tid < a.K) {
     const float mx = rt.sel_v[0];
     float sum = 0.f;
     for (int k = 0; k < a.K; ++k) sum += expf(rt.sel_v[k] - mx);
@@ -370,9 +426,8 @@ __global__ void __launch_bounds__(256, 2) moe_t1_down_kernel(const MoeT1Args a) 
     iv[q] = make_uint4(0, 0, 0, 0);
     sc[q] = 0.f;
     if (row_ok && p < P) {
-      const uint8_t* rec = a.pool + rt.pid[p] * a.rec;
-      iv[q] = ld_stream_u4(rec + a.off_dn_idx + ((int64_t)r * (kT1I / 8) + li * 8) * 2, pol_s);
-      sc[q] = to_f32<TV>(reinterpret_cast<const TV*>(rec + a.off_dn_scale)[r]);
+      iv[q] = t1_rec_u4(rt.src[p], rt.dst[p], a.off_dn_idx + ((int64_t)r * (kT1I / 8) + li * 8) * 2, pol_s);
+      sc[q] = t1_rec_scale<TV>(rt.src[p], rt.dst[p], a.off_dn_scale + 2 * r, li == 0);
     }
   }
   pdl_wait();
@@ -466,6 +521,16 @@ static int launch_t1(const MoeT1Args& a, cudaStream_t st) {
   return launch_kernel(k2, grid, dim3(256), (size_t)s2, st, a);
 }
 
+// Shape checks shared by both modes: -1 when the layer is not the specialisation's.
+static int t1_shapes_ok(int64_t K, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, int64_t hb_in,
+                        int64_t hb_mid, int val_dtype) {
+  if (K <= 0 || K > kT1MaxK) return -1;
+  if (gu_cols * 8 != kT1H || gu_rows != kT1GuRows || dn_rows != kT1H || dn_cols * 8 != kT1I) return -1;
+  if (hb_in != kT1H || hb_mid != kT1I) return -1;
+  if (val_dtype != VQ2_F16 && val_dtype != VQ2_BF16) return -1;
+  return 0;
+}
+
 int run_moe_t1(const void* h, int h_dtype, const float* logits, int64_t E, int64_t K, const float* shared_gate,
                int64_t lo, int64_t hi, int rank, int world, const void* pool, int64_t pool_rows, int64_t gu_rows,
                int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
@@ -474,10 +539,8 @@ int run_moe_t1(const void* h, int h_dtype, const float* logits, int64_t E, int64
                int64_t off_gu_scale, int64_t off_dn_idx, int64_t off_dn_scale, float* gu, void* out, int out_dtype,
                cudaStream_t st) {
   if (!moe_t1_enabled()) return -1;
-  if (E <= 0 || E > kT1MaxE || K <= 0 || K > kT1MaxK || K > E) return -1;
-  if (gu_cols * 8 != kT1H || gu_rows != kT1GuRows || dn_rows != kT1H || dn_cols * 8 != kT1I) return -1;
-  if (hb_in != kT1H || hb_mid != kT1I) return -1;
-  if (val_dtype != VQ2_F16 && val_dtype != VQ2_BF16) return -1;
+  if (E <= 0 || E > kT1MaxE || K > E) return -1;
+  if (t1_shapes_ok(K, gu_rows, gu_cols, dn_rows, dn_cols, hb_in, hb_mid, val_dtype) != 0) return -1;
   if (!aligned(h, 16) || !aligned(gu, 16) || (shared_gate && !aligned(shared_gate, 16)) || !aligned(perm_in, 16) ||
       !aligned(sign_in, 4) || !aligned(perm_mid, 16) || !aligned(sign_mid, 4))
     return -1;
@@ -492,4 +555,57 @@ int run_moe_t1(const void* h, int h_dtype, const float* logits, int64_t E, int64
   return val_dtype == VQ2_F16 ? launch_t1<__half>(a, st) : launch_t1<__nv_bfloat16>(a, st);
 }
 
+// Paged mode (vq2_paged_moe_t1): the same two launches on the LRU step's slots.
+int run_moe_t1_paged(const void* h, int h_dtype, int64_t K, const int32_t* ids, const int32_t* slots,
+                     const int32_t* miss, const float* w, const void* pool, int64_t capacity, int64_t gu_rows,
+                     int64_t gu_cols, int64_t dn_rows, int64_t dn_cols, const void* cb0, int val_dtype,
+                     const int32_t* perm_in, const int8_t* sign_in, int64_t hb_in, float scale_in,
+                     const int32_t* perm_mid, const int8_t* sign_mid, int64_t hb_mid, float scale_mid,
+                     const void* image, const int64_t* rec_off, int64_t num_experts, float* gu, void* out,
+                     int out_dtype, cudaStream_t st) {
+  if (t1_shapes_ok(K, gu_rows, gu_cols, dn_rows, dn_cols, hb_in, hb_mid, val_dtype) != 0) return VQ2_ERR_SHAPE;
+  if (!aligned(h, 16) || !aligned(gu, 16) || !aligned(pool, 16) || !aligned(image, 16) || !aligned(cb0, 16) ||
+      !aligned(perm_in, 16) || !aligned(sign_in, 4) || !aligned(perm_mid, 16) || !aligned(sign_mid, 4))
+    return VQ2_ERR_ALIGN;
+  MoeT1Args a{};
+  a.h = h; a.h_dtype = h_dtype; a.K = (int)K; a.E = 0; a.gate = nullptr;
+  a.pool = static_cast<const uint8_t*>(pool); a.pool_rows = capacity;
+  a.rec = 2 * gu_rows * gu_cols + 2 * gu_rows + 2 * dn_rows * dn_cols + 2 * dn_rows;
+  a.off_gu_idx = 0; a.off_gu_scale = 2 * gu_rows * gu_cols; a.off_dn_idx = a.off_gu_scale + 2 * gu_rows;
+  a.off_dn_scale = a.off_dn_idx + 2 * dn_rows * dn_cols;
+  a.cb0 = cb0; a.perm_in = perm_in; a.sign_in = sign_in; a.scale_in = scale_in;
+  a.perm_mid = perm_mid; a.sign_mid = sign_mid; a.scale_mid = scale_mid;
+  a.gu = gu; a.out = out; a.out_dtype = out_dtype;
+  a.ids_in = ids; a.slots = slots; a.miss = miss; a.w_in = w; a.image = static_cast<const uint8_t*>(image);
+  a.rec_off = rec_off; a.num_experts = num_experts;
+  return val_dtype == VQ2_F16 ? launch_t1<__half>(a, st) : launch_t1<__nv_bfloat16>(a, st);
+}
+
 }  // namespace vq2
+
+extern "C" int vq2_paged_moe_t1(const void* h, int h_dtype, int64_t top_k, const int32_t* ids,
+                                const int32_t* slots, const int32_t* miss, const float* w, const void* pool,
+                                int64_t capacity, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                                int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in,
+                                const int8_t* sign_in, int64_t hb_in, float scale_in, const int32_t* perm_mid,
+                                const int8_t* sign_mid, int64_t hb_mid, float scale_mid, const void* image_dev,
+                                const int64_t* rec_off, int64_t num_experts, void* workspace, int64_t workspace_bytes,
+                                void* out, int out_dtype, void* stream) {
+  using namespace vq2;
+  if (!h || !ids || !slots || !miss || !w || !pool || !cb0 || !perm_in || !sign_in || !perm_mid || !sign_mid ||
+      !image_dev || !rec_off || !workspace || !out)
+    return VQ2_ERR_ARG;
+  if (h_dtype != VQ2_F32 && h_dtype != VQ2_F16 && h_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (out_dtype != VQ2_F32 && out_dtype != VQ2_F16 && out_dtype != VQ2_BF16) return VQ2_ERR_DTYPE;
+  if (capacity <= 0 || num_experts <= 0) return VQ2_ERR_SHAPE;
+  if (workspace_bytes < vq2_paged_moe_t1_workspace(top_k)) return VQ2_ERR_ARG;
+  return run_moe_t1_paged(h, h_dtype, top_k, ids, slots, miss, w, pool, capacity, gu_rows, gu_cols, dn_rows,
+                          dn_cols, cb0, val_dtype, perm_in, sign_in, hb_in, scale_in, perm_mid, sign_mid, hb_mid,
+                          scale_mid, image_dev, rec_off, num_experts, static_cast<float*>(workspace), out, out_dtype,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t vq2_paged_moe_t1_workspace(int64_t top_k) {
+  if (top_k <= 0 || top_k > vq2::kT1MaxK) return -1;
+  return top_k * vq2::kT1GuRows * 4;
+}

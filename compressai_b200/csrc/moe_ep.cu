@@ -3,7 +3,7 @@
 // combine -> NCCL all_reduce(SUM) -> cast.
 //
 // Every rank holds an identical symmetric buffer (peer-mapped; the device array `peers` has each
-// rank's base address): [flags: world x 128 uint32][slots: 2 parities x world ranks x T_max x H
+// rank's base address): [flags: world x kPeerFlagStride uint32][slots: 2 parities x world ranks x T_max x H
 // fp32]. The [T, H] output is split into contiguous float4 ranges, one per CTA:
 //   1. CTA b computes its range of this rank's partial (sum_j w[t, j] * y[t*k + j] over local
 //      problems) and stores it into slot [parity][rank] of EVERY rank's buffer (posted NVLink
@@ -23,20 +23,6 @@
 #include "gemv.cuh"
 
 namespace vq2 {
-
-constexpr int kPeerWaitPolls = 1 << 22;  // ~1 s at 64 ns naps
-constexpr int kPeerTimeout = 0x200;
-constexpr int kPeerTightPolls = 2048;    // polls before napping between them
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __restrict__ y, const float* __restrict__ w,
                                                                const int32_t* __restrict__ ids, int64_t num_experts,
@@ -87,23 +73,7 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
   }
   __syncthreads();
   // 2. publish, then wait for every peer's range b of this call
-  if (tid == 0) {
-    fence_acq_rel_sys();
-    for (int q = 0; q < world; ++q)
-      if (q != rank) st_release_sys(reinterpret_cast<uint32_t*>(peers[q]) + rank * kPeerMaxBlocks + b, e);
-    const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers[rank]);
-    bool ok = true;
-    for (int q = 0; q < world; ++q) {
-      if (q == rank) continue;
-      int it = 0;
-      while ((int)(ld_acquire_sys(flags + q * kPeerMaxBlocks + b) - e) < 0 && it < max_polls) {
-        if (it >= kPeerTightPolls) __nanosleep(64);
-        ++it;
-      }
-      if (it == max_polls) ok = false;
-    }
-    if (!ok && err) atomicMax(err, kPeerTimeout);
-  }
+  if (tid == 0) peer_flags_exchange(peers, rank, world, b, e, max_polls, err);
   __syncthreads();
   // 3. sum of all ranks' ranges from local memory, in rank order
   const uint8_t* base = peers[rank] + part_off + par * world * slot_bytes;
@@ -141,7 +111,7 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
   }
 }
 
-int64_t peer_flag_bytes(int world) { return ((int64_t)world * kPeerMaxBlocks * 4 + 4095) / 4096 * 4096; }
+int64_t peer_flag_bytes(int world) { return ((int64_t)world * kPeerFlagStride * 4 + 4095) / 4096 * 4096; }
 int64_t peer_slot_bytes(int64_t max_tokens, int64_t H) { return (max_tokens * H * 4 + 255) / 256 * 256; }
 
 int run_combine_peer(const float* y, const float* w, int64_t T, int top_k, int64_t H, const int32_t* ids,

@@ -643,8 +643,10 @@ class PagedMoEExpert(nn.Module):
 class DeviceResidentPagedMoE:
     """Device-resident paged MoE decode (T = 1) over a pinned ``.vq2m`` image: per layer step,
     ``vq2_lru_step`` (the reference ``_get_slot`` LRU, vq2/paged_runtime.py:415-437, as a GPU
-    kernel), ``vq2_fetch_records`` (missed records read by the SMs from the pinned image,
-    zero-copy) and the routed-expert FFN on the slots -- no host synchronisation, so the steps of
+    kernel), then the routed-expert FFN on the slots with the missed records read by its kernels
+    from the pinned image (zero-copy) and written into their slots on the way
+    (``vq2_paged_moe_t1``; ``vq2_fetch_records`` + ``vq2_moe_expert_ffn`` for other shapes or with
+    VQ2_PAGED_FUSED=0) -- no host synchronisation, so the steps of
     all layers (with the router) can be captured in one CUDA graph. This removes the per-layer
     ``.tolist()`` read-back of reference ``PagedMoEExpert.forward`` (:443). Hit/miss/slot
     sequences are bit-exact with the reference LRU; capacity must be at least top_k."""
@@ -674,10 +676,17 @@ class DeviceResidentPagedMoE:
                                     device=self.device)
         self.slots = torch.empty(L, top_k, dtype=torch.int32, device=self.device)
         self.miss = torch.zeros(L, 1 + 2 * top_k, dtype=torch.int32, device=self.device)
-        self.ws_bytes = lib.vq2_moe_expert_ffn_workspace(1, top_k, store.gu_rows, store.dn_rows)
-        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.device)
         self.rot_in = vq.get_rot("moe_expert_2048", store.gu_cols * 8, self.device)
         self.rot_mid = vq.get_rot("moe_expert_512", store.gu_rows // 2, self.device)
+        # the fetch fused into the FFN (vq2_paged_moe_t1) where the shapes are its specialisation;
+        # VQ2_PAGED_FUSED=0 keeps the separate fetch + FFN (the same outputs)
+        self.fused = (os.environ.get("VQ2_PAGED_FUSED", "1") != "0" and lib.vq2_paged_moe_t1_workspace(top_k) > 0
+                      and store.gu_cols * 8 == 2048 and store.gu_rows == 1024 and store.dn_rows == 2048
+                      and store.dn_cols * 8 == 512 and self.rot_in.hb == 2048 and self.rot_mid.hb == 512
+                      and cb16.dtype in (torch.float16, torch.bfloat16))
+        self.ws_bytes = max(lib.vq2_moe_expert_ffn_workspace(1, top_k, store.gu_rows, store.dn_rows),
+                            lib.vq2_paged_moe_t1_workspace(top_k) if self.fused else 0)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.device)
 
     @staticmethod
     def initial_lru_state(num_experts, capacity):
@@ -707,10 +716,20 @@ class DeviceResidentPagedMoE:
         pool = self.pools[ln]
         _lib.check(lib.vq2_lru_step(_lib.ptr(self.state[ln]), _lib.ptr(ids), K, _lib.ptr(self.slots[ln]),
                                     _lib.ptr(self.miss[ln]), st), "vq2_lru_step")
+        ri, rm = self.rot_in, self.rot_mid
+        w = weights.reshape(-1).float().contiguous()
+        if self.fused:  # missed records read from the image by the FFN kernels, written into their slots
+            _lib.call("vq2_paged_moe_t1", _lib.ptr(h), _lib.dtype_code(h), K, _lib.ptr(ids), _lib.ptr(self.slots[ln]),
+                      _lib.ptr(self.miss[ln]), _lib.ptr(w), _lib.ptr(pool.raw), self.capacity, self.store.gu_rows,
+                      self.store.gu_cols, self.store.dn_rows, self.store.dn_cols, _lib.ptr(self.cb16),
+                      _lib.dtype_code(self.cb16), _lib.ptr(ri.perm), _lib.ptr(ri.sign), ri.hb, float(ri.scale),
+                      _lib.ptr(rm.perm), _lib.ptr(rm.sign), rm.hb, float(rm.scale), self.image_dev,
+                      _lib.ptr(self.rec_off[ln]), self.num_experts, _lib.ptr(self.ws), self.ws_bytes, _lib.ptr(out),
+                      _lib.dtype_code(out), st)
+            return out
         _lib.check(lib.vq2_fetch_records(self.image_dev, _lib.ptr(self.rec_off[ln]), pool.record_bytes,
                                          _lib.ptr(pool.raw), self.capacity, _lib.ptr(self.miss[ln]), K,
                                          self.num_experts, st), "vq2_fetch_records")
-        ri, rm = self.rot_in, self.rot_mid
         _lib.call("vq2_moe_expert_ffn", _lib.ptr(h), _lib.dtype_code(h), 1, K, _lib.ptr(self.slots[ln]),
                   _lib.ptr(weights), _lib.ptr(pool.raw), self.capacity, self.store.gu_rows, self.store.gu_cols,
                   self.store.dn_rows, self.store.dn_cols, _lib.ptr(self.cb16), _lib.dtype_code(self.cb16),

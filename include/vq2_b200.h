@@ -575,6 +575,27 @@ VQ2_API int vq2_fetch_records(const void* image_dev, const int64_t* rec_off, int
                               int64_t num_experts, void* stream);
 /* Device address of page-locked host memory (VQ2_ERR_ARG if it is not mapped). */
 VQ2_API int vq2_host_device_pointer(const void* host, void** device_ptr);
+/*
+ * The routed-expert FFN of one token on the slots of a vq2_lru_step, with the fetch of the missed
+ * records fused in: two launches (gate_up rows; down rows over all problems + the combine) that
+ * read a record on this step's miss list straight from the page-locked image (image_dev +
+ * rec_off[ids[k]]) and write it into its slot on the way, so the PCIe reads overlap the hits'
+ * codebook gathers and no separate copy pass runs. Replaces vq2_fetch_records + the expert FFN
+ * (the copy + compute of reference PagedMoEExpert.forward, vq2/paged_runtime.py:439-511, the
+ * LRU decision staying in vq2_lru_step). ids, slots, miss, w: device arrays of the step (top_k
+ * entries; miss as written by vq2_lru_step). Shapes: hidden 2048, expert intermediate 512
+ * (RHT blocks 2048 / 512), top_k <= 8, 2 bpw records; others return VQ2_ERR_SHAPE. workspace:
+ * vq2_paged_moe_t1_workspace(top_k) bytes. Outputs are bit-identical to the separate fetch + FFN.
+ */
+VQ2_API int64_t vq2_paged_moe_t1_workspace(int64_t top_k);
+VQ2_API int vq2_paged_moe_t1(const void* h, int h_dtype, int64_t top_k, const int32_t* ids,
+                             const int32_t* slots, const int32_t* miss, const float* w, const void* pool,
+                             int64_t capacity, int64_t gu_rows, int64_t gu_cols, int64_t dn_rows,
+                             int64_t dn_cols, const void* cb0, int val_dtype, const int32_t* perm_in,
+                             const int8_t* sign_in, int64_t hb_in, float scale_in, const int32_t* perm_mid,
+                             const int8_t* sign_mid, int64_t hb_mid, float scale_mid, const void* image_dev,
+                             const int64_t* rec_off, int64_t num_experts, void* workspace,
+                             int64_t workspace_bytes, void* out, int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -92,6 +92,15 @@ def test_device_paging_outputs_equal_host_paging(tmp_path):
             assert torch.equal(h_d, h_h), (step, ln)
             hits, misses, e2s, _, _ = dr.lru_view(ln)
             assert (hits, misses, e2s) == (host[ln].hits, host[ln].misses, host[ln].expert_to_slot)
+    # the fused path wrote every missed record into its slot while computing with it: each
+    # resident expert's slot holds exactly its record of the image
+    assert dr.fused
+    for ln in range(layers):
+        _, _, e2s, _, _ = dr.lru_view(ln)
+        for e, slot in e2s.items():
+            off = int(dr.rec_off[ln, e])
+            rec = store.image[off:off + dr.pools[ln].record_bytes].to(DEV)
+            assert torch.equal(dr.pools[ln].raw[slot], rec), (ln, e, slot)
     store.close()
 
 

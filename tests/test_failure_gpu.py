@@ -1,4 +1,4 @@
-"""Failure detection without a GPU fault: the expert-parallel combine's bounded wait for a peer.
+"""Failure detection without a GPU fault: the expert-parallel rank sum's bounded wait for a peer.
 
 One GPU, one process: the layer is called as rank 0 of a world of 2 whose "peer" buffer is a
 second local buffer that no other rank ever writes, so the wait for rank 1's flags cannot be
@@ -29,8 +29,11 @@ class _LoneRankPeers:
         self.err = torch.zeros(1, dtype=torch.int32, device=DEV)
 
 
-def test_peer_wait_gives_up_and_reports_timeout():
-    E, T = 16, 2
+@pytest.mark.parametrize("T", [1, 2])
+def test_peer_wait_gives_up_and_reports_timeout(T):
+    """T = 1 exercises the exchange fused into the one-token down kernel, T = 2 the peer combine
+    kernel; both use the same flags and sequence number."""
+    E = 16
     pool = moe.ExpertRecordPool(E // 2 + 1, DEV)
     for e in range(E // 2 + 1):
         pool.set_expert(e, *[torch.from_numpy(a) for a in synth.synth_expert(41, e)])
