@@ -7,9 +7,11 @@ behind the launch lists and captures summarised in profiles/. Not part of the pa
       `reps` launches of one VQ GEMV (input RHT fused in the prologue) on a seeded matrix;
       with --swiglu the input is an fp32 [gate | up] row of 2n and SwiGLU + RHT run in the
       prologue (the MLP down projection); with --argmax the fused greedy argmax (keys only)
-  python bench_diag.py moe --T 1 --reps 3 [--graph --layers 40] [--shared]
+  python bench_diag.py moe --T 1 --reps 3 [--graph --layers 40] [--shared] [--world 8 --rank 0]
       `reps` MoE layers (router + expert FFN) over 256 resident seeded experts; with --graph,
-      `reps` replays of a CUDA graph of `layers` chained layers (each its own router logits)
+      `reps` replays of a CUDA graph of `layers` chained layers (each its own router logits); with
+      --world N, rank `rank`'s share of an expert-parallel layer (its E/N experts + the shared
+      expert, the rank-sum exchange into local buffers whose peer waits give up after one poll)
   python bench_diag.py rans --n 16777216 --reps 2
       `reps` GPU decodes of one VQ2A stream of n skewed index bytes, then `reps` decodes of one
       ANS-coded expert record (vq2_rans_decode_segments)
@@ -92,9 +94,59 @@ def cmd_gemv(a):
     print(json.dumps({"gemv": [a.out, a.n, a.M, a.bpw], "us": round(t * 1e6, 2), "GBs": round(nbytes / t / 1e9, 1)}))
 
 
+class _LoneRankPeers:
+    """The fields moe.moe_layer reads from ep.PeerReduceContext, backed by local buffers that no
+    other rank writes: one GPU runs rank `rank`'s share of an expert-parallel layer, and every
+    wait for a peer gives up after `max_polls` polls (the partial of this rank is what remains)."""
+
+    def __init__(self, dev, world, rank, max_tokens, hidden, max_polls=1):
+        from compressai_b200 import _lib
+        nbytes = _lib.load().vq2_moe_peer_buffer_bytes(max_tokens, hidden, world)
+        self.bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(world)]
+        self.ptrs = torch.tensor([b.data_ptr() for b in self.bufs], dtype=torch.int64, device=dev)
+        self.peers_dev = self.ptrs.data_ptr()
+        self.rank, self.world, self.max_tokens, self.max_polls = rank, world, max_tokens, max_polls
+        self.epochs = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+
 def cmd_moe(a):
     dev = torch.device("cuda", 0)
     cbs = _cbs(dev)
+    if a.world > 1:  # one rank of an expert-parallel layer: its expert slice + the shared expert
+        from compressai_b200 import vq
+        lo, hi = a.rank * a.E // a.world, (a.rank + 1) * a.E // a.world
+        pool = moe.ExpertRecordPool(hi - lo + 1, dev)
+        g = torch.Generator(device=dev).manual_seed(a.seed)
+        pool.raw.view(torch.int16).copy_(torch.randint(-32768, 32768, pool.raw.view(torch.int16).shape, generator=g,
+                                                       device=dev, dtype=torch.int16))
+        pool.gu_scale.fill_(0.02)
+        pool.dn_scale.fill_(0.02)
+        peer = _LoneRankPeers(dev, a.world, a.rank, a.T, 2048)
+        r_in, r_mid = vq.get_rot("moe_expert_2048", 2048, dev), vq.get_rot("moe_expert_512", 512, dev)
+        gate = 0.02 * torch.randn(2048, device=dev)
+        h = torch.randn(a.T, 2048, device=dev).half()
+        lg = [torch.randn(a.T, a.E, device=dev) for _ in range(a.layers)]
+
+        def step():
+            x = h
+            for li in range(a.layers):
+                x = moe.moe_layer(x, lg[li], pool, cbs["16"], r_in, r_mid, 8, shared_gate=gate, lo=lo, hi=hi,
+                                  rank=a.rank, world=a.world, peer=peer)
+            return x
+        step()
+        torch.cuda.synchronize()
+        if not a.graph:
+            t = _time(step, a.reps) / a.layers
+        else:
+            st = torch.cuda.Stream(dev)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                step()
+            t = _time(gr.replay, a.reps) / a.layers
+        print(json.dumps({"moe_T": a.T, "world": a.world, "rank": a.rank, "layers": a.layers,
+                          "us_per_layer": round(t * 1e6, 2), "peer_waits_gave_up": bool(peer.err.item())}))
+        return
     pool = moe.ExpertRecordPool(a.E, dev)
     g = torch.Generator(device=dev).manual_seed(a.seed)
     pool.raw.view(torch.int16).copy_(torch.randint(-32768, 32768, pool.raw.view(torch.int16).shape, generator=g,
@@ -294,6 +346,8 @@ def main(argv=None):
     m.add_argument("--graph", action="store_true")
     m.add_argument("--layers", type=int, default=40)
     m.add_argument("--shared", action="store_true", help="the last pool row as a shared expert (9 problems)")
+    m.add_argument("--world", type=int, default=1, help="> 1: one rank of an expert-parallel layer on this GPU")
+    m.add_argument("--rank", type=int, default=0)
     r = sub.add_parser("rans")
     r.add_argument("--n", type=int, default=1 << 24)
     r.add_argument("--reps", type=int, default=2)

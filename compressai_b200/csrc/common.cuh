@@ -142,6 +142,51 @@ int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, i
   return launch_status();
 }
 
+// ---- flags between GPUs over peer memory -----------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// The flag handshake of one CTA with every other rank, by ALL 32 lanes of one warp, after a CTA
+// barrier that follows the CTA's stores into the peers' buffers. Each flag array lives at the
+// base of a rank's buffer; this CTA's flag for sender s is word s * stride + b. Lane q (one per
+// peer, in rounds of 32): a system-scope fence (it covers the CTA's earlier peer stores, ordered
+// before it by the barrier), sequence number e into flag [rank][b] of peer q (release store), then
+// a bounded wait (max_polls acquire loads, napping after the first tight_polls) until flag [q][b]
+// of the local buffer has reached e. The peers are served in parallel, one per lane: serially,
+// every release and every acquire is a system-scope round trip. Returns false on every lane when
+// any wait gave up, after lane 0 raised *err to `timeout_code`; nothing traps. The caller's CTA
+// barrier afterwards orders the acquires before the other threads' reads of the peers' data.
+__device__ inline bool peer_flags_handshake(uint8_t* const* peers, int rank, int world, int stride, int b,
+                                            uint32_t e, int max_polls, int tight_polls, int32_t* err,
+                                            int timeout_code) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers[rank]);
+  bool ok = true;
+  for (int q0 = 0; q0 < world; q0 += 32) {
+    const int q = q0 + lane;
+    if (q < world && q != rank) {
+      fence_acq_rel_sys();
+      st_release_sys(reinterpret_cast<uint32_t*>(peers[q]) + rank * stride + b, e);
+      int it = 0;
+      while ((int)(ld_acquire_sys(flags + q * stride + b) - e) < 0 && it < max_polls) {
+        if (it >= tight_polls) __nanosleep(64);
+        ++it;
+      }
+      if (it == max_polls) ok = false;
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && lane == 0 && err) atomicMax(err, timeout_code);
+  return ok;
+}
+
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 

@@ -144,40 +144,6 @@ constexpr int kPeerWaitPolls = 1 << 22;  // default poll limit of a peer wait, ~
 constexpr int kPeerTimeout = 0x200;      // status word of a wait that gave up
 constexpr int kPeerTightPolls = 2048;    // polls before napping between them
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-// One thread of CTA b, after a CTA barrier that follows the CTA's peer stores: a system-scope
-// fence, sequence number e into flag [rank][b] of every peer's buffer (release stores), then a
-// bounded wait (max_polls polls per peer, napping after the first kPeerTightPolls) until flag
-// [q][b] of the local buffer has reached e for every peer q. A wait that gives up raises *err
-// (kPeerTimeout) and returns false; nothing traps.
-__device__ inline bool peer_flags_exchange(uint8_t* const* peers, int rank, int world, int b, uint32_t e,
-                                           int max_polls, int32_t* err) {
-  fence_acq_rel_sys();
-  for (int q = 0; q < world; ++q)
-    if (q != rank) st_release_sys(reinterpret_cast<uint32_t*>(peers[q]) + rank * kPeerFlagStride + b, e);
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers[rank]);
-  bool ok = true;
-  for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;
-    int it = 0;
-    while ((int)(ld_acquire_sys(flags + q * kPeerFlagStride + b) - e) < 0 && it < max_polls) {
-      if (it >= kPeerTightPolls) __nanosleep(64);
-      ++it;
-    }
-    if (it == max_polls) ok = false;
-  }
-  if (!ok && err) atomicMax(err, kPeerTimeout);
-  return ok;
-}
 struct PeerReduce {
   uint8_t* const* peers;  // device array [world] of the symmetric buffers' base addresses
   int rank, world;

@@ -405,12 +405,28 @@ __global__ void __launch_bounds__(1024) moe_route_token_kernel(const RouteArgs r
     *r.c_cnt = base;
     *r.arrive = 0;
   }
+  // per-token counts in parallel, then their exclusive prefix (the transform scratch is free now;
+  // T <= kRouteMaxH fits it)
+  int* cnt = reinterpret_cast<int*>(sc);
   for (int tt = tid; tt < r.T; tt += 1024) {
-    int before = 0, mine = 0;
-    for (int p = 0; p < tt * r.ks; ++p) before += __ldcg(r.ids + p) >= 0 ? 1 : 0;
+    int mine = 0;
     for (int k = 0; k < r.ks; ++k) mine += __ldcg(r.ids + tt * r.ks + k) >= 0 ? 1 : 0;
-    r.tstart[tt] = before;
-    r.tcnt[tt] = mine;
+    cnt[tt] = mine;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int tt = 0; tt < r.T; ++tt) {
+      const int c = cnt[tt];
+      cnt[tt] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int tt = tid; tt < r.T; tt += 1024) {
+    const int start = cnt[tt];
+    r.tstart[tt] = start;
+    r.tcnt[tt] = (tt + 1 < r.T ? cnt[tt + 1] : base) - start;
   }
 }
 

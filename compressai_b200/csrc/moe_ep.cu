@@ -8,9 +8,9 @@
 //   1. CTA b computes its range of this rank's partial (sum_j w[t, j] * y[t*k + j] over local
 //      problems) and stores it into slot [parity][rank] of EVERY rank's buffer (posted NVLink
 //      writes; no remote reads anywhere);
-//   2. one thread fences at system scope and publishes the call's sequence number into flag
-//      [rank][b] of every peer (release stores), then waits (bounded; acquire loads of its own
-//      flags) until every peer's flag [q][b] has it;
+//   2. the lanes of warp 0, one per peer, fence at system scope, publish the call's sequence
+//      number into flag [rank][b] of their peer (release stores) and wait (bounded; acquire loads
+//      of the local flags) until that peer's flag [q][b] has it;
 //   3. the CTA adds slots [parity][0..world) of its range from LOCAL memory in rank order (the
 //      same values in the same order on every rank) and writes the output in its dtype.
 // The sequence number lives in local device memory (state[0]); the last CTA to finish advances
@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(const float* __re
   }
   __syncthreads();
   // 2. publish, then wait for every peer's range b of this call
-  if (tid == 0) peer_flags_exchange(peers, rank, world, b, e, max_polls, err);
+  if (tid < 32) peer_flags_handshake(peers, rank, world, kPeerFlagStride, b, e, max_polls, kPeerTightPolls, err,
+                                     kPeerTimeout);
   __syncthreads();
   // 3. sum of all ranks' ranges from local memory, in rank order
   const uint8_t* base = peers[rank] + part_off + par * world * slot_bytes;

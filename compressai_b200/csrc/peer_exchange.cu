@@ -21,15 +21,6 @@ namespace vq2 {
 constexpr int kXchgTimeout = 0x400;
 constexpr int kXchgDefaultPolls = 1 << 22;
 
-__device__ __forceinline__ void xchg_st_release(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t xchg_ld_acquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(256) peer_exchange_kernel(const void* __restrict__ src, int64_t bytes, int mode,
                                                             int64_t row_offset, uint8_t* const* __restrict__ peers,
                                                             int rank, int world, int64_t slot_bytes,
@@ -66,24 +57,8 @@ __global__ void __launch_bounds__(256) peer_exchange_kernel(const void* __restri
     }
   }
   __syncthreads();
-  // 2. publish and wait
-  if (tid == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (int q = 0; q < world; ++q)
-      if (q != rank) xchg_st_release(reinterpret_cast<uint32_t*>(peers[q]) + rank, e);
-    const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers[rank]);
-    bool ok = true;
-    for (int q = 0; q < world; ++q) {
-      if (q == rank) continue;
-      int it = 0;
-      while ((int)(xchg_ld_acquire(flags + q) - e) < 0 && it < max_polls) {
-        if (it >= 2048) __nanosleep(64);
-        ++it;
-      }
-      if (it == max_polls) ok = false;
-    }
-    if (!ok && err) atomicMax(err, kXchgTimeout);
-  }
+  // 2. publish and wait (one peer per lane of warp 0)
+  if (tid < 32) peer_flags_handshake(peers, rank, world, 1, 0, e, max_polls, 2048, err, kXchgTimeout);
   __syncthreads();
   // 3. read all slots from local memory in rank order
   const uint8_t* base = peers[rank] + slots + par * world * slot_bytes;

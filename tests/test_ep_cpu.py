@@ -117,7 +117,10 @@ def _leaving_worker(rank, world, port, results):
     import time
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    # the group timeout also bounds rendezvous and step 0, which a loaded host can stretch (spawned
+    # ranks import torch and run the fp64 stand-in); the leaving rank's closed connection is
+    # reported to its peers at once, well inside it
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
     cbs = _cbs()
     r2048, r512 = O.rot_params("moe_expert_2048", 2048), O.rot_params("moe_expert_512", 512)
     lo, hi = ep.partition(E, world, rank)
@@ -148,4 +151,4 @@ def test_rank_leaving_between_steps_is_detected_by_the_others():
     for r in range(world - 1):
         res = results[r]
         assert isinstance(res, tuple), (r, res)
-        assert res[1] < 30, (r, res)   # ended by the error, not by hanging
+        assert res[1] < 40, (r, res)   # ended by the error, not by hanging
