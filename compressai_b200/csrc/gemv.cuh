@@ -64,6 +64,16 @@ struct GemvArgs {
   int row_blocks;         // row blocks per (problem, M tile) (expert mode) / total (multi mode)
 };
 
+// Order-preserving 64-bit key of a router logit: larger value first, equal values to the smaller
+// expert id (the router's rank rule o > l || (o == l && j < i)), -0 as +0 (as float comparison);
+// 0 is below every key.
+__device__ __forceinline__ unsigned long long route_key(float v, int i) {
+  uint32_t u = __float_as_uint(v);
+  if (u == 0x80000000u) u = 0u;
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+}
+
 // Launch the GEMV described by `a` (expert-indexed when a.nprob == 0, multi-matrix otherwise);
 // total_rows = rows of all problems (sizes the work split); res = 3 bpw.
 int run_gemv(GemvArgs a, int64_t total_rows, bool res, int val_dtype, cudaStream_t st, void* ws = nullptr,

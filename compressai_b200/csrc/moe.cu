@@ -269,8 +269,33 @@ __global__ void __launch_bounds__(1024) moe_route_token_kernel(const RouteArgs r
   if (lane == 0) red[warp] = d;
   for (int64_t z = tid; r.zero && z < r.zero_n / r.T; z += 1024) r.zero[(int64_t)t * (r.zero_n / r.T) + z] = 0;
   __syncthreads();
-  // ---- rank of each logit: PARTS threads count interleaved slices of the others
-  {
+  // ---- rank of each logit
+  if (TPT <= 256 && r.K <= 8) {
+    // top-k by route_key (the rank rule below): each of the first 8 warps ranks its 32 keys by
+    // shuffles and keeps its top k; one pass ranks the 8 x k candidates
+    __shared__ unsigned long long cand[64];
+    if (tid < 256) {
+      const float v = tid < r.E ? sl[tid] : 0.f;
+      const unsigned long long key = tid < r.E ? route_key(v, tid) : 0ull;
+      if (lane < r.K) cand[warp * r.K + lane] = 0ull;
+      int cnt = 0;
+#pragma unroll
+      for (int m = 0; m < 32; ++m) cnt += __shfl_sync(0xffffffffu, key, m) > key ? 1 : 0;
+      __syncwarp();
+      if (cnt < r.K) cand[warp * r.K + cnt] = key;  // lanes past E share one zero key's slot
+    }
+    __syncthreads();
+    if (tid < 8 * r.K) {
+      const unsigned long long k = cand[tid];
+      int rank = 0;
+      for (int d = 0; d < 8 * r.K; ++d) rank += cand[d] > k ? 1 : 0;
+      if (rank < r.K && k != 0ull) {
+        const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffull));
+        sel_e[rank] = e;
+        sel_v[rank] = sl[e];
+      }
+    }
+  } else {  // PARTS threads count interleaved slices of the others
     const float li = i < r.E ? sl[i] : -FLT_MAX;
     int rank = 0;
 #pragma unroll 8

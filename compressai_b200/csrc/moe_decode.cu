@@ -90,22 +90,13 @@ struct T1Route {
   int P;
 };
 
-// Order-preserving key: larger logit first, equal logits to the smaller expert id (the rank rule
-// of the router kernel: o > l || (o == l && j < i)); -0 ranks as +0, as float comparison does.
-__device__ __forceinline__ unsigned long long t1_key(float v, int i) {
-  uint32_t u = __float_as_uint(v);
-  if (u == 0x80000000u) u = 0u;
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
-}
-
 // Top-k, local pool rows and the compacted problem list of the token (router kernel semantics:
 // ids in rank order; routed expert e -> pool row e - lo when lo <= e < hi; the shared expert's
 // problem on rank 0 of the group, as the token index is 0). All 256 threads; ends with a barrier.
 __device__ __forceinline__ void t1_route(const MoeT1Args& a, T1Route& s) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float v = tid < a.E ? __ldcg(a.logits + tid) : 0.f;
-  const unsigned long long key = tid < a.E ? t1_key(v, tid) : 0ull;
+  const unsigned long long key = tid < a.E ? route_key(v, tid) : 0ull;
   if (tid < a.E) s.lg[tid] = v;
   if (lane < a.K) s.cand[warp * a.K + lane] = 0ull;
   int cnt = 0;
